@@ -1,0 +1,100 @@
+"""The CPU oracle against the golden fixtures made by the reference's own oracle code
+(tests/golden/make_golden.py runs colabfold-legacy-kernels' reference_grads and packed
+reference). This pins the oracle before it is trusted as the checker of the CUDA path."""
+import numpy as np
+import pytest
+
+from conftest import golden
+from oracle import attention as oa
+from oracle import fused as of
+from oracle.numerics import rel_max, round_bf16, round_to
+
+ATTN = golden('attn_*.npz')
+PACKED = golden('packed_*.npz')
+
+
+def test_fixtures_present():
+    assert len(ATTN) >= 8 and len(PACKED) >= 4
+
+
+@pytest.mark.parametrize('name,z', ATTN, ids=[n for n, _ in ATTN])
+def test_attention_grads_match_reference_oracle(name, z):
+    got = oa.attention_grads(z['q'], z['k'], z['v'], z['bias'], z['kmask'], z['dout'],
+                             float(z['scale']))
+    for key, g in zip(('out', 'lse2', 'dq', 'dk', 'dv', 'dbias'), got):
+        want = z[key].astype(np.float64)
+        err = np.abs(g - want).max() if want.size else 0.0
+        # the fixtures hold float32 copies of float64 results
+        assert err <= 1e-6 * max(1.0, np.abs(want).max()), (name, key, err)
+
+
+@pytest.mark.parametrize('name,z', ATTN, ids=[n for n, _ in ATTN])
+def test_float32_port_close_to_truth(name, z):
+    got = oa.attention_grads_f32(z['q'], z['k'], z['v'], z['bias'], z['kmask'], z['dout'],
+                                 float(z['scale']))
+    for key, g in zip(('out', 'lse2', 'dq', 'dk', 'dv', 'dbias'), got):
+        assert rel_max(g, z[key]) < 1e-3, (name, key)
+
+
+@pytest.mark.parametrize('name,z', PACKED, ids=[n for n, _ in PACKED])
+def test_packed_forward_matches_reference(name, z):
+    """Rows with a live key match the reference's float32 packed oracle; the reference masks
+    with -1e9 where the kernel uses -1e4, which only matters for rows with no live key."""
+    column = bool(z['column'])
+    X, Y, G, H, D = z['p'].shape
+    out = oa.packed_forward(z['p'], z['bias'], z['kmask'], z['gate_bias'], D ** -0.5, column)
+    rows = z['kmask'].any(axis=1)
+    to_bs = (lambda o: np.transpose(o, (1, 0, 2, 3))) if column else (lambda o: o)
+    # the reference returns [batch, sequence, H, D]; the kernel layout is [X, Y, H, D]
+    o, r = to_bs(out), z['out'].astype(np.float64)
+    assert np.abs(o[rows] - r[rows]).max() < 1e-5
+    lims = oa.trim_limits(z['kmask'])
+    np.testing.assert_array_equal(lims, z['lims'])
+    t = to_bs(oa.packed_forward(z['p'], z['bias'], z['kmask'], z['gate_bias'], D ** -0.5,
+                                column, lims))
+    assert np.abs(t[~rows]).max(initial=0) == 0
+    np.testing.assert_array_equal(t[rows], o[rows])
+
+
+def test_dead_row_is_uniform_average():
+    """A batch row with every key masked averages its keys (masked logit -1e4, not -inf)."""
+    rng = np.random.default_rng(1)
+    q, k, v = (rng.standard_normal((2, 1, 5, 8)) for _ in range(3))
+    bias = rng.standard_normal((1, 5, 7))[:, :, :5]
+    km = np.ones((2, 5), np.uint8)
+    km[1] = 0
+    out, lse = oa.attention_forward(q, k, v, bias, km, 0.3)
+    np.testing.assert_allclose(out[1, 0], np.broadcast_to(v[1, 0].mean(0), (5, 8)), atol=1e-12)
+    np.testing.assert_allclose(lse[1], (-1e4 + np.log(5)) * oa.LOG2E, rtol=1e-12)
+
+
+def test_bf16_rounding():
+    x = np.array([1.0, 1.00390625, 1.01171875, -3.14159, 65504.0, 1e-30], np.float32)
+    r = round_bf16(x)
+    import torch
+    want = torch.tensor(x).to(torch.bfloat16).float().numpy()
+    np.testing.assert_array_equal(r, want)
+    np.testing.assert_array_equal(round_to(x, 'f16'), x.astype(np.float16).astype(np.float64))
+
+
+def test_layer_norm_two_pass():
+    rng = np.random.default_rng(2)
+    x = rng.standard_normal((7, 64)) * 5 + 1e3
+    y = of.layer_norm(x, np.ones(64), np.zeros(64), 1e-5)
+    np.testing.assert_allclose(y.mean(-1), 0, atol=1e-3)
+    np.testing.assert_allclose(y.std(-1), 1, atol=1e-3)
+
+
+def test_tile_work():
+    keep = np.array([1, 0, -1, -1, 0, 0, -1, -1, -1, -1], np.float32)
+    assert of.tile_work(keep, 10, 2, -1.0) == ['compute', 'skip', 'padding', 'skip', 'skip']
+    assert of.tile_work(keep, 10, 4, 0.0) == ['compute', 'padding', 'padding']
+    assert of.tile_work(None, 10, 4, 0.0) == ['compute'] * 3
+
+
+def test_transition_chunking_round_trip():
+    w2 = np.arange(128 * 64, dtype=np.float64).reshape(128, 64)
+    c = of.chunk_w2(w2)
+    assert c.shape == (2, 64, 64)
+    assert c[1, 5, 7] == w2[64 + 7, 5]
+    np.testing.assert_array_equal(of.unchunk_w2(c), w2)

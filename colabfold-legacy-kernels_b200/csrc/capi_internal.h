@@ -1,0 +1,24 @@
+// Status codes, dtype codes and the last-error message shared by the C-ABI entry points.
+#pragma once
+
+#include <string>
+
+namespace cflk {
+
+// return codes of every entry point (the XLA FFI handler maps them to ffi::Error kinds)
+enum Status : int { kOk = 0, kInvalidArgument = 1, kInternal = 2 };
+// element type of the 16-bit buffers
+enum DType : int { kF16 = 0, kBF16 = 1 };
+
+constexpr int kMaxDevices = 64;
+
+// record msg as this thread's last error and return code
+int fail(int code, const std::string& msg);
+void clear_error();
+
+// each translation unit's device status word (bounded waits that gave up), read and cleared
+unsigned read_and_clear_status_fwd();
+unsigned read_and_clear_status_bwd();
+unsigned read_and_clear_status_fused();
+
+}  // namespace cflk

@@ -1,0 +1,148 @@
+/* C ABI of the B200 (sm_100a) library that takes over colabfold-legacy-kernels' hot path for
+ * compute capability 100: libcflk_sm100.so.
+ *
+ * Every entry point takes plain device pointers, sizes and attributes, launches asynchronously
+ * on the given CUDA stream (a cudaStream_t, NULL for the legacy default stream) on the current
+ * device, does no host synchronisation and allocates nothing. Each one replaces one XLA FFI
+ * target of the reference (named below with its file:line); an XLA FFI handler, where the XLA
+ * headers exist, is a thin shim over these functions.
+ *
+ * 16-bit buffers hold `dtype` elements: CFLK_F16 (the reference's F16, bit-compatible) or
+ * CFLK_BF16 (an extension). float buffers are float32. Pointers to 16-bit data must be 16-byte
+ * aligned. Returns CFLK_OK, CFLK_INVALID_ARGUMENT (nothing launched; message from
+ * cflk_last_error) or CFLK_INTERNAL (a launch failed).
+ */
+#ifndef CFLK_B200_H
+#define CFLK_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define CFLK_API __attribute__((visibility("default")))
+#else
+#define CFLK_API
+#endif
+
+#define CFLK_OK 0
+#define CFLK_INVALID_ARGUMENT 1
+#define CFLK_INTERNAL 2
+
+#define CFLK_F16 0
+#define CFLK_BF16 1
+
+/* Message of this thread's last failed call ("" after a successful one). */
+CFLK_API const char* cflk_last_error(void);
+
+/* 100: the compute capability the library is built for. */
+CFLK_API int cflk_version(void);
+
+/* OR of the bit codes that kernels record when a bounded wait gave up (1: a TMA load,
+ * 2: an MMA, 4: a thread-group barrier), cleared by the read. Call after synchronising. */
+CFLK_API unsigned cflk_device_status(void);
+
+/* ---- attention ------------------------------------------------------------------------- */
+
+/* VoltaMma: out = softmax(scale * q k^T + bias[h]; kmask) v, and the log2-domain row statistic.
+ * q [N,H,Sq,D], k and v [N,H,Sk,D], bias [H,Sq,Sk] (16-bit); kmask [N,Sk] u8 (0 masks a key);
+ * out [N,H,Sq,D]; lse [N,H,Sq] float32, left untouched when want_lse is 0 (a one-element buffer
+ * is then enough, or NULL). D in {8,16,24,32,48,64,96}; (D, block_q, block_k) must be a tuple
+ * the reference accepts, taken as a hint only.
+ * Replaces VoltaMma, cuda/volta_mma_attn.cu:524-542,625-640. */
+CFLK_API int cflk_volta_mma(void* stream, int dtype, const void* q, const void* k, const void* v,
+                            const void* bias, const uint8_t* kmask, void* out, float* lse,
+                            int64_t N, int64_t H, int64_t Sq, int64_t Sk, int64_t D, float scale,
+                            int64_t block_q, int64_t block_k, int want_lse);
+
+/* VoltaMmaPacked / VoltaMmaPackedTrim: q, k, v (and the gate when G == 4) read in place from
+ * p [X,Y,G,H,D]; out [X,Y,H,D] = attention * sigmoid(gate + gate_bias[h,c]). Rows attend along
+ * Y (batch X); with column set, columns attend along X (batch Y). bias [H,S,S], kmask [N,S],
+ * gate_bias [H,D]; the *_elems arguments are those buffers' element counts, checked as the
+ * reference checks them. lims [N+1] int32 or NULL: with lims, batch row n's keys end at
+ * lims[n], and a row with lims[n] == 0 or a query tile past lims[N] is written as zeros.
+ * Replaces VoltaMmaPacked and VoltaMmaPackedTrim, cuda/volta_mma_attn.cu:544-623. */
+CFLK_API int cflk_volta_mma_packed(void* stream, int dtype, const void* p, const void* bias,
+                                   const uint8_t* kmask, const void* gate_bias,
+                                   const int32_t* lims, void* out, int64_t X, int64_t Y,
+                                   int64_t G, int64_t H, int64_t D, int64_t bias_elems,
+                                   int64_t kmask_elems, int64_t gate_bias_elems, float scale,
+                                   int64_t block_q, int64_t block_k, int column);
+
+/* Bytes of device workspace cflk_volta_mma_bwd needs for these sizes (the reference takes the
+ * same scratch, a float32 dQ accumulator and the row statistic, from XLA's ScratchAllocator,
+ * cuda/volta_mma_attn_bwd.cu:346-361). */
+CFLK_API int cflk_volta_mma_bwd_workspace_size(int64_t N, int64_t H, int64_t Sq, int64_t Sk,
+                                               int64_t D, size_t* bytes);
+
+/* VoltaMmaBwd: dq, dk, dv [as q, k, v] and dbias [H,Sq,Sk] float32 = dS summed over the batch
+ * (unscaled). out and lse are the forward's; dout [N,H,Sq,D]. dbias is always zero-filled and
+ * only accumulated when want_dbias is set. dk and dv are bitwise deterministic.
+ * workspace: at least cflk_volta_mma_bwd_workspace_size bytes, 256-byte aligned.
+ * Replaces VoltaMmaBwd, cuda/volta_mma_attn_bwd.cu:385-473. */
+CFLK_API int cflk_volta_mma_bwd(void* stream, int dtype, const void* q, const void* k,
+                                const void* v, const void* bias, const uint8_t* kmask,
+                                const void* out, const void* dout, const float* lse, void* dq,
+                                void* dk, void* dv, float* dbias, void* workspace,
+                                size_t workspace_bytes, int64_t N, int64_t H, int64_t Sq,
+                                int64_t Sk, int64_t D, float scale, int want_dbias);
+
+/* ---- LayerNorm-folded pair-stack fusions ------------------------------------------------ */
+/* keep [M] (16-bit) or NULL: per row tile, compute when a row of keep is above zero, write
+ * padding (zeros, or nothing where the output aliases its input) when the tile is all zero,
+ * nothing when it is all below zero (tile_work, cuda/volta_gdp.h:114-136). M == 0 launches
+ * nothing. */
+
+/* VoltaLnGdp: left, right [P/2, M] = the two halves of max(mask,0) * (y wp + bp) *
+ * sigmoid(y wg + bg), channel major, y = LayerNorm(x). x [M,K]; scale, offset [K] float32;
+ * wpT, wgT [P,K]; bp, bg [P]; mask [M] (also the keep, rows past M reading 0). K and P/2 in
+ * {64, 128}. Replaces VoltaLnGdp, cuda/volta_fused_ffi.h:42-80,337-351. */
+CFLK_API int cflk_volta_ln_gdp(void* stream, int dtype, const void* x, const float* scale,
+                               const float* offset, const void* wpT, const void* bp,
+                               const void* wgT, const void* bg, const void* mask, void* left,
+                               void* right, int64_t M, int64_t K, int64_t P, float eps);
+
+/* VoltaTrimulEpilogue: out [M,O] = (LN(x_cm^T) wo + bo) * sigmoid(LN_in(x) wg + bg), + x with
+ * add_input (then O == CA, and out may alias x). x_cm [C,M] float32; x [M,CA]; in_scale,
+ * in_offset [CA] and ln_scale, ln_offset [C] float32; woT [O,C], bo [O], wgT [O,CA], bg [O].
+ * C, CA, O in {64, 128}. Replaces VoltaTrimulEpilogue, cuda/volta_fused_ffi.h:82-133,353-371. */
+CFLK_API int cflk_volta_trimul_epilogue(void* stream, int dtype, const float* x_cm,
+                                        const void* x, const float* in_scale,
+                                        const float* in_offset, const float* ln_scale,
+                                        const float* ln_offset, const void* woT, const void* bo,
+                                        const void* wgT, const void* bg, const void* keep,
+                                        void* out, int64_t M, int64_t C, int64_t CA, int64_t O,
+                                        float eps, int add_input);
+
+/* VoltaLnProj: p [M,n] = LN(x) w and bias [heads,M] = (LN(x) wb)^T. x [M,K]; scale, offset [K]
+ * float32; wT [n,K]; wbT [heads,K]. K in {64, 128}, n a multiple of 64 (0: p untouched),
+ * heads <= 8 (0: bias untouched). Replaces VoltaLnProj, cuda/volta_fused_ffi.h:135-176,373-388. */
+CFLK_API int cflk_volta_ln_proj(void* stream, int dtype, const void* x, const float* scale,
+                                const float* offset, const void* wT, const void* wbT,
+                                const void* keep, void* p, void* bias, int64_t M, int64_t K,
+                                int64_t n, int64_t heads, float eps);
+
+/* VoltaOutProj: out [M,N] = o w + b, + residual when residual is not NULL (out may alias it).
+ * o [M,K]; wT [N,K]; b [N]. K, N in {64, 128}.
+ * Replaces VoltaOutProj, cuda/volta_fused_ffi.h:178-214,390-401. */
+CFLK_API int cflk_volta_out_proj(void* stream, int dtype, const void* o, const void* wT,
+                                 const void* b, const void* residual, const void* keep,
+                                 void* out, int64_t M, int64_t K, int64_t N);
+
+/* VoltaTransition: out [M,C] = relu(LN(x) w1 + b1) w2 + b2, + x with add_input (out may alias
+ * x). x [M,C]; scale, offset [C] float32; w1T [H,C]; b1 [H]; w2T = w2 [H,C] as [H/64][C][64]
+ * chunks, each transposed; b2 [C]. C in {64, 128, 256}, H in {2C, 4C}.
+ * Replaces VoltaTransition, cuda/volta_fused_ffi.h:216-259,403-418. */
+CFLK_API int cflk_volta_transition(void* stream, int dtype, const void* x, const float* scale,
+                                   const float* offset, const void* w1T, const void* b1,
+                                   const void* w2T, const void* b2, const void* keep, void* out,
+                                   int64_t M, int64_t C, int64_t H, float eps, int add_input);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CFLK_B200_H */

@@ -37,13 +37,14 @@ def rel_max(a, b):
 
 
 def rel_l2(a, b):
-    """||a-b||_2 / max(||b||_2, 1e-12); NaN or inf counts as inf."""
+    """||a-b||_2 / max(||b||_2, 1e-3 sqrt(n)); NaN or inf counts as inf. The floor is the
+    rel_max floor per element: an exactly-zero gradient (one key) has no relative scale."""
     a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
     if not np.isfinite(a).all():
         return float('inf')
     if a.size == 0:
         return 0.0
-    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-12))
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-3 * np.sqrt(a.size)))
 
 
 def max_abs(a, b):

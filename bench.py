@@ -1,0 +1,400 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 hot path: pair-biased attention fwd+bwd (headline) and the pair-stack
+fusions, printed as one JSON line by rank 0.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N ...
+
+Headline workload (BASELINE.json's metric, quoted at N_res=512): MSA row attention with pair
+bias, N_seq=512 sequences x N_res=512 residues, H=8 heads of d=32, bf16; q, k, v = LN(m) W for a
+synthetic MSA m [512, 512, 256] ~ N(0,1) and W ~ N(0, 1/sqrt(256)); bias [8, 512, 512] ~ N(0,1);
+upstream gradient ~ N(0,1); seed 0. One step = VoltaMma (with lse) + VoltaMmaBwd (with dBias)
+over every sequence; with N GPUs the sequences are split across ranks (strong scaling) and the
+dBias partials are summed by an NCCL all-reduce. value = algorithmic FLOPs of the step
+(4 N H S^2 d forward + 10 N H S^2 d backward) / device time, max over ranks. L2 is flushed
+(a 256 MiB write) before every timed step.
+
+--impl reference times the reference's CPU arithmetic for the same path (the float32 port of
+its closed-form oracle, oracle/attention.py) on this host's cores, one bounded sample per step.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, 'colabfold-legacy-kernels_b200', 'src'))
+sys.path.insert(0, ROOT)
+
+METRIC = ("attn fwd+bwd TFLOP/s & %bf16 peak at N_res=512; pair-fusion GB/s & %HBM, "
+          "1/2/4/8 GPU")
+N_SEQ, N_RES, HEADS, HEAD_DIM, C_M = 512, 512, 8, 32, 256
+FALLBACK_PEAKS = {'hbm_gbs': 6650.0, 'bf16_tflops': 1590.0, 'bf16_tflops_sustained': 1400.0}
+CPU_SAMPLE_SEQ = 32      # sequences per CPU step (of 512)
+
+
+def peaks():
+    path = os.path.join(ROOT, 'MEASURED_PEAKS.json')
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return p, 'measured'
+    except (OSError, ValueError):
+        return dict(FALLBACK_PEAKS), 'fallback'
+
+
+def attn_flops(n, h=HEADS, s=N_RES, d=HEAD_DIM):
+    return 14.0 * n * h * s * s * d
+
+
+# ------------------------------------------------------------------------------------------
+# CPU: the reference's arithmetic (float32 port of its closed form), all host cores
+# ------------------------------------------------------------------------------------------
+def _cpu_worker(args):
+    import numpy as np
+    from oracle import attention as oa
+    seed, n = args
+    rng = np.random.default_rng(seed)
+    q, k, v, dout = (rng.standard_normal((n, HEADS, N_RES, HEAD_DIM), dtype=np.float32)
+                     for _ in range(4))
+    bias = rng.standard_normal((HEADS, N_RES, N_RES), dtype=np.float32)
+    km = np.ones((n, N_RES), np.uint8)
+    t0 = time.perf_counter()
+    oa.attention_grads_f32(q, k, v, bias, km, dout, HEAD_DIM ** -0.5)
+    return time.perf_counter() - t0
+
+
+class CpuBaseline:
+    """A spawn pool of one process per host core, each running single-threaded BLAS."""
+
+    def __init__(self):
+        import multiprocessing as mp
+        self.cores = os.cpu_count() or 1
+        for var in ('OMP_NUM_THREADS', 'OPENBLAS_NUM_THREADS', 'MKL_NUM_THREADS'):
+            os.environ[var] = '1'
+        self.pool = mp.get_context('spawn').Pool(self.cores)
+        self.pool.map(_cpu_worker, [(0, 1)] * self.cores)  # import and warm every worker
+
+    def step(self, seqs=CPU_SAMPLE_SEQ):
+        """Seconds of wall time for `seqs` sequences, spread over the pool."""
+        t0 = time.perf_counter()
+        self.pool.map(_cpu_worker, [(i, 1) for i in range(seqs)])
+        return time.perf_counter() - t0
+
+    def close(self):
+        self.pool.close()
+        self.pool.join()
+
+
+def cpu_sample_line(steps, warmup):
+    cpu = CpuBaseline()
+    try:
+        for _ in range(warmup):
+            cpu.step()
+        times = [cpu.step() for _ in range(steps)]
+    finally:
+        cpu.close()
+    t = sum(times) / len(times)
+    return {'value': attn_flops(CPU_SAMPLE_SEQ) / t / 1e12, 'unit': 'TFLOP/s',
+            'cores': cpu.cores, 'kind': 'port',
+            'sample': '%d of %d sequences per step (fwd+bwd, float32 numpy, one process per '
+                      'core), %.2f s per step' % (CPU_SAMPLE_SEQ, N_SEQ, t)}, t
+
+
+def run_reference(args):
+    rank = int(os.environ.get('RANK', '0'))
+    if rank != 0:
+        return
+    line, t = cpu_sample_line(max(args.steps, 1), max(args.warmup, 0))
+    out = {'impl': 'reference', 'metric': METRIC, 'value': line['value'], 'unit': 'TFLOP/s',
+           'n_gpus': args.gpus, 'steps': args.steps, 'warmup': args.warmup,
+           'ms_per_step': t * 1e3, 'higher_is_better': True, 'scaling': 'strong',
+           'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic',
+           'config': workload_config(1),
+           'cpu_baseline': line,
+           'e2e': {'value': line['value'], 'unit': 'TFLOP/s', 'h2d_bytes_per_step': 0,
+                   'd2h_bytes_per_step': 0}}
+    print(json.dumps(out), flush=True)
+
+
+def workload_config(world):
+    return {'workload': 'MSA row attention fwd+bwd with pair bias and dBias (BASELINE '
+                        'configs[2]): N_seq=512, N_res=512, H=8, d=32, bf16',
+            'N_seq': N_SEQ, 'N_res': N_RES, 'H': HEADS, 'd': HEAD_DIM, 'c_m': C_M,
+            'step': 'VoltaMma(want_lse) + VoltaMmaBwd(want_dbias)' +
+                    (' + NCCL dBias all-reduce' if world > 1 else ''),
+            'parallelism': 'dp%d over sequences' % world,
+            'l2': 'flushed before every timed step (256 MiB write)'}
+
+
+# ------------------------------------------------------------------------------------------
+# GPU
+# ------------------------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi sampling of this GPU's clocks and throttle reasons during a timed region."""
+
+    FIELDS = ('clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
+              'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
+              'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, bus_id):
+        self.proc = None
+        try:
+            cmd = ['nvidia-smi', '--query-gpu=' + self.FIELDS, '--format=csv,noheader,nounits',
+                   '-lms', '200']
+            if bus_id:
+                cmd += ['-i', bus_id]
+            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL,
+                                         text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], None, set()
+        names = ('hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap')
+        for line in out.splitlines():
+            f = [x.strip() for x in line.split(',')]
+            if len(f) < 8:
+                continue
+            try:
+                sm.append(float(f[0]))
+                mx = float(f[1])
+            except ValueError:
+                continue
+            for name, val in zip(names, f[4:8]):
+                if val.lower().startswith('active'):
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {'sm_mhz': statistics.median(sm), 'sm_max_mhz': mx, 'samples': len(sm),
+                'reasons': sorted(reasons)}
+
+
+def bus_id(torch, dev):
+    try:
+        p = torch.cuda.get_device_properties(dev)
+        return '%08x:%02x:%02x.0' % (p.pci_domain_id, p.pci_bus_id, p.pci_device_id)
+    except Exception:  # noqa: BLE001 - older torch without the PCI fields
+        return None
+
+
+def make_inputs(torch, dev, rank, world):
+    """Config 3's inputs, generated whole from one seed on every rank, then this rank's slice."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    bf = torch.bfloat16
+    m = torch.randn(N_SEQ, N_RES, C_M, generator=g, device=dev, dtype=torch.float32)
+    m = torch.nn.functional.layer_norm(m, (C_M,)).to(bf)
+    proj = []
+    for _ in range(3):
+        w = (torch.randn(C_M, HEADS * HEAD_DIM, generator=g, device=dev) * C_M ** -0.5).to(bf)
+        x = (m @ w).view(N_SEQ, N_RES, HEADS, HEAD_DIM).permute(0, 2, 1, 3).contiguous()
+        proj.append(x)
+    del m
+    bias = torch.randn(HEADS, N_RES, N_RES, generator=g, device=dev).to(bf)
+    dout = torch.randn(N_SEQ, HEADS, N_RES, HEAD_DIM, generator=g, device=dev).to(bf)
+    kmask = torch.ones(N_SEQ, N_RES, dtype=torch.uint8, device=dev)
+    per = N_SEQ // world
+    sl = slice(rank * per, (rank + 1) * per)
+    q, k, v = (x[sl].contiguous() for x in proj)
+    return q, k, v, bias, kmask[sl].contiguous(), dout[sl].contiguous()
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from colabfold_legacy_kernels import b200
+
+    rank = int(os.environ.get('RANK', '0'))
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    torch.cuda.set_device(local)
+    dev = torch.device('cuda', local)
+    if world > 1:
+        import datetime
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=300),
+                                device_id=dev)
+    pk, pk_kind = peaks()
+
+    cpu_line = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        # before any CUDA work: the pool is spawned, never forked
+        cpu_line, _ = cpu_sample_line(2, 1)
+
+    q, k, v, bias, kmask, dout = make_inputs(torch, dev, rank, world)
+    n_local = q.shape[0]
+    scale = HEAD_DIM ** -0.5
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def step():
+        out, lse = b200.volta_mma(q, k, v, bias, kmask, scale=scale, block_q=64, block_k=32)
+        dq, dk, dv, dbias = b200.volta_mma_bwd(q, k, v, bias, kmask, out, dout, lse, scale=scale)
+        if world > 1:
+            dist.all_reduce(dbias)
+        return dbias
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if b200.device_status() != 0:
+        raise RuntimeError('a kernel reported a wait that gave up')
+
+    clocks = ClockSampler(bus_id(torch, dev)) if rank == 0 else None
+    time.sleep(0.3)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        flush.fill_(i & 0xff)
+        starts[i].record()
+        step()
+        ends[i].record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop() if clocks else None
+    ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / args.steps
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    value = attn_flops(N_SEQ) / (ms * 1e-3) / 1e12
+
+    # per-kernel device time (the forward is one launch, the backward call four), L2 flushed
+    def timed(fn, reps):
+        evs = []
+        for _ in range(reps):
+            flush.fill_(1)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            evs.append((a, b))
+        torch.cuda.synchronize()
+        return sum(a.elapsed_time(b) for a, b in evs) / reps
+
+    out, lse = b200.volta_mma(q, k, v, bias, kmask, scale=scale)
+    fwd_ms = timed(lambda: b200.volta_mma(q, k, v, bias, kmask, scale=scale), args.steps)
+    bwd_ms = timed(lambda: b200.volta_mma_bwd(q, k, v, bias, kmask, out, dout, lse,
+                                              scale=scale), args.steps)
+    fwd_tf = 4.0 * n_local * HEADS * N_RES ** 2 * HEAD_DIM / (fwd_ms * 1e-3) / 1e12
+    bwd_tf = 10.0 * n_local * HEADS * N_RES ** 2 * HEAD_DIM / (bwd_ms * 1e-3) / 1e12
+
+    e2e = run_e2e(args, torch, dist, b200, dev, world, q, k, v, bias, kmask, dout, scale)
+
+    fusions = None
+    if not args.no_fusions:
+        fusions = bench_fusions(torch, b200, dev, rank, world, args.steps, args.warmup, flush,
+                                pk)
+
+    if rank == 0:
+        peak = pk['bf16_tflops']
+        line = {
+            'metric': METRIC, 'value': value, 'unit': 'TFLOP/s', 'n_gpus': world,
+            'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': ms,
+            'higher_is_better': True, 'scaling': 'strong', 'vs_baseline': None,
+            'dtype': 'bf16', 'data': 'synthetic', 'config': workload_config(world),
+            'frac_of_bf16_peak': value / (peak * world),
+            'roofline': {
+                'kernel': 'VoltaMmaBwd (attn_bwd_kernel + row_delta + dq_convert + fills)',
+                'bound': 'tensor', 'achieved': bwd_tf, 'peak': peak,
+                'peak_kind': pk_kind + ' burst bf16', 'unit': 'TFLOP/s',
+                'frac': bwd_tf / peak, 'traffic': None},
+            'kernels': {'fwd_ms': fwd_ms, 'fwd_tflops': fwd_tf, 'fwd_frac': fwd_tf / peak,
+                        'bwd_ms': bwd_ms, 'bwd_tflops': bwd_tf, 'bwd_frac': bwd_tf / peak,
+                        'sequences_per_gpu': n_local},
+            'e2e': e2e,
+            'gpu_launches': 4 * args.steps,
+            'clocks': clk,
+        }
+        if cpu_line is not None:
+            line['cpu_baseline'] = cpu_line
+        if fusions is not None:
+            line['fusions'] = fusions
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def bench_fusions(torch, b200, dev, rank, world, steps, warmup, flush, pk):
+    """Pair-stack fusion throughput; filled in with the fusion kernels."""
+    return None
+
+
+def run_e2e(args, torch, dist, b200, dev, world, q, k, v, bias, kmask, dout, scale):
+    """The same step through the public API from pinned host buffers: inputs copied in and the
+    gradients copied out inside the timed region."""
+    hosts = [t.cpu().pin_memory() for t in (q, k, v, bias, kmask, dout)]
+    devs = [torch.empty_like(t) for t in (q, k, v, bias, kmask, dout)]
+    outs_h = [torch.empty(q.shape, dtype=q.dtype).pin_memory() for _ in range(3)]
+    dbias_h = torch.empty(bias.shape, dtype=torch.float32).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in hosts)
+    d2h = sum(t.numel() * t.element_size() for t in outs_h) + dbias_h.numel() * 4
+
+    def step():
+        for d, h in zip(devs, hosts):
+            d.copy_(h, non_blocking=True)
+        tq, tk, tv, tb, tm, td = devs
+        out, lse = b200.volta_mma(tq, tk, tv, tb, tm, scale=scale)
+        dq, dk, dv, dbias = b200.volta_mma_bwd(tq, tk, tv, tb, tm, out, td, lse, scale=scale)
+        if world > 1:
+            dist.all_reduce(dbias)
+        for h, d in zip(outs_h, (dq, dk, dv)):
+            h.copy_(d, non_blocking=True)
+        dbias_h.copy_(dbias, non_blocking=True)
+
+    step()
+    torch.cuda.synchronize()
+    reps = max(3, min(args.steps, 10))
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    a.record()
+    for _ in range(reps):
+        step()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / reps
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    return {'value': attn_flops(N_SEQ) / (ms * 1e-3) / 1e12, 'unit': 'TFLOP/s',
+            'ms_per_step': ms, 'h2d_bytes_per_step': h2d, 'd2h_bytes_per_step': d2h,
+            'api': 'colabfold_legacy_kernels.b200.volta_mma / volta_mma_bwd (C ABI)'}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=20)
+    ap.add_argument('--warmup', type=int, default=5)
+    ap.add_argument('--impl', choices=('ours', 'reference'), default='ours')
+    ap.add_argument('--no-cpu', action='store_true', help='skip the cpu_baseline sample')
+    ap.add_argument('--no-fusions', action='store_true', help='skip the pair-fusion lines')
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == 'ours':
+        args.warmup = 3
+    if args.impl == 'reference':
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == '__main__':
+    main()

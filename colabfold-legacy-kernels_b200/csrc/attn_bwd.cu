@@ -631,3 +631,79 @@ extern "C" int cflk_volta_mma_bwd(void* stream_, int dtype, const void* q, const
     }
     return kOk;
 }
+
+// ---------------------------------------------------------------------------------------------
+// The backward without caller-provided workspace.
+//
+// Some callers of this library cannot allocate device memory: a plugin host that owns every
+// device allocation and hands a kernel only its inputs and outputs (no scratch allocator), or
+// latency-critical code that must not call cudaMalloc because it may synchronise the device.
+// For them the backward's scratch (the float32 dQ accumulator and the row statistic) lives in
+// this file-scope array instead, kNoAllocScratchBytes long. Every GPU that loads the library
+// holds the array until the process exits. All calls on a device share it and it keeps the last
+// call's contents: the backward zero-fills the accumulator itself on every call, and calls whose
+// kernels overlap on the GPU (different streams, no ordering) race on it.
+// ---------------------------------------------------------------------------------------------
+static constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+// The array's device address on the current device, looked up once per device. The host-side
+// name g_noalloc_scratch is only a stand-in for the symbol, never a device pointer.
+static int noalloc_scratch(void** out) {
+    static void* addr[cflk::kMaxDevices] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        return cflk::fail(cflk::kInternal, std::string("volta_mma_bwd_noalloc: ") +
+                                               cudaGetErrorString(e));
+    }
+    if (dev < 0 || dev >= cflk::kMaxDevices) {
+        return cflk::fail(cflk::kInternal, "volta_mma_bwd_noalloc: device ordinal out of range");
+    }
+    if (addr[dev] == nullptr) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || p == nullptr) {
+            return cflk::fail(cflk::kInternal,
+                              std::string("volta_mma_bwd_noalloc: scratch address: ") +
+                                  cudaGetErrorString(e));
+        }
+        addr[dev] = p;
+    }
+    *out = addr[dev];
+    return cflk::kOk;
+}
+
+extern "C" size_t cflk_volta_mma_bwd_noalloc_max_scratch(void) {
+    return kNoAllocScratchBytes;
+}
+
+extern "C" int cflk_volta_mma_bwd_noalloc(void* stream, int dtype, const void* q, const void* k,
+                                          const void* v, const void* bias, const uint8_t* kmask,
+                                          const void* out, const void* dout, const float* lse,
+                                          void* dq, void* dk, void* dv, float* dbias, int64_t N,
+                                          int64_t H, int64_t Sq, int64_t Sk, int64_t D,
+                                          float scale, int want_dbias) {
+    cflk::clear_error();
+    size_t need = 0;
+    int rc = cflk_volta_mma_bwd_workspace_size(N, H, Sq, Sk, D, &need);
+    if (rc != cflk::kOk) {
+        return rc;
+    }
+    if (need > kNoAllocScratchBytes) {
+        return cflk::fail(cflk::kInvalidArgument,
+                          "volta_mma_bwd_noalloc: needs " + std::to_string(need) +
+                              " bytes of scratch, the static scratch holds " +
+                              std::to_string(kNoAllocScratchBytes) +
+                              " (N*H*Sq*(D+1)*4 bytes plus alignment); use cflk_volta_mma_bwd "
+                              "with a workspace");
+    }
+    void* scratch = nullptr;
+    rc = noalloc_scratch(&scratch);
+    if (rc != cflk::kOk) {
+        return rc;
+    }
+    return cflk_volta_mma_bwd(stream, dtype, q, k, v, bias, kmask, out, dout, lse, dq, dk, dv,
+                              dbias, scratch, kNoAllocScratchBytes, N, H, Sq, Sk, D, scale,
+                              want_dbias);
+}

@@ -90,6 +90,25 @@ CFLK_API int cflk_volta_mma_bwd(void* stream, int dtype, const void* q, const vo
                                 size_t workspace_bytes, int64_t N, int64_t H, int64_t Sq,
                                 int64_t Sk, int64_t D, float scale, int want_dbias);
 
+/* VoltaMmaBwd for callers that cannot allocate device memory: the same computation and
+ * arguments as cflk_volta_mma_bwd without the workspace. This entry point has no counterpart in
+ * the reference; it exists for hosts that own every device allocation and give a kernel only its
+ * inputs and outputs, and for code that must not call cudaMalloc (which may synchronise the
+ * device). Its scratch is a static device array of cflk_volta_mma_bwd_noalloc_max_scratch()
+ * bytes (32 MiB) that every GPU loading the library holds until exit; a problem needing more
+ * (cflk_volta_mma_bwd_workspace_size) is rejected with CFLK_INVALID_ARGUMENT. The first call on
+ * a device looks up the array's device address (cudaGetSymbolAddress) for the current device,
+ * so make that first call before any stream capture. All calls on a device share the array:
+ * calls whose kernels overlap on the GPU race on it; calls ordered on one stream do not. The
+ * accumulator is zero-filled by every call. Nothing is allocated. */
+CFLK_API size_t cflk_volta_mma_bwd_noalloc_max_scratch(void);
+CFLK_API int cflk_volta_mma_bwd_noalloc(void* stream, int dtype, const void* q, const void* k,
+                                        const void* v, const void* bias, const uint8_t* kmask,
+                                        const void* out, const void* dout, const float* lse,
+                                        void* dq, void* dk, void* dv, float* dbias, int64_t N,
+                                        int64_t H, int64_t Sq, int64_t Sk, int64_t D,
+                                        float scale, int want_dbias);
+
 /* ---- LayerNorm-folded pair-stack fusions ------------------------------------------------ */
 /* keep [M] (16-bit) or NULL: per row tile, compute when a row of keep is above zero, write
  * padding (zeros, or nothing where the output aliases its input) when the tile is all zero,

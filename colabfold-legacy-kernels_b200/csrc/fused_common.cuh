@@ -1,0 +1,141 @@
+// The persistent row-tile pipeline shared by the LayerNorm-folded pair-stack fusions.
+//
+// A CTA walks 128-row tiles of the input (tile = blockIdx.x, + gridDim.x, ...). Warp 8 is the
+// producer: lane 0 loads the op's weights once (TMA, resident in shared memory for the whole
+// CTA), streams x tiles two stages deep, and issues the tcgen05 MMAs of each tile into tensor
+// memory. Warps 0-7 are two warpgroups of workers; worker (g, t) owns row t of the tile (TMEM
+// lane t) and half g of its columns: it runs the op's prologue (LayerNorm in place on the
+// swizzled tile) and epilogue (accumulators from TMEM, bias, gating, residual, stores).
+//
+// Row tiles follow the reference's keep rule (tile_work, colabfold-legacy-kernels
+// cuda/volta_gdp.h:114-136): a tile is computed when a row's keep is above zero, written as
+// padding when all are zero, and left alone when all are below zero; rows past M count as the
+// op's `other`. Every warp classifies a tile itself, so producer and workers agree on which
+// tiles enter the pipeline without talking to each other.
+#pragma once
+
+#include "sm100.cuh"
+
+namespace cflk {
+namespace fused {
+
+constexpr int BM = 128;            // rows per tile = TMEM lanes
+constexpr int kWorkers = 256;      // two warpgroups
+constexpr int kThreads = kWorkers + 32;
+constexpr int kProducerWarp = 8;
+constexpr int ATOM = BM * 128;     // one 64-column, 128-byte-swizzled atom of a 128-row tile
+
+enum Work : int { kCompute = 0, kPadding = 1, kSkip = 2 };
+
+// Byte offset of element (row r, column c) in a K-major tile of 128 rows stored as 64-column
+// atoms with the 128-byte swizzle (TMA's and the MMA's layout); c a multiple of 8 gives a
+// 16-byte chunk.
+__device__ __forceinline__ uint32_t sw128(int r, int c) {
+    return (uint32_t)((c >> 6) * ATOM + r * 128 + ((((c >> 3) & 7) ^ (r & 7)) << 4) + (c & 7) * 2);
+}
+
+// The same for a weight matrix [rows][K] staged as 64-column atoms of `rows` rows each.
+__device__ __forceinline__ uint32_t sw128_rows(int rows, int r, int c) {
+    return (uint32_t)((c >> 6) * rows * 128 + r * 128 + ((((c >> 3) & 7) ^ (r & 7)) << 4) +
+                      (c & 7) * 2);
+}
+
+// keep classification of rows [m0, m0 + BM), by one whole warp (every lane gets the result)
+template <typename T>
+__device__ __forceinline__ int tile_work(const T* keep, int M, int m0, float other) {
+    if (keep == nullptr) {
+        return kCompute;
+    }
+    const int lane = threadIdx.x & 31;
+    bool live = false, zero = false;
+#pragma unroll
+    for (int i = 0; i < BM / 32; ++i) {
+        const int r = m0 + lane + 32 * i;
+        const float k = r < M ? Elem<T>::to_f(keep[r]) : other;
+        live |= k > 0.f;
+        zero |= k == 0.f;
+    }
+    if (__any_sync(0xffffffffu, live)) {
+        return kCompute;
+    }
+    return __any_sync(0xffffffffu, zero) ? kPadding : kSkip;
+}
+
+// Barrier among the 256 workers (id 1).
+__device__ __forceinline__ void workers_sync() {
+    named_sync(1, kWorkers);
+}
+
+// K-major operand descriptor for the 128-byte-swizzled layout: 8-row groups 1024 bytes apart.
+__device__ __forceinline__ uint64_t desc_k128(uint32_t saddr) {
+    return smem_desc(saddr, 16, 1024, kSwizzle128B);
+}
+
+// LayerNorm of row t in place on a swizzled tile: worker half g holds columns
+// [g*K/2, (g+1)*K/2). Two-pass float32 statistics exchanged through red[2][2][BM]; the result
+// is rounded to T, as the reference rounds LN(x) before its GEMM. raw (optional) receives the
+// half row as it was, packed 2 per word.
+template <typename T, int K>
+__device__ __forceinline__ void ln_rows_half(uint8_t* tile, int t, int g, const float* scale,
+                                             const float* offset, float eps, float* red,
+                                             uint32_t* raw, float* y_out) {
+    using E = Elem<T>;
+    constexpr int KH = K / 2;
+    float v[KH];
+#pragma unroll
+    for (int ch = 0; ch < KH / 8; ++ch) {
+        const uint4 w = *reinterpret_cast<const uint4*>(tile + sw128(t, g * KH + 8 * ch));
+        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            if (raw != nullptr) {
+                raw[4 * ch + e] = ww[e];
+            }
+            const float2 f = E::unpack(ww[e]);
+            v[8 * ch + 2 * e] = f.x;
+            v[8 * ch + 2 * e + 1] = f.y;
+        }
+    }
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < KH; ++i) {
+        s += v[i];
+    }
+    red[(0 * 2 + g) * BM + t] = s;
+    workers_sync();
+    const float mean = (red[0 * BM + t] + red[1 * BM + t]) * (1.f / K);
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < KH; ++i) {
+        v[i] -= mean;
+        q += v[i] * v[i];
+    }
+    red[(2 + g) * BM + t] = q;
+    workers_sync();
+    const float rstd = rsqrtf((red[2 * BM + t] + red[3 * BM + t]) * (1.f / K) + eps);
+#pragma unroll
+    for (int ch = 0; ch < KH / 8; ++ch) {
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int c = g * KH + 8 * ch + 2 * e;
+            const float y0 = v[8 * ch + 2 * e] * rstd * scale[c] + offset[c];
+            const float y1 = v[8 * ch + 2 * e + 1] * rstd * scale[c + 1] + offset[c + 1];
+            w[e] = E::pack(y0, y1);
+            if (y_out != nullptr) {
+                const float2 r = E::unpack(w[e]);
+                y_out[8 * ch + 2 * e] = r.x;
+                y_out[8 * ch + 2 * e + 1] = r.y;
+            }
+        }
+        *reinterpret_cast<uint4*>(tile + sw128(t, g * KH + 8 * ch)) =
+            make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
+__device__ __forceinline__ float sigmoid_fast(float g) {
+    return __fdividef(1.f, 1.f + ex2(-1.4426950408889634f * g));
+}
+
+}  // namespace fused
+}  // namespace cflk

@@ -1,0 +1,710 @@
+// LayerNorm-folded pair-stack fusions for sm_100a: VoltaLnGdp, VoltaLnProj, VoltaOutProj,
+// VoltaTrimulEpilogue, VoltaTransition (colabfold-legacy-kernels cuda/volta_fused_ffi.h:42-259,
+// kernels cuda/volta_ops.cu:330-641). All run on the persistent row-tile pipeline of
+// fused_common.cuh: TMA-fed 128-row tiles, resident weights, tcgen05 MMAs into tensor memory,
+// LayerNorm prologue and epilogue in two worker warpgroups.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+#include <string>
+
+#include "capi_internal.h"
+#include "cflk_b200.h"
+#include "fused_common.cuh"
+#include "tmap.h"
+
+namespace cflk {
+namespace {
+
+__device__ unsigned g_status;
+
+using namespace fused;
+
+// ---------------------------------------------------------------------------------------------
+// the pipeline
+// ---------------------------------------------------------------------------------------------
+// Op supplies: T, Args (with M, w_bytes, param_floats, tmem_cols, nacc, eps), keep(), kOther,
+// X_BYTES, load_params, load_weights, load_x, issue_mma, prologue, epilogue, padding, Regs.
+template <class Op>
+__global__ void __launch_bounds__(kThreads, 1)
+    row_tile_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tw0,
+                    const __grid_constant__ CUtensorMap tw1, const typename Op::Args a) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* xs0 = smem;
+    uint8_t* ws = smem + 2 * Op::X_BYTES;
+    float* sp = reinterpret_cast<float*>(ws + a.w_bytes);
+    float* red = sp + a.param_floats;  // [Op::RED_FLOATS]
+    __shared__ uint64_t x_full[2], x_empty[2], a_ready[2], acc_full[2], acc_empty[2], w_full;
+    __shared__ uint32_t tmem_sh;
+    __shared__ int abort_flag;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ntiles = (a.M + BM - 1) / BM;
+    if (warp == kProducerWarp) {
+        if (lane == 0) {
+            for (int i = 0; i < 2; ++i) {
+                mbar_init(&x_full[i], 1);
+                mbar_init(&x_empty[i], 1);
+                mbar_init(&a_ready[i], kWorkers);
+                mbar_init(&acc_full[i], 1);
+                mbar_init(&acc_empty[i], kWorkers);
+            }
+            mbar_init(&w_full, 1);
+            abort_flag = 0;
+            fence_mbar_init();
+        }
+        __syncwarp();
+        tmem_alloc(&tmem_sh, a.tmem_cols * a.nacc <= 32    ? 32
+                             : a.tmem_cols * a.nacc <= 64  ? 64
+                             : a.tmem_cols * a.nacc <= 128 ? 128
+                             : a.tmem_cols * a.nacc <= 256 ? 256
+                                                           : 512);
+        tmem_relinquish();
+    } else {
+        Op::load_params(a, sp, threadIdx.x);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_sh;
+
+    if (warp == kProducerWarp) {
+        const auto next = [&](int& cursor) -> int {
+            while (cursor < ntiles) {
+                const int m0 = cursor * BM;
+                cursor += gridDim.x;
+                if (tile_work(Op::keep(a), a.M, m0, Op::kOther) == kCompute) {
+                    return m0;
+                }
+            }
+            return -1;
+        };
+        int cur = blockIdx.x, pcur = blockIdx.x, c = 0, pc = 0;
+        if (lane == 0) {
+            Op::load_weights(a, &tw0, &tw1, ws, &w_full);
+        }
+        for (int k = 0; k < 2; ++k) {
+            const int m = next(pcur);
+            if (m < 0) {
+                break;
+            }
+            if (lane == 0) {
+                Op::load_x(a, &tx, xs0 + (pc & 1) * Op::X_BYTES, &x_full[pc & 1], m);
+            }
+            ++pc;
+        }
+        bool weights_ready = false;
+        while (true) {
+            const int m = next(cur);
+            if (m < 0) {
+                break;
+            }
+            const int s = c & 1, r = c % a.nacc;
+            if (lane == 0) {
+                if (!weights_ready) {
+                    mbar_wait(&w_full, 0, &g_status, kStatusTmaWait, &abort_flag);
+                    weights_ready = true;
+                }
+                mbar_wait(&a_ready[s], (c >> 1) & 1, &g_status, kStatusSyncWait, &abort_flag);
+                if (c >= a.nacc) {
+                    mbar_wait(&acc_empty[r], ((c - a.nacc) / a.nacc) & 1, &g_status,
+                              kStatusSyncWait, &abort_flag);
+                }
+                tc_fence_after();
+                Op::issue_mma(a, smem_u32(xs0 + s * Op::X_BYTES), smem_u32(ws),
+                              tmem + r * a.tmem_cols);
+                mma_commit(&acc_full[r]);
+                mma_commit(&x_empty[s]);
+            }
+            __syncwarp();
+            const int m2 = next(pcur);
+            if (m2 >= 0) {
+                if (lane == 0) {
+                    mbar_wait(&x_empty[s], (c >> 1) & 1, &g_status, kStatusMmaWait, &abort_flag);
+                    Op::load_x(a, &tx, xs0 + s * Op::X_BYTES, &x_full[s], m2);
+                }
+                ++pc;
+            }
+            __syncwarp();
+            ++c;
+        }
+    } else {
+        const int g = warp >> 2, t = ((warp & 3) << 5) | lane;
+        const uint32_t lane_base = tmem_lane_base(warp);
+        typename Op::Regs regs;
+        int c = 0;
+        for (int cursor = blockIdx.x; cursor < ntiles; cursor += gridDim.x) {
+            const int m0 = cursor * BM;
+            const int work = tile_work(Op::keep(a), a.M, m0, Op::kOther);
+            if (work == kPadding) {
+                Op::padding(a, m0, t, g);
+                continue;
+            }
+            if (work == kSkip) {
+                continue;
+            }
+            const int s = c & 1, r = c % a.nacc;
+            uint8_t* stage = xs0 + s * Op::X_BYTES;
+            mbar_wait(&x_full[s], (c >> 1) & 1, &g_status, kStatusTmaWait, &abort_flag);
+            Op::prologue(a, stage, sp, red, t, g, m0, regs);
+            fence_async_smem();
+            mbar_arrive(&a_ready[s]);
+            mbar_wait(&acc_full[r], (c / a.nacc) & 1, &g_status, kStatusMmaWait, &abort_flag);
+            tc_fence_after();
+            Op::epilogue(a, tmem + r * a.tmem_cols + lane_base, sp, t, g, m0, regs);
+            tc_fence_before();
+            mbar_arrive(&acc_empty[r]);
+            ++c;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kProducerWarp) {
+        tc_fence_after();
+        tmem_dealloc(tmem, a.tmem_cols * a.nacc <= 32    ? 32
+                           : a.tmem_cols * a.nacc <= 64  ? 64
+                           : a.tmem_cols * a.nacc <= 128 ? 128
+                           : a.tmem_cols * a.nacc <= 256 ? 256
+                                                         : 512);
+    }
+}
+
+// TMA of the K columns of rows [m0, m0+128) of a row-major [M][K] map as 64-column atoms
+__device__ __forceinline__ void load_rows_tile(const CUtensorMap* map, uint8_t* dst,
+                                               uint64_t* bar, int K, int m0) {
+    mbar_arrive_expect_tx(bar, (uint32_t)(K * BM * 2));
+    for (int a = 0; a < K / 64; ++a) {
+        tma_load_2d(dst + a * ATOM, map, bar, a * 64, m0);
+    }
+}
+
+// Rows of one TMA box of a weight matrix: the largest of 256, 128, 64 that divides rows (a
+// multiple of 64), so that boxes tile the matrix exactly.
+__host__ __device__ __forceinline__ int weight_box(int rows) {
+    return rows % 256 == 0 ? 256 : rows % 128 == 0 ? 128 : 64;
+}
+
+// TMA of a whole weight matrix [rows][K] (row-major) into 64-column atoms of `rows` rows
+__device__ __forceinline__ void load_weight(const CUtensorMap* map, uint8_t* dst, uint64_t* bar,
+                                            int rows, int K) {
+    const int box = weight_box(rows);
+    for (int a = 0; a < K / 64; ++a) {
+        for (int r0 = 0; r0 < rows; r0 += box) {
+            tma_load_2d(dst + a * rows * 128 + r0 * 128, map, bar, a * 64, r0);
+        }
+    }
+}
+
+// D[128 x N] (+)= A[128 x K] W^T for W [rows][K] staged by load_weight, output columns
+// [n0, n0 + N), N <= 256 and a multiple of 16
+__device__ __forceinline__ void mma_rows(uint32_t d, uint32_t a_base, uint32_t w_base, int rows,
+                                         int K, int n0, int N, bool bf16, bool accumulate) {
+    const uint32_t id = idesc_f16(bf16, 128, N, false, false);
+    for (int k = 0; k < K / 16; ++k) {
+        const int at = k >> 2, off = (k & 3) * 32;
+        mma_ss(d, desc_k128(a_base + at * ATOM + off),
+               desc_k128(w_base + at * rows * 128 + n0 * 128 + off), id,
+               (accumulate || k > 0) ? 1u : 0u);
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// VoltaLnGdp: left/right [CI, M] = max(mask, 0) * (y wp + bp) * sigmoid(y wg + bg), y = LN(x)
+// ---------------------------------------------------------------------------------------------
+template <typename T_, int K, int CI>
+struct LnGdpOp {
+    using T = T_;
+    using E = Elem<T>;
+    static constexpr int P = 2 * CI;
+    static constexpr int X_BYTES = K * BM * 2;
+    static constexpr float kOther = 0.f;
+    static constexpr int RED_FLOATS = 4 * BM;
+    struct Args {
+        const T *x, *wpT, *bp, *wgT, *bg, *mask;
+        const float *scale, *offset;
+        T *left, *right;
+        int M, w_bytes, param_floats, tmem_cols, nacc;
+        float eps;
+    };
+    struct Regs {};
+    static __device__ const T* keep(const Args& a) { return a.mask; }
+    // scale [K], offset [K], bp [P], bg [P]
+    static __device__ void load_params(const Args& a, float* sp, int tid) {
+        for (int i = tid; i < K; i += kWorkers) {
+            sp[i] = a.scale[i];
+            sp[K + i] = a.offset[i];
+        }
+        for (int i = tid; i < P; i += kWorkers) {
+            sp[2 * K + i] = E::to_f(a.bp[i]);
+            sp[2 * K + P + i] = E::to_f(a.bg[i]);
+        }
+    }
+    static __device__ void load_weights(const Args& a, const CUtensorMap* tw0,
+                                        const CUtensorMap* tw1, uint8_t* ws, uint64_t* bar) {
+        mbar_arrive_expect_tx(bar, (uint32_t)(2 * P * K * 2));
+        load_weight(tw0, ws, bar, P, K);
+        load_weight(tw1, ws + P * K * 2, bar, P, K);
+    }
+    static __device__ void load_x(const Args& a, const CUtensorMap* tx, uint8_t* dst,
+                                  uint64_t* bar, int m0) {
+        load_rows_tile(tx, dst, bar, K, m0);
+    }
+    static __device__ void issue_mma(const Args& a, uint32_t xa, uint32_t wa, uint32_t acc) {
+        for (int mat = 0; mat < 2; ++mat) {
+            for (int n0 = 0; n0 < P; n0 += 256) {
+                const int N = P - n0 < 256 ? P - n0 : 256;
+                mma_rows(acc + mat * P + n0, xa, wa + mat * P * K * 2, P, K, n0, N, E::kBf16,
+                         false);
+            }
+        }
+    }
+    static __device__ void prologue(const Args& a, uint8_t* stage, const float* sp, float* red,
+                                    int t, int g, int m0, Regs&) {
+        ln_rows_half<T, K>(stage, t, g, sp, sp + K, a.eps, red, nullptr, nullptr);
+    }
+    static __device__ void epilogue(const Args& a, uint32_t acc, const float* sp, int t, int g,
+                                    int m0, Regs&) {
+        const int m = m0 + t;
+        const float mv = m < a.M ? fmaxf(E::to_f(a.mask[m]), 0.f) : 0.f;
+        T* out = g == 0 ? a.left : a.right;
+        const float* bp = sp + 2 * K + g * CI;
+        const float* bg = sp + 2 * K + P + g * CI;
+#pragma unroll 1
+        for (int c0 = 0; c0 < CI; c0 += 16) {
+            uint32_t pr[16], gr[16];
+            tmem_ld16(acc + g * CI + c0, pr);
+            tmem_ld16(acc + P + g * CI + c0, gr);
+            tmem_wait_ld();
+            if (m < a.M) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const float pv = __uint_as_float(pr[j]) + bp[c0 + j];
+                    const float gv = __uint_as_float(gr[j]) + bg[c0 + j];
+                    out[(long long)(c0 + j) * a.M + m] = E::from_f(mv * pv * sigmoid_fast(gv));
+                }
+            }
+        }
+    }
+    static __device__ void padding(const Args& a, int m0, int t, int g) {
+        const int m = m0 + t;
+        if (m >= a.M) {
+            return;
+        }
+        T* out = g == 0 ? a.left : a.right;
+        for (int c = 0; c < CI; ++c) {
+            out[(long long)c * a.M + m] = E::from_f(0.f);
+        }
+    }
+};
+
+// ---------------------------------------------------------------------------------------------
+// VoltaLnProj (LN = true): p [M, n] = LN(x) w, bias [heads, M] = (LN(x) wb)^T
+// VoltaOutProj (LN = false): out [M, n] = o w + b (+ residual)
+// One launch covers output columns [0, n) of a pass, n <= 512, p's row stride ldp.
+// ---------------------------------------------------------------------------------------------
+template <typename T_, int K, bool LN>
+struct ProjOp {
+    using T = T_;
+    using E = Elem<T>;
+    static constexpr int X_BYTES = K * BM * 2;
+    static constexpr float kOther = -1.f;
+    static constexpr int RED_FLOATS = 4 * BM + 16 * BM;  // LN sums + per-head halves
+    struct Args {
+        const T *x, *wT, *b, *residual, *wbT, *keep;
+        const float *scale, *offset;
+        T *out, *bias;
+        int M, n, ldp, heads;
+        int w_bytes, param_floats, tmem_cols, nacc;
+        float eps;
+    };
+    struct Regs {};
+    static __device__ const T* keep(const Args& a) { return a.keep; }
+    // scale [K], offset [K], b [n], wb [8][K]
+    static __device__ void load_params(const Args& a, float* sp, int tid) {
+        for (int i = tid; i < K; i += kWorkers) {
+            sp[i] = LN ? a.scale[i] : 0.f;
+            sp[K + i] = LN ? a.offset[i] : 0.f;
+        }
+        for (int i = tid; i < a.n; i += kWorkers) {
+            sp[2 * K + i] = a.b != nullptr ? E::to_f(a.b[i]) : 0.f;
+        }
+        for (int i = tid; i < 8 * K; i += kWorkers) {
+            sp[2 * K + a.n + i] = (i / K) < a.heads ? E::to_f(a.wbT[i]) : 0.f;
+        }
+    }
+    static __device__ void load_weights(const Args& a, const CUtensorMap* tw0,
+                                        const CUtensorMap*, uint8_t* ws, uint64_t* bar) {
+        mbar_arrive_expect_tx(bar, (uint32_t)(a.n * K * 2));
+        if (a.n > 0) {
+            load_weight(tw0, ws, bar, a.n, K);
+        }
+    }
+    static __device__ void load_x(const Args& a, const CUtensorMap* tx, uint8_t* dst,
+                                  uint64_t* bar, int m0) {
+        load_rows_tile(tx, dst, bar, K, m0);
+    }
+    static __device__ void issue_mma(const Args& a, uint32_t xa, uint32_t wa, uint32_t acc) {
+        for (int n0 = 0; n0 < a.n; n0 += 256) {
+            const int N = a.n - n0 < 256 ? a.n - n0 : 256;
+            mma_rows(acc + n0, xa, wa, a.n, K, n0, N, E::kBf16, false);
+        }
+    }
+    static __device__ void prologue(const Args& a, uint8_t* stage, const float* sp, float* red,
+                                    int t, int g, int m0, Regs&) {
+        if constexpr (LN) {
+            float y[K / 2];
+            ln_rows_half<T, K>(stage, t, g, sp, sp + K, a.eps, red, nullptr, y);
+            if (a.heads > 0) {
+                // the per-head bias: a row reduction over the rounded LN(x), halves summed
+                const float* wb = sp + 2 * K + a.n;
+                float* hred = red + 4 * BM;
+                for (int h = 0; h < a.heads; ++h) {
+                    float d = 0.f;
+#pragma unroll
+                    for (int i = 0; i < K / 2; ++i) {
+                        d = fmaf(y[i], wb[h * K + g * (K / 2) + i], d);
+                    }
+                    hred[(h * 2 + g) * BM + t] = d;
+                }
+                workers_sync();
+                if (g == 0 && m0 + t < a.M) {
+                    for (int h = 0; h < a.heads; ++h) {
+                        a.bias[(long long)h * a.M + m0 + t] =
+                            E::from_f(hred[(h * 2) * BM + t] + hred[(h * 2 + 1) * BM + t]);
+                    }
+                }
+            }
+        }
+    }
+    static __device__ void epilogue(const Args& a, uint32_t acc, const float* sp, int t, int g,
+                                    int m0, Regs&) {
+        const int m = m0 + t;
+        const int half = a.n / 2;
+        const float* b = sp + 2 * K;
+        T* orow = a.out + (long long)m * a.ldp;
+        const T* rrow = a.residual != nullptr ? a.residual + (long long)m * a.ldp : nullptr;
+#pragma unroll 1
+        for (int c0 = g * half; c0 < (g + 1) * half; c0 += 16) {
+            uint32_t r[16];
+            tmem_ld16(acc + c0, r);
+            tmem_wait_ld();
+            if (m < a.M) {
+                float v[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    v[j] = __uint_as_float(r[j]) + b[c0 + j];
+                }
+                if (rrow != nullptr) {
+                    const uint4 q0 = *reinterpret_cast<const uint4*>(rrow + c0);
+                    const uint4 q1 = *reinterpret_cast<const uint4*>(rrow + c0 + 8);
+                    const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        const float2 f = E::unpack(qw[e]);
+                        v[2 * e] += f.x;
+                        v[2 * e + 1] += f.y;
+                    }
+                }
+                uint32_t w[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    w[e] = E::pack(v[2 * e], v[2 * e + 1]);
+                }
+                *reinterpret_cast<uint4*>(orow + c0) = make_uint4(w[0], w[1], w[2], w[3]);
+                *reinterpret_cast<uint4*>(orow + c0 + 8) = make_uint4(w[4], w[5], w[6], w[7]);
+            }
+        }
+    }
+    static __device__ void padding(const Args& a, int m0, int t, int g) {
+        const int m = m0 + t;
+        if (m >= a.M) {
+            return;
+        }
+        // with a residual the output aliases it, which it keeps
+        if (a.n > 0 && a.residual == nullptr) {
+            const int half = a.n / 2;
+            T* orow = a.out + (long long)m * a.ldp;
+            for (int c = g * half; c < (g + 1) * half; c += 8) {
+                *reinterpret_cast<uint4*>(orow + c) = make_uint4(0, 0, 0, 0);
+            }
+        }
+        if (g == 0) {
+            for (int h = 0; h < a.heads; ++h) {
+                a.bias[(long long)h * a.M + m] = E::from_f(0.f);
+            }
+        }
+    }
+};
+
+// ---------------------------------------------------------------------------------------------
+// host
+// ---------------------------------------------------------------------------------------------
+int sm_count() {
+    static int cache[kMaxDevices] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= kMaxDevices) {
+        return 148;
+    }
+    if (cache[dev] == 0) {
+        cudaDeviceGetAttribute(&cache[dev], cudaDevAttrMultiProcessorCount, dev);
+        if (cache[dev] <= 0) {
+            cache[dev] = 148;
+        }
+    }
+    return cache[dev];
+}
+
+bool aligned16(const void* p) {
+    return (reinterpret_cast<uintptr_t>(p) & 15) == 0;
+}
+
+CUtensorMapDataType tdt(int dtype) {
+    return dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+}
+
+// row-major [rows][cols] 16-bit matrix, boxes of 64 columns x box_rows rows, 128-byte swizzle
+bool map_rows(CUtensorMap* m, int dtype, const void* base, long long rows, long long cols,
+              long long ld, int box_rows) {
+    const uint64_t dims[2] = {(uint64_t)cols, (uint64_t)(rows > 0 ? rows : 1)};
+    const uint64_t strides[1] = {(uint64_t)ld};
+    const uint32_t box[2] = {64, (uint32_t)box_rows};
+    return encode_tiled(m, tdt(dtype), 2, 2, base, dims, strides, box,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+template <class Op>
+cudaError_t launch_op(cudaStream_t stream, const CUtensorMap& tx, const CUtensorMap& tw0,
+                      const CUtensorMap& tw1, const typename Op::Args& a) {
+    auto kern = row_tile_kernel<Op>;
+    const int smem = 2 * Op::X_BYTES + a.w_bytes + (a.param_floats + Op::RED_FLOATS) * 4 + 1024;
+    const cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) {
+        return e;
+    }
+    const int ntiles = (a.M + BM - 1) / BM;
+    const int grid = std::min(ntiles, sm_count());
+    kern<<<grid, kThreads, smem, stream>>>(tx, tw0, tw1, a);
+    return cudaGetLastError();
+}
+
+int launch_status(cudaError_t e, const char* who) {
+    if (e != cudaSuccess) {
+        return fail(kInternal, std::string(who) + " launch: " + cudaGetErrorString(e));
+    }
+    return kOk;
+}
+
+template <typename T, int K, int CI>
+cudaError_t ln_gdp_typed(cudaStream_t stream, int dtype, const void* x, const float* scale,
+                         const float* offset, const void* wpT, const void* bp, const void* wgT,
+                         const void* bg, const void* mask, void* left, void* right, int M,
+                         float eps) {
+    using Op = LnGdpOp<T, K, CI>;
+    CUtensorMap tx, tw0, tw1;
+    if (!map_rows(&tx, dtype, x, M, K, K, BM) ||
+        !map_rows(&tw0, dtype, wpT, 2 * CI, K, K, weight_box(2 * CI)) ||
+        !map_rows(&tw1, dtype, wgT, 2 * CI, K, K, weight_box(2 * CI))) {
+        return cudaErrorInvalidValue;
+    }
+    typename Op::Args a;
+    a.x = static_cast<const T*>(x);
+    a.wpT = static_cast<const T*>(wpT);
+    a.bp = static_cast<const T*>(bp);
+    a.wgT = static_cast<const T*>(wgT);
+    a.bg = static_cast<const T*>(bg);
+    a.mask = static_cast<const T*>(mask);
+    a.scale = scale;
+    a.offset = offset;
+    a.left = static_cast<T*>(left);
+    a.right = static_cast<T*>(right);
+    a.M = M;
+    a.w_bytes = 2 * Op::P * K * 2;
+    a.param_floats = 2 * K + 2 * Op::P;
+    a.tmem_cols = 2 * Op::P;
+    a.nacc = 2 * Op::P <= 256 ? 2 : 1;
+    a.eps = eps;
+    return launch_op<Op>(stream, tx, tw0, tw1, a);
+}
+
+template <typename T, int K, bool LN>
+cudaError_t proj_typed(cudaStream_t stream, int dtype, const void* x, const float* scale,
+                       const float* offset, const void* wT, const void* b, const void* residual,
+                       const void* wbT, const void* keep, void* out, void* bias, int M, int n,
+                       int ldp, int heads, float eps) {
+    using Op = ProjOp<T, K, LN>;
+    CUtensorMap tx, tw0;
+    if (!map_rows(&tx, dtype, x, M, K, K, BM)) {
+        return cudaErrorInvalidValue;
+    }
+    if (n > 0) {
+        if (!map_rows(&tw0, dtype, wT, n, K, K, weight_box(n))) {
+            return cudaErrorInvalidValue;
+        }
+    } else {
+        tw0 = tx;
+    }
+    typename Op::Args a;
+    a.x = static_cast<const T*>(x);
+    a.wT = static_cast<const T*>(wT);
+    a.b = static_cast<const T*>(b);
+    a.residual = static_cast<const T*>(residual);
+    a.wbT = static_cast<const T*>(wbT);
+    a.keep = static_cast<const T*>(keep);
+    a.scale = scale;
+    a.offset = offset;
+    a.out = static_cast<T*>(out);
+    a.bias = static_cast<T*>(bias);
+    a.M = M;
+    a.n = n;
+    a.ldp = ldp;
+    a.heads = heads;
+    a.w_bytes = n * K * 2;
+    a.param_floats = 2 * K + n + 8 * K;
+    a.tmem_cols = n > 0 ? n : 32;
+    a.nacc = n <= 256 ? 2 : 1;
+    a.eps = eps;
+    return launch_op<Op>(stream, tx, tw0, tw0, a);
+}
+
+}  // namespace
+
+unsigned read_and_clear_status_fused() {
+    unsigned v = 0, z = 0;
+    cudaMemcpyFromSymbol(&v, g_status, sizeof(v));
+    cudaMemcpyToSymbol(g_status, &z, sizeof(z));
+    return v;
+}
+
+}  // namespace cflk
+
+using namespace cflk;
+
+extern "C" int cflk_volta_ln_gdp(void* stream, int dtype, const void* x, const float* scale,
+                                 const float* offset, const void* wpT, const void* bp,
+                                 const void* wgT, const void* bg, const void* mask, void* left,
+                                 void* right, int64_t M, int64_t K, int64_t P, float eps) {
+    clear_error();
+    if (dtype != kF16 && dtype != kBF16) {
+        return fail(kInvalidArgument, "ln_gdp: dtype must be f16 or bf16");
+    }
+    if ((K != 64 && K != 128) || P % 2 || (P / 2 != 64 && P / 2 != 128) || M < 0) {
+        return fail(kInvalidArgument, "ln_gdp: K and P/2 must be 64 or 128");
+    }
+    if (M == 0) {
+        return kOk;
+    }
+    if (!aligned16(x) || !aligned16(wpT) || !aligned16(wgT)) {
+        return fail(kInvalidArgument, "ln_gdp: buffers must be 16-byte aligned");
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int m = (int)M, ci = (int)(P / 2);
+    cudaError_t e;
+#define CFLK_GDP(T)                                                                              \
+    (K == 64 ? (ci == 64 ? ln_gdp_typed<T, 64, 64>(s, dtype, x, scale, offset, wpT, bp, wgT, bg, \
+                                                   mask, left, right, m, eps)                    \
+                         : ln_gdp_typed<T, 64, 128>(s, dtype, x, scale, offset, wpT, bp, wgT,    \
+                                                    bg, mask, left, right, m, eps))              \
+             : (ci == 64 ? ln_gdp_typed<T, 128, 64>(s, dtype, x, scale, offset, wpT, bp, wgT,    \
+                                                    bg, mask, left, right, m, eps)               \
+                         : ln_gdp_typed<T, 128, 128>(s, dtype, x, scale, offset, wpT, bp, wgT,   \
+                                                     bg, mask, left, right, m, eps)))
+    e = dtype == kBF16 ? CFLK_GDP(__nv_bfloat16) : CFLK_GDP(__half);
+#undef CFLK_GDP
+    return launch_status(e, "ln_gdp");
+}
+
+extern "C" int cflk_volta_ln_proj(void* stream, int dtype, const void* x, const float* scale,
+                                  const float* offset, const void* wT, const void* wbT,
+                                  const void* keep, void* p, void* bias, int64_t M, int64_t K,
+                                  int64_t n, int64_t heads, float eps) {
+    clear_error();
+    if (dtype != kF16 && dtype != kBF16) {
+        return fail(kInvalidArgument, "ln_projection: dtype must be f16 or bf16");
+    }
+    if ((K != 64 && K != 128) || n < 0 || n % 64 || heads < 0 || heads > 8 || M < 0) {
+        return fail(kInvalidArgument,
+                    "ln_projection: K must be 64 or 128, n a multiple of 64, at most 8 heads");
+    }
+    if (M == 0 || (n == 0 && heads == 0)) {
+        return kOk;
+    }
+    if (!aligned16(x) || (n > 0 && (!aligned16(wT) || !aligned16(p)))) {
+        return fail(kInvalidArgument, "ln_projection: buffers must be 16-byte aligned");
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int esz = 2;
+    // passes of at most 512 output columns over the same rows; the head bias in the first
+    for (int64_t n0 = 0; n0 < n || (n0 == 0 && n == 0); n0 += 512) {
+        const int np = (int)std::min<int64_t>(512, n - n0);
+        const void* w = n > 0 ? static_cast<const uint8_t*>(wT) + n0 * K * esz : nullptr;
+        void* po = n > 0 ? static_cast<uint8_t*>(p) + n0 * esz : nullptr;
+        const int hp = n0 == 0 ? (int)heads : 0;
+        cudaError_t e;
+        if (dtype == kBF16) {
+            e = K == 64 ? proj_typed<__nv_bfloat16, 64, true>(s, dtype, x, scale, offset, w,
+                                                              nullptr, nullptr, wbT, keep, po,
+                                                              bias, (int)M, np, (int)n, hp, eps)
+                        : proj_typed<__nv_bfloat16, 128, true>(s, dtype, x, scale, offset, w,
+                                                               nullptr, nullptr, wbT, keep, po,
+                                                               bias, (int)M, np, (int)n, hp, eps);
+        } else {
+            e = K == 64 ? proj_typed<__half, 64, true>(s, dtype, x, scale, offset, w, nullptr,
+                                                       nullptr, wbT, keep, po, bias, (int)M, np,
+                                                       (int)n, hp, eps)
+                        : proj_typed<__half, 128, true>(s, dtype, x, scale, offset, w, nullptr,
+                                                        nullptr, wbT, keep, po, bias, (int)M, np,
+                                                        (int)n, hp, eps);
+        }
+        if (e != cudaSuccess) {
+            return launch_status(e, "ln_projection");
+        }
+        if (n == 0) {
+            break;
+        }
+    }
+    return kOk;
+}
+
+extern "C" int cflk_volta_out_proj(void* stream, int dtype, const void* o, const void* wT,
+                                   const void* b, const void* residual, const void* keep,
+                                   void* out, int64_t M, int64_t K, int64_t N) {
+    clear_error();
+    if (dtype != kF16 && dtype != kBF16) {
+        return fail(kInvalidArgument, "output_projection: dtype must be f16 or bf16");
+    }
+    if ((K != 64 && K != 128) || (N != 64 && N != 128) || M < 0) {
+        return fail(kInvalidArgument, "output_projection: K and N must be 64 or 128");
+    }
+    if (M == 0) {
+        return kOk;
+    }
+    if (!aligned16(o) || !aligned16(wT) || !aligned16(out) ||
+        (residual != nullptr && !aligned16(residual))) {
+        return fail(kInvalidArgument, "output_projection: buffers must be 16-byte aligned");
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e;
+    if (dtype == kBF16) {
+        e = K == 64 ? proj_typed<__nv_bfloat16, 64, false>(s, dtype, o, nullptr, nullptr, wT, b,
+                                                           residual, nullptr, keep, out, nullptr,
+                                                           (int)M, (int)N, (int)N, 0, 0.f)
+                    : proj_typed<__nv_bfloat16, 128, false>(s, dtype, o, nullptr, nullptr, wT, b,
+                                                            residual, nullptr, keep, out,
+                                                            nullptr, (int)M, (int)N, (int)N, 0,
+                                                            0.f);
+    } else {
+        e = K == 64 ? proj_typed<__half, 64, false>(s, dtype, o, nullptr, nullptr, wT, b,
+                                                    residual, nullptr, keep, out, nullptr,
+                                                    (int)M, (int)N, (int)N, 0, 0.f)
+                    : proj_typed<__half, 128, false>(s, dtype, o, nullptr, nullptr, wT, b,
+                                                     residual, nullptr, keep, out, nullptr,
+                                                     (int)M, (int)N, (int)N, 0, 0.f);
+    }
+    return launch_status(e, "output_projection");
+}

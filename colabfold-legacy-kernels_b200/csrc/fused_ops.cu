@@ -441,6 +441,546 @@ struct ProjOp {
 };
 
 // ---------------------------------------------------------------------------------------------
+// VoltaTrimulEpilogue: out [M, O] = (LN(x_cm^T) wo + bo) * sigmoid(LN_in(x) wg + bg) (+ x)
+// A tile stage holds Y = LN(x_cm^T) (C columns, written by the workers from the float32
+// channel-major triangle product) and then x (CA columns, TMA), normalised in place.
+// ---------------------------------------------------------------------------------------------
+template <typename T_, int C, int CA, int O, bool ADD>
+struct TrimulOp {
+    using T = T_;
+    using E = Elem<T>;
+    static constexpr int X_BYTES = (C + CA) * BM * 2;
+    static constexpr int XOFF = C * BM * 2;  // x's atoms after Y's
+    static constexpr float kOther = -1.f;
+    static constexpr int RED_FLOATS = 8 * BM;
+    struct Args {
+        const float* x_cm;
+        const T *x, *woT, *bo, *wgT, *bg, *keep;
+        const float *in_scale, *in_offset, *ln_scale, *ln_offset;
+        T* out;
+        int M, w_bytes, param_floats, tmem_cols, nacc;
+        float eps;
+    };
+    struct Regs {};
+    static __device__ const T* keep(const Args& a) { return a.keep; }
+    // in_scale [CA], in_offset [CA], ln_scale [C], ln_offset [C], bo [O], bg [O]
+    static __device__ void load_params(const Args& a, float* sp, int tid) {
+        for (int i = tid; i < CA; i += kWorkers) {
+            sp[i] = a.in_scale[i];
+            sp[CA + i] = a.in_offset[i];
+        }
+        for (int i = tid; i < C; i += kWorkers) {
+            sp[2 * CA + i] = a.ln_scale[i];
+            sp[2 * CA + C + i] = a.ln_offset[i];
+        }
+        for (int i = tid; i < O; i += kWorkers) {
+            sp[2 * CA + 2 * C + i] = E::to_f(a.bo[i]);
+            sp[2 * CA + 2 * C + O + i] = E::to_f(a.bg[i]);
+        }
+    }
+    static __device__ void load_weights(const Args& a, const CUtensorMap* tw0,
+                                        const CUtensorMap* tw1, uint8_t* ws, uint64_t* bar) {
+        mbar_arrive_expect_tx(bar, (uint32_t)((O * C + O * CA) * 2));
+        load_weight(tw0, ws, bar, O, C);
+        load_weight(tw1, ws + O * C * 2, bar, O, CA);
+    }
+    static __device__ void load_x(const Args& a, const CUtensorMap* tx, uint8_t* dst,
+                                  uint64_t* bar, int m0) {
+        load_rows_tile(tx, dst + XOFF, bar, CA, m0);
+    }
+    static __device__ void issue_mma(const Args& a, uint32_t xa, uint32_t wa, uint32_t acc) {
+        mma_rows(acc, xa, wa, O, C, 0, O, E::kBf16, false);
+        mma_rows(acc + O, xa + XOFF, wa + O * C * 2, O, CA, 0, O, E::kBf16, false);
+    }
+    static __device__ void prologue(const Args& a, uint8_t* stage, const float* sp, float* red,
+                                    int t, int g, int m0, Regs&) {
+        // LN over the C channels of column m of the channel-major float32 x_cm
+        constexpr int CH = C / 2;
+        const int m = m0 + t;
+        const bool in = m < a.M;
+        float v[CH];
+#pragma unroll
+        for (int i = 0; i < CH; ++i) {
+            v[i] = in ? a.x_cm[(long long)(g * CH + i) * a.M + m] : 0.f;
+        }
+        float s = 0.f;
+#pragma unroll
+        for (int i = 0; i < CH; ++i) {
+            s += v[i];
+        }
+        float* r2 = red + 4 * BM;
+        r2[g * BM + t] = s;
+        workers_sync();
+        const float mean = (r2[t] + r2[BM + t]) * (1.f / C);
+        float q = 0.f;
+#pragma unroll
+        for (int i = 0; i < CH; ++i) {
+            v[i] -= mean;
+            q += v[i] * v[i];
+        }
+        r2[(2 + g) * BM + t] = q;
+        workers_sync();
+        const float rstd = rsqrtf((r2[2 * BM + t] + r2[3 * BM + t]) * (1.f / C) + a.eps);
+        const float* ls = sp + 2 * CA;
+        const float* lo = sp + 2 * CA + C;
+#pragma unroll
+        for (int ch = 0; ch < CH / 8; ++ch) {
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int c = g * CH + 8 * ch + 2 * e;
+                w[e] = E::pack(v[8 * ch + 2 * e] * rstd * ls[c] + lo[c],
+                               v[8 * ch + 2 * e + 1] * rstd * ls[c + 1] + lo[c + 1]);
+            }
+            *reinterpret_cast<uint4*>(stage + sw128(t, g * CH + 8 * ch)) =
+                make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        // then LN_in(x) in place on the TMA-loaded x atoms
+        ln_rows_half<T, CA>(stage + XOFF, t, g, sp, sp + CA, a.eps, red, nullptr, nullptr);
+    }
+    static __device__ void epilogue(const Args& a, uint32_t acc, const float* sp, int t, int g,
+                                    int m0, Regs&) {
+        const int m = m0 + t;
+        const float* bo = sp + 2 * CA + 2 * C;
+        const float* bg = bo + O;
+        T* orow = a.out + (long long)m * O;
+        const T* xrow = a.x + (long long)m * CA;
+#pragma unroll 1
+        for (int c0 = g * (O / 2); c0 < (g + 1) * (O / 2); c0 += 16) {
+            uint32_t ro[16], rg[16];
+            tmem_ld16(acc + c0, ro);
+            tmem_ld16(acc + O + c0, rg);
+            tmem_wait_ld();
+            if (m < a.M) {
+                float v[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    v[j] = (__uint_as_float(ro[j]) + bo[c0 + j]) *
+                           sigmoid_fast(__uint_as_float(rg[j]) + bg[c0 + j]);
+                }
+                if constexpr (ADD) {
+                    const uint4 q0 = *reinterpret_cast<const uint4*>(xrow + c0);
+                    const uint4 q1 = *reinterpret_cast<const uint4*>(xrow + c0 + 8);
+                    const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        const float2 f = E::unpack(qw[e]);
+                        v[2 * e] += f.x;
+                        v[2 * e + 1] += f.y;
+                    }
+                }
+                uint32_t w[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    w[e] = E::pack(v[2 * e], v[2 * e + 1]);
+                }
+                *reinterpret_cast<uint4*>(orow + c0) = make_uint4(w[0], w[1], w[2], w[3]);
+                *reinterpret_cast<uint4*>(orow + c0 + 8) = make_uint4(w[4], w[5], w[6], w[7]);
+            }
+        }
+    }
+    static __device__ void padding(const Args& a, int m0, int t, int g) {
+        const int m = m0 + t;
+        if (ADD || m >= a.M) {  // with add_input the output aliases x, which it keeps
+            return;
+        }
+        T* orow = a.out + (long long)m * O;
+        for (int c = g * (O / 2); c < (g + 1) * (O / 2); c += 8) {
+            *reinterpret_cast<uint4*>(orow + c) = make_uint4(0, 0, 0, 0);
+        }
+    }
+};
+
+// ---------------------------------------------------------------------------------------------
+// VoltaTransition: out [M, C] = relu(LN(x) w1 + b1) w2 + b2 (+ x)
+//
+// A CTA tile is SUB*128 rows (SUB = 2 for C <= 128, so that every weight chunk serves 256 rows;
+// 1 for C = 256). The hidden dimension is walked in 64-wide chunks j: GEMM1 writes
+// acc1[s][j%2] = LN(x)_s w1[:, chunk] into tensor memory; the workers add b1, apply the ReLU and
+// write the 16-bit result back over the same columns; GEMM2 accumulates acc2[s] += hidden_s
+// w2[chunk, :] with its A operand read from tensor memory. Weight chunks (w1's 64 rows and w2T's
+// chunk, [C][64], exactly the reference's chunked layout) stream through a shared-memory ring
+// filled by a loader warp (warp 9); warp 8 issues the MMAs.
+// ---------------------------------------------------------------------------------------------
+template <int C>
+struct TransCfg {
+    static constexpr int SUB = C <= 128 ? 2 : 1;
+    static constexpr int ROWS = SUB * BM;
+    static constexpr int X_BYTES = ROWS * C * 2;           // one stage
+    static constexpr int SLOT = 2 * C * 128;               // w1 chunk + w2 chunk
+    static constexpr int NSLOT = C == 64 ? 6 : C == 128 ? 4 : 2;
+    static constexpr int ACC2 = 0;                         // acc2[s] at s * C
+    static constexpr int ACC1 = SUB * C;                   // acc1[s][b] at ACC1 + (b*SUB + s)*64
+    static constexpr int COLS = ACC1 + 2 * SUB * 64;
+    static constexpr int ALLOC = COLS <= 256 ? 256 : 512;
+    static constexpr int THREADS = kWorkers + 64;          // + MMA warp + loader warp
+};
+
+template <typename T>
+struct TransArgs {
+    const T *x, *w1T, *b1, *w2T, *b2, *keep;
+    const float *scale, *offset;
+    T* out;
+    int M, H;
+    float eps;
+    bool add;
+};
+
+template <typename T, int C>
+__global__ void __launch_bounds__(TransCfg<C>::THREADS, 1)
+    transition_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tw1,
+                      const __grid_constant__ CUtensorMap tw2, const TransArgs<T> a) {
+    using G = TransCfg<C>;
+    using E = Elem<T>;
+    constexpr int SUB = G::SUB, ROWS = G::ROWS, NSLOT = G::NSLOT;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* xs = smem;                       // [SUB][C/64 atoms][128 rows][128 B]
+    uint8_t* ring = smem + G::X_BYTES;        // NSLOT x (w1 chunk [C/64][64][128B], w2 chunk)
+    float* sp = reinterpret_cast<float*>(ring + NSLOT * G::SLOT);  // scale, offset, b2, b1
+    float* red = sp + 3 * C + a.H;            // [4][BM]
+    __shared__ uint64_t x_full, x_empty, a_ready, acc1_full[2], hid_ready[2], g2_done[2],
+        acc2_full, acc2_empty, w_full[NSLOT], w_empty[NSLOT];
+    __shared__ uint32_t tmem_sh;
+    __shared__ int abort_flag;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int NH = a.H / 64;
+    const int ntiles = (a.M + ROWS - 1) / ROWS;
+    if (warp == kProducerWarp) {
+        if (lane == 0) {
+            mbar_init(&x_full, 1);
+            mbar_init(&x_empty, 1);
+            mbar_init(&a_ready, kWorkers);
+            for (int i = 0; i < 2; ++i) {
+                mbar_init(&acc1_full[i], 1);
+                mbar_init(&hid_ready[i], kWorkers);
+                mbar_init(&g2_done[i], 1);
+            }
+            mbar_init(&acc2_full, 1);
+            mbar_init(&acc2_empty, kWorkers);
+            for (int i = 0; i < NSLOT; ++i) {
+                mbar_init(&w_full[i], 1);
+                mbar_init(&w_empty[i], 1);
+            }
+            abort_flag = 0;
+            fence_mbar_init();
+        }
+        __syncwarp();
+        tmem_alloc(&tmem_sh, G::ALLOC);
+        tmem_relinquish();
+    } else if (warp < kProducerWarp) {
+        for (int i = threadIdx.x; i < C; i += kWorkers) {
+            sp[i] = a.scale[i];
+            sp[C + i] = a.offset[i];
+            sp[2 * C + i] = E::to_f(a.b2[i]);
+        }
+        for (int i = threadIdx.x; i < a.H; i += kWorkers) {
+            sp[3 * C + i] = E::to_f(a.b1[i]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_sh;
+    const auto work_of = [&](int tile) {
+        // a CTA tile is SUB row tiles; it is computed when any of them is
+        int w = kSkip;
+        for (int s = 0; s < SUB; ++s) {
+            w = min(w, tile_work(a.keep, a.M, tile * ROWS + s * BM, -1.f));
+        }
+        return w;
+    };
+
+    if (warp == kProducerWarp + 1) {
+        // loader: the weight chunks of every computed tile, in order
+        int q = 0;
+        for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+            if (work_of(tile) != kCompute) {
+                continue;
+            }
+            for (int j = 0; j < NH; ++j, ++q) {
+                const int slot = q % NSLOT;
+                if (lane == 0) {
+                    if (q >= NSLOT) {
+                        mbar_wait(&w_empty[slot], ((q - NSLOT) / NSLOT) & 1, &g_status,
+                                  kStatusMmaWait, &abort_flag);
+                    }
+                    uint8_t* dst = ring + slot * G::SLOT;
+                    mbar_arrive_expect_tx(&w_full[slot], G::SLOT);
+                    for (int at = 0; at < C / 64; ++at) {
+                        tma_load_2d(dst + at * 64 * 128, &tw1, &w_full[slot], at * 64, j * 64);
+                    }
+                    // w2T chunk j: [C][64] rows j*C .. j*C + C of the [H/64 * C][64] view
+                    for (int r0 = 0; r0 < C; r0 += 128) {
+                        tma_load_2d(dst + C * 128 + r0 * 128, &tw2, &w_full[slot], 0,
+                                    j * C + r0);
+                    }
+                }
+                __syncwarp();
+            }
+        }
+    } else if (warp == kProducerWarp) {
+        // MMA issue
+        int q = 0, c = 0;
+        int cursor = blockIdx.x;
+        const auto next = [&]() -> int {
+            while (cursor < ntiles) {
+                const int tile = cursor;
+                cursor += gridDim.x;
+                if (work_of(tile) == kCompute) {
+                    return tile;
+                }
+            }
+            return -1;
+        };
+        int tile = next();
+        if (tile >= 0 && lane == 0) {
+            mbar_arrive_expect_tx(&x_full, G::X_BYTES);
+            for (int s = 0; s < SUB; ++s) {
+                for (int at = 0; at < C / 64; ++at) {
+                    tma_load_2d(xs + s * BM * C * 2 + at * ATOM, &tx, &x_full, at * 64,
+                                tile * ROWS + s * BM);
+                }
+            }
+        }
+        const uint32_t id1 = idesc_f16(E::kBf16, 128, 64, false, false);
+        const uint32_t id2 = idesc_f16(E::kBf16, 128, C, false, false);
+        while (tile >= 0) {
+            const int ntile = next();
+            if (lane == 0) {
+                mbar_wait(&a_ready, c & 1, &g_status, kStatusSyncWait, &abort_flag);
+                tc_fence_after();
+                const auto gemm2 = [&](int jj) {
+                    const int hq = q + jj, b = hq & 1, slot = hq % NSLOT;
+                    mbar_wait(&hid_ready[b], (hq >> 1) & 1, &g_status, kStatusSyncWait,
+                              &abort_flag);
+                    if (jj == 0 && c > 0) {
+                        mbar_wait(&acc2_empty, (c - 1) & 1, &g_status, kStatusSyncWait,
+                                  &abort_flag);
+                    }
+                    tc_fence_after();
+                    const uint32_t w2 = smem_u32(ring + slot * G::SLOT + C * 128);
+                    for (int s = 0; s < SUB; ++s) {
+                        for (int k = 0; k < 4; ++k) {
+                            mma_ts(tmem + G::ACC2 + s * C,
+                                   tmem + G::ACC1 + (b * SUB + s) * 64 + k * 8,
+                                   desc_k128(w2 + k * 32), id2, (jj > 0 || k > 0) ? 1u : 0u);
+                        }
+                    }
+                    mma_commit(&g2_done[b]);
+                    mma_commit(&w_empty[slot]);
+                };
+                for (int j = 0; j < NH; ++j) {
+                    const int hq = q + j, b = hq & 1, slot = hq % NSLOT;
+                    mbar_wait(&w_full[slot], (hq / NSLOT) & 1, &g_status, kStatusTmaWait,
+                              &abort_flag);
+                    if (hq >= 2) {
+                        mbar_wait(&g2_done[b], ((hq - 2) >> 1) & 1, &g_status, kStatusMmaWait,
+                                  &abort_flag);
+                    }
+                    tc_fence_after();
+                    const uint32_t w1 = smem_u32(ring + slot * G::SLOT);
+                    for (int s = 0; s < SUB; ++s) {
+                        mma_rows(tmem + G::ACC1 + (b * SUB + s) * 64, smem_u32(xs + s * BM * C * 2),
+                                 w1, 64, C, 0, 64, E::kBf16, false);
+                    }
+                    mma_commit(&acc1_full[b]);
+                    if (j == NH - 1) {
+                        mma_commit(&x_empty);
+                    }
+                    if (j >= 1) {
+                        gemm2(j - 1);
+                    }
+                }
+                gemm2(NH - 1);
+                mma_commit(&acc2_full);
+                if (ntile >= 0) {
+                    // the next tile's x, once this tile's GEMM1s no longer read the stage
+                    mbar_wait(&x_empty, c & 1, &g_status, kStatusMmaWait, &abort_flag);
+                    mbar_arrive_expect_tx(&x_full, G::X_BYTES);
+                    for (int s = 0; s < SUB; ++s) {
+                        for (int at = 0; at < C / 64; ++at) {
+                            tma_load_2d(xs + s * BM * C * 2 + at * ATOM, &tx, &x_full, at * 64,
+                                        ntile * ROWS + s * BM);
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+            q += NH;
+            ++c;
+            tile = ntile;
+        }
+    } else {
+        // workers: (g, t) = sub-tile g, row t (SUB = 2), or column half g of row t (SUB = 1)
+        const int g = warp >> 2, t = ((warp & 3) << 5) | lane;
+        const uint32_t lane_base = tmem_lane_base(warp);
+        int q = 0, c = 0;
+        for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+            const int w = work_of(tile);
+            const int s = SUB == 2 ? g : 0;
+            const int m = tile * ROWS + s * BM + t;
+            if (w == kPadding) {
+                if (!a.add && m < a.M) {
+                    T* orow = a.out + (long long)m * C;
+                    const int c0 = SUB == 2 ? 0 : g * (C / 2), c1 = SUB == 2 ? C : c0 + C / 2;
+                    for (int cc = c0; cc < c1; cc += 8) {
+                        *reinterpret_cast<uint4*>(orow + cc) = make_uint4(0, 0, 0, 0);
+                    }
+                }
+                continue;
+            }
+            if (w == kSkip) {
+                continue;
+            }
+            mbar_wait(&x_full, c & 1, &g_status, kStatusTmaWait, &abort_flag);
+            uint8_t* tile_s = xs + s * BM * C * 2;
+            if constexpr (SUB == 2) {
+                // a full row per worker: plain two-pass LN, no exchange
+                using Ev = Elem<T>;
+                float v[C];
+#pragma unroll
+                for (int ch = 0; ch < C / 8; ++ch) {
+                    const uint4 u = *reinterpret_cast<const uint4*>(tile_s + sw128(t, 8 * ch));
+                    const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 f = Ev::unpack(uw[e]);
+                        v[8 * ch + 2 * e] = f.x;
+                        v[8 * ch + 2 * e + 1] = f.y;
+                    }
+                }
+                float sum = 0.f;
+#pragma unroll
+                for (int i = 0; i < C; ++i) {
+                    sum += v[i];
+                }
+                const float mean = sum * (1.f / C);
+                float sq = 0.f;
+#pragma unroll
+                for (int i = 0; i < C; ++i) {
+                    v[i] -= mean;
+                    sq += v[i] * v[i];
+                }
+                const float rstd = rsqrtf(sq * (1.f / C) + a.eps);
+#pragma unroll
+                for (int ch = 0; ch < C / 8; ++ch) {
+                    uint32_t ww[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int cc = 8 * ch + 2 * e;
+                        ww[e] = Ev::pack(v[cc] * rstd * sp[cc] + sp[C + cc],
+                                         v[cc + 1] * rstd * sp[cc + 1] + sp[C + cc + 1]);
+                    }
+                    *reinterpret_cast<uint4*>(tile_s + sw128(t, 8 * ch)) =
+                        make_uint4(ww[0], ww[1], ww[2], ww[3]);
+                }
+            } else {
+                ln_rows_half<T, C>(tile_s, t, g, sp, sp + C, a.eps, red, nullptr, nullptr);
+            }
+            fence_async_smem();
+            mbar_arrive(&a_ready);
+            // hidden chunks: bias, ReLU, 16-bit pairs back over the accumulator's columns
+            for (int j = 0; j < NH; ++j) {
+                const int hq = q + j, b = hq & 1;
+                mbar_wait(&acc1_full[b], (hq >> 1) & 1, &g_status, kStatusMmaWait, &abort_flag);
+                tc_fence_after();
+                const uint32_t base = tmem + G::ACC1 + (b * SUB + s) * 64 + lane_base;
+                const float* b1 = sp + 3 * C + j * 64;
+                if constexpr (SUB == 2) {
+                    uint32_t r0[32], r1[32];
+                    tmem_ld32(base, r0);
+                    tmem_ld32(base + 32, r1);
+                    tmem_wait_ld();
+                    uint32_t pk[32];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        pk[i] = E::pack(fmaxf(__uint_as_float(r0[2 * i]) + b1[2 * i], 0.f),
+                                        fmaxf(__uint_as_float(r0[2 * i + 1]) + b1[2 * i + 1], 0.f));
+                        pk[16 + i] =
+                            E::pack(fmaxf(__uint_as_float(r1[2 * i]) + b1[32 + 2 * i], 0.f),
+                                    fmaxf(__uint_as_float(r1[2 * i + 1]) + b1[33 + 2 * i], 0.f));
+                    }
+                    tmem_st16(base, *reinterpret_cast<uint32_t(*)[16]>(pk));
+                    tmem_st16(base + 16, *reinterpret_cast<uint32_t(*)[16]>(pk + 16));
+                } else {
+                    // column half g: hidden columns [32g, 32g+32) -> packed columns [16g, 16g+16)
+                    uint32_t r0[32];
+                    tmem_ld32(base + 32 * g, r0);
+                    tmem_wait_ld();
+                    uint32_t pk[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        pk[i] = E::pack(
+                            fmaxf(__uint_as_float(r0[2 * i]) + b1[32 * g + 2 * i], 0.f),
+                            fmaxf(__uint_as_float(r0[2 * i + 1]) + b1[32 * g + 2 * i + 1], 0.f));
+                    }
+                    // both halves must have read the fp32 columns before either overwrites them
+                    workers_sync();
+                    tmem_st16(base + 16 * g, pk);
+                }
+                tmem_wait_st();
+                tc_fence_before();
+                mbar_arrive(&hid_ready[b]);
+            }
+            mbar_wait(&acc2_full, c & 1, &g_status, kStatusMmaWait, &abort_flag);
+            tc_fence_after();
+            {
+                const uint32_t acc = tmem + G::ACC2 + s * C + lane_base;
+                const int c0 = SUB == 2 ? 0 : g * (C / 2), c1 = SUB == 2 ? C : c0 + C / 2;
+                T* orow = a.out + (long long)m * C;
+                const T* xrow = a.x + (long long)m * C;
+#pragma unroll 1
+                for (int cc = c0; cc < c1; cc += 16) {
+                    uint32_t r[16];
+                    tmem_ld16(acc + cc, r);
+                    tmem_wait_ld();
+                    if (m < a.M) {
+                        float v[16];
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            v[i] = __uint_as_float(r[i]) + sp[2 * C + cc + i];
+                        }
+                        if (a.add) {
+                            const uint4 q0 = *reinterpret_cast<const uint4*>(xrow + cc);
+                            const uint4 q1 = *reinterpret_cast<const uint4*>(xrow + cc + 8);
+                            const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w,
+                                                    q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) {
+                                const float2 f = E::unpack(qw[e]);
+                                v[2 * e] += f.x;
+                                v[2 * e + 1] += f.y;
+                            }
+                        }
+                        uint32_t ww[8];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) {
+                            ww[e] = E::pack(v[2 * e], v[2 * e + 1]);
+                        }
+                        *reinterpret_cast<uint4*>(orow + cc) = make_uint4(ww[0], ww[1], ww[2], ww[3]);
+                        *reinterpret_cast<uint4*>(orow + cc + 8) =
+                            make_uint4(ww[4], ww[5], ww[6], ww[7]);
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&acc2_empty);
+            q += NH;
+            ++c;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kProducerWarp) {
+        tc_fence_after();
+        tmem_dealloc(tmem, G::ALLOC);
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
 // host
 // ---------------------------------------------------------------------------------------------
 int sm_count() {
@@ -570,6 +1110,113 @@ cudaError_t proj_typed(cudaStream_t stream, int dtype, const void* x, const floa
     a.nacc = n <= 256 ? 2 : 1;
     a.eps = eps;
     return launch_op<Op>(stream, tx, tw0, tw0, a);
+}
+
+
+template <typename T, int C, int CA, int O, bool ADD>
+cudaError_t trimul_typed(cudaStream_t stream, int dtype, const float* x_cm, const void* x,
+                         const float* in_scale, const float* in_offset, const float* ln_scale,
+                         const float* ln_offset, const void* woT, const void* bo, const void* wgT,
+                         const void* bg, const void* keep, void* out, int M, float eps) {
+    using Op = TrimulOp<T, C, CA, O, ADD>;
+    CUtensorMap tx, tw0, tw1;
+    if (!map_rows(&tx, dtype, x, M, CA, CA, BM) ||
+        !map_rows(&tw0, dtype, woT, O, C, C, weight_box(O)) ||
+        !map_rows(&tw1, dtype, wgT, O, CA, CA, weight_box(O))) {
+        return cudaErrorInvalidValue;
+    }
+    typename Op::Args a;
+    a.x_cm = x_cm;
+    a.x = static_cast<const T*>(x);
+    a.woT = static_cast<const T*>(woT);
+    a.bo = static_cast<const T*>(bo);
+    a.wgT = static_cast<const T*>(wgT);
+    a.bg = static_cast<const T*>(bg);
+    a.keep = static_cast<const T*>(keep);
+    a.in_scale = in_scale;
+    a.in_offset = in_offset;
+    a.ln_scale = ln_scale;
+    a.ln_offset = ln_offset;
+    a.out = static_cast<T*>(out);
+    a.M = M;
+    a.w_bytes = (O * C + O * CA) * 2;
+    a.param_floats = 2 * CA + 2 * C + 2 * O;
+    a.tmem_cols = 2 * O;
+    a.nacc = 2;
+    a.eps = eps;
+    return launch_op<Op>(stream, tx, tw0, tw1, a);
+}
+
+template <typename T, int C, int CA>
+cudaError_t trimul_o(cudaStream_t s, int dtype, int O, bool add, const float* x_cm,
+                     const void* x, const float* is, const float* io, const float* ls,
+                     const float* lo, const void* woT, const void* bo, const void* wgT,
+                     const void* bg, const void* keep, void* out, int M, float eps) {
+    if (add) {  // O == CA
+        return trimul_typed<T, C, CA, CA, true>(s, dtype, x_cm, x, is, io, ls, lo, woT, bo, wgT,
+                                                bg, keep, out, M, eps);
+    }
+    return O == 64 ? trimul_typed<T, C, CA, 64, false>(s, dtype, x_cm, x, is, io, ls, lo, woT,
+                                                       bo, wgT, bg, keep, out, M, eps)
+                   : trimul_typed<T, C, CA, 128, false>(s, dtype, x_cm, x, is, io, ls, lo, woT,
+                                                        bo, wgT, bg, keep, out, M, eps);
+}
+
+template <typename T>
+cudaError_t trimul_dispatch(cudaStream_t s, int dtype, int C, int CA, int O, bool add,
+                            const float* x_cm, const void* x, const float* is, const float* io,
+                            const float* ls, const float* lo, const void* woT, const void* bo,
+                            const void* wgT, const void* bg, const void* keep, void* out, int M,
+                            float eps) {
+    if (C == 64) {
+        return CA == 64 ? trimul_o<T, 64, 64>(s, dtype, O, add, x_cm, x, is, io, ls, lo, woT, bo,
+                                              wgT, bg, keep, out, M, eps)
+                        : trimul_o<T, 64, 128>(s, dtype, O, add, x_cm, x, is, io, ls, lo, woT,
+                                               bo, wgT, bg, keep, out, M, eps);
+    }
+    return CA == 64 ? trimul_o<T, 128, 64>(s, dtype, O, add, x_cm, x, is, io, ls, lo, woT, bo,
+                                           wgT, bg, keep, out, M, eps)
+                    : trimul_o<T, 128, 128>(s, dtype, O, add, x_cm, x, is, io, ls, lo, woT, bo,
+                                            wgT, bg, keep, out, M, eps);
+}
+
+
+template <typename T, int C>
+cudaError_t transition_typed(cudaStream_t stream, int dtype, const void* x, const float* scale,
+                             const float* offset, const void* w1T, const void* b1,
+                             const void* w2T, const void* b2, const void* keep, void* out, int M,
+                             int H, float eps, bool add) {
+    using G = TransCfg<C>;
+    CUtensorMap tx, tw1, tw2;
+    // w2T [H/64][C][64] viewed as [H/64 * C] rows of 64
+    if (!map_rows(&tx, dtype, x, M, C, C, BM) || !map_rows(&tw1, dtype, w1T, H, C, C, 64) ||
+        !map_rows(&tw2, dtype, w2T, (long long)(H / 64) * C, 64, 64, std::min(C, 128))) {
+        return cudaErrorInvalidValue;
+    }
+    TransArgs<T> a;
+    a.x = static_cast<const T*>(x);
+    a.w1T = static_cast<const T*>(w1T);
+    a.b1 = static_cast<const T*>(b1);
+    a.w2T = static_cast<const T*>(w2T);
+    a.b2 = static_cast<const T*>(b2);
+    a.keep = static_cast<const T*>(keep);
+    a.scale = scale;
+    a.offset = offset;
+    a.out = static_cast<T*>(out);
+    a.M = M;
+    a.H = H;
+    a.eps = eps;
+    a.add = add;
+    auto kern = transition_kernel<T, C>;
+    const int smem = G::X_BYTES + G::NSLOT * G::SLOT + (3 * C + H + 4 * BM) * 4 + 1024;
+    const cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) {
+        return e;
+    }
+    const int ntiles = (M + G::ROWS - 1) / G::ROWS;
+    kern<<<std::min(ntiles, sm_count()), G::THREADS, smem, stream>>>(tx, tw1, tw2, a);
+    return cudaGetLastError();
 }
 
 }  // namespace
@@ -707,4 +1354,69 @@ extern "C" int cflk_volta_out_proj(void* stream, int dtype, const void* o, const
                                                      (int)M, (int)N, (int)N, 0, 0.f);
     }
     return launch_status(e, "output_projection");
+}
+
+extern "C" int cflk_volta_trimul_epilogue(void* stream, int dtype, const float* x_cm,
+                                          const void* x, const float* in_scale,
+                                          const float* in_offset, const float* ln_scale,
+                                          const float* ln_offset, const void* woT, const void* bo,
+                                          const void* wgT, const void* bg, const void* keep,
+                                          void* out, int64_t M, int64_t C, int64_t CA, int64_t O,
+                                          float eps, int add_input) {
+    clear_error();
+    if (dtype != kF16 && dtype != kBF16) {
+        return fail(kInvalidArgument, "trimul_epilogue: dtype must be f16 or bf16");
+    }
+    const auto w = [](int64_t c) { return c == 64 || c == 128; };
+    if (!w(C) || !w(CA) || !w(O) || (add_input && O != CA) || M < 0) {
+        return fail(kInvalidArgument,
+                    "trimul_epilogue: C, CA and O must be 64 or 128, O == CA with add_input");
+    }
+    if (M == 0) {
+        return kOk;
+    }
+    if (!aligned16(x) || !aligned16(woT) || !aligned16(wgT) || !aligned16(out)) {
+        return fail(kInvalidArgument, "trimul_epilogue: buffers must be 16-byte aligned");
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const cudaError_t e =
+        dtype == kBF16
+            ? trimul_dispatch<__nv_bfloat16>(s, dtype, (int)C, (int)CA, (int)O, add_input != 0,
+                                             x_cm, x, in_scale, in_offset, ln_scale, ln_offset,
+                                             woT, bo, wgT, bg, keep, out, (int)M, eps)
+            : trimul_dispatch<__half>(s, dtype, (int)C, (int)CA, (int)O, add_input != 0, x_cm, x,
+                                      in_scale, in_offset, ln_scale, ln_offset, woT, bo, wgT, bg,
+                                      keep, out, (int)M, eps);
+    return launch_status(e, "trimul_epilogue");
+}
+
+extern "C" int cflk_volta_transition(void* stream, int dtype, const void* x, const float* scale,
+                                     const float* offset, const void* w1T, const void* b1,
+                                     const void* w2T, const void* b2, const void* keep, void* out,
+                                     int64_t M, int64_t C, int64_t H, float eps, int add_input) {
+    clear_error();
+    if (dtype != kF16 && dtype != kBF16) {
+        return fail(kInvalidArgument, "transition: dtype must be f16 or bf16");
+    }
+    if ((C != 64 && C != 128 && C != 256) || (H != 2 * C && H != 4 * C) || M < 0) {
+        return fail(kInvalidArgument, "transition: C must be 64, 128 or 256, H 2C or 4C");
+    }
+    if (M == 0) {
+        return kOk;
+    }
+    if (!aligned16(x) || !aligned16(w1T) || !aligned16(w2T) || !aligned16(out)) {
+        return fail(kInvalidArgument, "transition: buffers must be 16-byte aligned");
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e;
+#define CFLK_TR(T)                                                                              \
+    (C == 64    ? transition_typed<T, 64>(s, dtype, x, scale, offset, w1T, b1, w2T, b2, keep,   \
+                                          out, (int)M, (int)H, eps, add_input != 0)             \
+     : C == 128 ? transition_typed<T, 128>(s, dtype, x, scale, offset, w1T, b1, w2T, b2, keep,  \
+                                           out, (int)M, (int)H, eps, add_input != 0)            \
+                : transition_typed<T, 256>(s, dtype, x, scale, offset, w1T, b1, w2T, b2, keep,  \
+                                           out, (int)M, (int)H, eps, add_input != 0))
+    e = dtype == kBF16 ? CFLK_TR(__nv_bfloat16) : CFLK_TR(__half);
+#undef CFLK_TR
+    return launch_status(e, "transition");
 }

@@ -244,3 +244,106 @@ def test_rejects_unsupported_widths(cuda_device):
     with pytest.raises(ValueError, match='multiple of 64'):
         m.volta_ln_proj(x[:, :128].contiguous(), f[:128], f[:128], w[:32, :128].contiguous(),
                         w[:4, :128].contiguous(), f, eps=1e-5, n=32, heads=4, has_keep=False)
+
+
+# ---- trimul_epilogue ------------------------------------------------------------------------
+
+def trimul_case(CA, C, M, dt, d, add, amp=50., mean=0., keep=None, seed=0, alias=False):
+    g = Gen(seed, dt)
+    O = CA
+    x = g.h(M, CA, s=2.)
+    x_cm = g.f(C, M, s=amp, mean=mean)
+    isc, iof = g.f(CA, s=.1, mean=1.), g.f(CA, s=.1)
+    lsc, lof = g.f(C, s=.1, mean=1.), g.f(C, s=.1)
+    woT, bo, wgT, bg = g.h(O, C, s=.1), g.h(O, s=.1), g.h(O, CA, s=.1), g.h(O, s=.1)
+    before = x if alias else np.zeros((M, O))
+    want = of.trimul_epilogue(x_cm, x, isc, iof, lsc, lof, woT, bo, wgT, bg, keep, 1e-5, add, dt,
+                              TILE, before=before)
+    m = b200()
+    z = torch.zeros(1, dtype=TD[dt], device=d)
+    tx = dev16(x, dt, d)
+    out = m.volta_trimul_epilogue(
+        dev32(x_cm, d), tx, dev32(isc, d), dev32(iof, d), dev32(lsc, d), dev32(lof, d),
+        dev16(woT, dt, d), dev16(bo, dt, d), dev16(wgT, dt, d), dev16(bg, dt, d),
+        dev16(keep, dt, d) if keep is not None else z, eps=1e-5, add_input=add,
+        has_keep=keep is not None, out=tx if alias else None)
+    assert m.device_status() == 0
+    return host(out), want
+
+
+@pytest.mark.parametrize('dt', ['bf16', 'f16'])
+@pytest.mark.parametrize('M', ROWS)
+@pytest.mark.parametrize('CA,C', WIDTHS)
+def test_trimul_epilogue(CA, C, M, dt, cuda_device):
+    # the triangle product is float32 and wide; one case sits far from zero (two-pass stats)
+    for amp, mean in ((50., 0.), (5., 1e3)):
+        for add in (False, True):
+            got, want = trimul_case(CA, C, M, dt, cuda_device, add, amp, mean)
+            close('trimul amp %g mean %g add %s' % (amp, mean, add), got, want)
+
+
+@pytest.mark.parametrize('case', KEEP_CASES[:3], ids=['%s_%d_%d' % c for c in KEEP_CASES[:3]])
+def test_trimul_keep_aliased(case, cuda_device):
+    keep = keep_vector(*case)
+    M = keep.size
+    got, want = trimul_case(128, 128, M, 'bf16', cuda_device, True, 20., 0., keep=keep,
+                            alias=True)
+    close('trimul keep aliased', got, want)
+    got0, _ = trimul_case(128, 128, M, 'bf16', cuda_device, True, 20., 0., alias=True)
+    live = keep > 0
+    assert np.array_equal(got[live], got0[live])
+
+
+# ---- transition ---------------------------------------------------------------------------
+
+def trans_tile(C):
+    return 256 if C <= 128 else 128
+
+
+def transition_case(C, factor, M, dt, d, add, keep=None, seed=0, alias=False):
+    g = Gen(seed, dt)
+    H = factor * C
+    x = g.h(M, C, s=2.)
+    sc, off = g.f(C, s=.1, mean=1.), g.f(C, s=.1)
+    w1T, b1 = g.h(H, C, s=C ** -.5), g.h(H, s=.1)
+    w2 = g.h(H, C, s=H ** -.5)
+    w2T = of.chunk_w2(w2)
+    b2 = g.h(C, s=.1)
+    before = x if alias else np.zeros((M, C))
+    want = of.transition(x, sc, off, w1T, b1, w2T, b2, keep, 1e-5, add, dt, trans_tile(C),
+                         before=before)
+    m = b200()
+    z = torch.zeros(1, dtype=TD[dt], device=d)
+    tx = dev16(x, dt, d)
+    out = m.volta_transition(tx, dev32(sc, d), dev32(off, d), dev16(w1T, dt, d),
+                             dev16(b1, dt, d), dev16(w2T, dt, d), dev16(b2, dt, d),
+                             dev16(keep, dt, d) if keep is not None else z, eps=1e-5,
+                             add_input=add, has_keep=keep is not None,
+                             out=tx if alias else None)
+    assert m.device_status() == 0
+    return host(out), want
+
+
+@pytest.mark.parametrize('dt', ['bf16', 'f16'])
+@pytest.mark.parametrize('M', ROWS)
+@pytest.mark.parametrize('C,factor', [(128, 4), (64, 2), (64, 4), (256, 4), (128, 2),
+                                      (256, 2)])
+def test_transition(C, factor, M, dt, cuda_device):
+    for add in (False, True):
+        got, want = transition_case(C, factor, M, dt, cuda_device, add)
+        close('transition add %s' % add, got, want)
+
+
+@pytest.mark.parametrize('case', KEEP_CASES, ids=['%s_%d_%d' % c for c in KEEP_CASES])
+@pytest.mark.parametrize('C', [128, 256])
+def test_transition_keep(case, C, cuda_device):
+    keep = keep_vector(*case)
+    M = keep.size
+    got, want = transition_case(C, 4, M, 'bf16', cuda_device, False, keep=keep)
+    close('transition keep', got, want)
+    got0, _ = transition_case(C, 4, M, 'bf16', cuda_device, False)
+    live = keep > 0
+    assert np.array_equal(got[live], got0[live])
+    assert np.all((got[~live] == got0[~live]) | (got[~live] == 0))
+    got, want = transition_case(C, 4, M, 'bf16', cuda_device, True, keep=keep, alias=True)
+    close('transition keep aliased', got, want)

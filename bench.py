@@ -189,8 +189,9 @@ def bus_id(torch, dev):
         return None
 
 
-def make_inputs(torch, dev, rank, world):
-    """Config 3's inputs, generated whole from one seed on every rank, then this rank's slice."""
+def make_inputs(torch, dev, rank, world, n_seq=N_SEQ):
+    """Config 3's inputs, generated whole from one seed on every rank, then this rank's slice
+    (the first n_seq sequences when a profiling run asks for fewer)."""
     g = torch.Generator(device=dev)
     g.manual_seed(0)
     bf = torch.bfloat16
@@ -205,7 +206,7 @@ def make_inputs(torch, dev, rank, world):
     bias = torch.randn(HEADS, N_RES, N_RES, generator=g, device=dev).to(bf)
     dout = torch.randn(N_SEQ, HEADS, N_RES, HEAD_DIM, generator=g, device=dev).to(bf)
     kmask = torch.ones(N_SEQ, N_RES, dtype=torch.uint8, device=dev)
-    per = N_SEQ // world
+    per = min(n_seq, N_SEQ) // world
     sl = slice(rank * per, (rank + 1) * per)
     q, k, v = (x[sl].contiguous() for x in proj)
     return q, k, v, bias, kmask[sl].contiguous(), dout[sl].contiguous()
@@ -232,7 +233,7 @@ def run_ours(args):
         # before any CUDA work: the pool is spawned, never forked
         cpu_line, _ = cpu_sample_line(2, 1)
 
-    q, k, v, bias, kmask, dout = make_inputs(torch, dev, rank, world)
+    q, k, v, bias, kmask, dout = make_inputs(torch, dev, rank, world, args.n_seq)
     n_local = q.shape[0]
     scale = HEAD_DIM ** -0.5
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
@@ -271,7 +272,7 @@ def run_ours(args):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
-    value = attn_flops(N_SEQ) / (ms * 1e-3) / 1e12
+    value = attn_flops(n_local * world) / (ms * 1e-3) / 1e12
 
     # per-kernel device time (the forward is one launch, the backward call four), L2 flushed
     def timed(fn, reps):
@@ -293,7 +294,8 @@ def run_ours(args):
     fwd_tf = 4.0 * n_local * HEADS * N_RES ** 2 * HEAD_DIM / (fwd_ms * 1e-3) / 1e12
     bwd_tf = 10.0 * n_local * HEADS * N_RES ** 2 * HEAD_DIM / (bwd_ms * 1e-3) / 1e12
 
-    e2e = run_e2e(args, torch, dist, b200, dev, world, q, k, v, bias, kmask, dout, scale)
+    e2e = None if args.no_e2e else run_e2e(args, torch, dist, b200, dev, world, q, k, v, bias,
+                                           kmask, dout, scale)
 
     fusions = None
     if not args.no_fusions:
@@ -306,7 +308,8 @@ def run_ours(args):
             'metric': METRIC, 'value': value, 'unit': 'TFLOP/s', 'n_gpus': world,
             'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': ms,
             'higher_is_better': True, 'scaling': 'strong', 'vs_baseline': None,
-            'dtype': 'bf16', 'data': 'synthetic', 'config': workload_config(world),
+            'dtype': 'bf16', 'data': 'synthetic',
+            'config': dict(workload_config(world), N_seq=n_local * world),
             'frac_of_bf16_peak': value / (peak * world),
             'roofline': {
                 'kernel': 'VoltaMmaBwd (attn_bwd_kernel + row_delta + dq_convert + fills)',
@@ -330,9 +333,93 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+PAIR = 768            # pair [768, 768, 128]
+C_Z = 128
+
+
 def bench_fusions(torch, b200, dev, rank, world, steps, warmup, flush, pk):
-    """Pair-stack fusion throughput; filled in with the fusion kernels."""
-    return None
+    """Pair-stack fusions on BASELINE configs[3] (pair [768, 768, 128] ~ N(0,1), M = 589,824
+    rows, W ~ N(0, 1/sqrt(128)), bf16), rows sharded across ranks. Algorithmic bytes: every
+    input read once and every output written once (bf16; float32 for x_cm and the LN
+    parameters), weights once. GB/s = bytes / device time (max over ranks)."""
+    import torch.distributed as dist
+    M_all = PAIR * PAIR
+    M = M_all // world
+    g = torch.Generator(device=dev)
+    g.manual_seed(1)
+    bf = torch.bfloat16
+
+    def rn(*shape, s=1.0, dt=bf):
+        return (torch.randn(*shape, generator=g, device=dev) * s).to(dt)
+
+    x = rn(M, C_Z)
+    ones = torch.ones(C_Z, device=dev)
+    zeros = torch.zeros(C_Z, device=dev)
+    keep1 = torch.ones(1, dtype=bf, device=dev)
+    mask = torch.ones(M, dtype=bf, device=dev)
+    w = C_Z ** -0.5
+    ops = []
+    for ci in (64, 128):
+        wpT, wgT = rn(2 * ci, C_Z, s=w), rn(2 * ci, C_Z, s=w)
+        bp, bg = torch.zeros(2 * ci, dtype=bf, device=dev), torch.ones(2 * ci, dtype=bf, device=dev)
+        ops.append(('ln_gated_dual_proj ci=%d' % ci,
+                    (lambda wpT=wpT, wgT=wgT, bp=bp, bg=bg: b200.volta_ln_gdp(
+                        x, ones, zeros, wpT, bp, wgT, bg, mask, eps=1e-5)),
+                    M * (C_Z * 2 + 2 + 2 * ci * 2) + 4 * ci * C_Z * 2, 2.0 * M * C_Z * 4 * ci))
+    for c in (64, 128):
+        x_cm = rn(c, M, dt=torch.float32)
+        woT, wgT = rn(C_Z, c, s=c ** -0.5), rn(C_Z, C_Z, s=w)
+        bo, bg = torch.zeros(C_Z, dtype=bf, device=dev), torch.zeros(C_Z, dtype=bf, device=dev)
+        lsc, lof = torch.ones(c, device=dev), torch.zeros(c, device=dev)
+        ops.append(('trimul_epilogue C=%d CA=O=128 add_input' % c,
+                    (lambda x_cm=x_cm, woT=woT, wgT=wgT, bo=bo, bg=bg, lsc=lsc, lof=lof:
+                     b200.volta_trimul_epilogue(x_cm, x, ones, zeros, lsc, lof, woT, bo, wgT, bg,
+                                                keep1, eps=1e-5, add_input=True,
+                                                has_keep=False)),
+                    M * (c * 4 + C_Z * 2 + C_Z * 2), 2.0 * M * C_Z * (c + C_Z)))
+    wT, wbT = rn(512, C_Z, s=w), rn(4, C_Z, s=w)
+    ops.append(('ln_projection n=512 heads=4',
+                lambda: b200.volta_ln_proj(x, ones, zeros, wT, wbT, keep1, eps=1e-5, n=512,
+                                           heads=4, has_keep=False),
+                M * (C_Z * 2 + 512 * 2 + 4 * 2), 2.0 * M * C_Z * 516))
+    o, woT, bo, res = rn(M, C_Z), rn(C_Z, C_Z, s=w), rn(C_Z, s=0.1), rn(M, C_Z)
+    ops.append(('output_projection 128->128 + residual',
+                lambda: b200.volta_out_proj(o, woT, bo, res, keep1, has_residual=True,
+                                            has_keep=False),
+                M * C_Z * 2 * 3, 2.0 * M * C_Z * C_Z))
+    w1T, b1 = rn(512, C_Z, s=w), rn(512, s=0.1)
+    w2T, b2 = rn(512 * C_Z, s=512 ** -0.5), rn(C_Z, s=0.1)
+    ops.append(('transition 128->512->128 add_input',
+                lambda: b200.volta_transition(x, ones, zeros, w1T, b1, w2T, b2, keep1, eps=1e-5,
+                                              add_input=True, has_keep=False),
+                M * C_Z * 2 * 2, 2.0 * M * C_Z * 512 * 2))
+    res_out = {}
+    for name, fn, nbytes, flops in ops:
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        evs = []
+        for _ in range(steps):
+            flush.fill_(3)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            evs.append((a, b))
+        torch.cuda.synchronize()
+        ms = sum(a.elapsed_time(b) for a, b in evs) / steps
+        t = torch.tensor([ms], device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        gbs = nbytes * world / (ms * 1e-3) / 1e9
+        tf = flops * world / (ms * 1e-3) / 1e12
+        res_out[name] = {'ms': ms, 'GB/s': gbs, 'frac_hbm': gbs / (pk['hbm_gbs'] * world),
+                         'TFLOP/s': tf, 'frac_bf16': tf / (pk['bf16_tflops'] * world),
+                         'bytes': nbytes * world, 'rows': M_all}
+    if b200.device_status() != 0:
+        raise RuntimeError('a fused kernel reported a wait that gave up')
+    return res_out
 
 
 def run_e2e(args, torch, dist, b200, dev, world, q, k, v, bias, kmask, dout, scale):
@@ -374,7 +461,7 @@ def run_e2e(args, torch, dist, b200, dev, world, q, k, v, bias, kmask, dout, sca
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
-    return {'value': attn_flops(N_SEQ) / (ms * 1e-3) / 1e12, 'unit': 'TFLOP/s',
+    return {'value': attn_flops(q.shape[0] * world) / (ms * 1e-3) / 1e12, 'unit': 'TFLOP/s',
             'ms_per_step': ms, 'h2d_bytes_per_step': h2d, 'd2h_bytes_per_step': d2h,
             'api': 'colabfold_legacy_kernels.b200.volta_mma / volta_mma_bwd (C ABI)'}
 
@@ -387,6 +474,9 @@ def main():
     ap.add_argument('--impl', choices=('ours', 'reference'), default='ours')
     ap.add_argument('--no-cpu', action='store_true', help='skip the cpu_baseline sample')
     ap.add_argument('--no-fusions', action='store_true', help='skip the pair-fusion lines')
+    ap.add_argument('--no-e2e', action='store_true', help='skip the host-buffer end-to-end leg')
+    ap.add_argument('--n-seq', type=int, default=N_SEQ,
+                    help='sequences of the attention workload (smaller for profiling runs)')
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == 'ours':
         args.warmup = 3

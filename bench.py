@@ -238,12 +238,10 @@ def run_ours(args):
     scale = HEAD_DIM ** -0.5
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
 
+    from colabfold_legacy_kernels import distributed as cd
+
     def step():
-        out, lse = b200.volta_mma(q, k, v, bias, kmask, scale=scale, block_q=64, block_k=32)
-        dq, dk, dv, dbias = b200.volta_mma_bwd(q, k, v, bias, kmask, out, dout, lse, scale=scale)
-        if world > 1:
-            dist.all_reduce(dbias)
-        return dbias
+        return cd.attention_fwd_bwd(q, k, v, bias, kmask, dout, scale=scale)[5]
 
     for _ in range(args.warmup):
         step()
@@ -302,6 +300,11 @@ def run_ours(args):
         fusions = bench_fusions(torch, b200, dev, rank, world, args.steps, args.warmup, flush,
                                 pk)
 
+    big = None
+    if not args.no_inference:
+        big = bench_inference(torch, b200, dev, rank, world, max(2, args.steps // 3), 2, flush,
+                              pk)
+
     if rank == 0:
         peak = pk['bf16_tflops']
         line = {
@@ -327,6 +330,8 @@ def run_ours(args):
             line['cpu_baseline'] = cpu_line
         if fusions is not None:
             line['fusions'] = fusions
+        if big is not None:
+            line['inference_2048'] = big
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -422,6 +427,82 @@ def bench_fusions(torch, b200, dev, rank, world, steps, warmup, flush, pk):
     return res_out
 
 
+BIG_RES, BIG_H = 2048, 4
+
+
+def bench_inference(torch, b200, dev, rank, world, steps, warmup, flush, pk):
+    """triangle attention forward only (want_lse off, one-element lse),
+    pair [2048, 2048, 128] ~ N(0,1), q/k/v = LN(z) W reshaped to H=4, d=32, bias [4, 2048, 2048]
+    ~ N(0,1), the last 5% of residues masked; rows sharded across ranks, then the output
+    all-gather. Reports the forward alone and forward + gather (device time, max over ranks)."""
+    import torch.distributed as dist
+    from colabfold_legacy_kernels import distributed as cd
+    S, H, d = BIG_RES, BIG_H, HEAD_DIM
+    a, b = cd.row_range(S, world, rank)
+    n = b - a
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    w = [(torch.randn(C_Z, H * d, generator=g, device=dev) * C_Z ** -0.5).to(torch.bfloat16)
+         for _ in range(3)]
+    bias = torch.randn(H, S, S, generator=g, device=dev).to(torch.bfloat16)
+    qkv = [torch.empty(n, H, S, d, dtype=torch.bfloat16, device=dev) for _ in range(3)]
+    for r0 in range(0, S, 256):
+        # rows [r0, r0+256) of the pair, generated in order so every rank sees the same pair
+        z = torch.randn(min(256, S - r0), S, C_Z, generator=g, device=dev)
+        z = torch.nn.functional.layer_norm(z, (C_Z,)).to(torch.bfloat16)
+        lo, hi = max(a, r0), min(b, r0 + z.shape[0])
+        if lo < hi:
+            zz = z[lo - r0:hi - r0]
+            for t, wt in zip(qkv, w):
+                t[lo - a:hi - a] = (zz @ wt).view(hi - lo, S, H, d).permute(0, 2, 1, 3)
+    kmask = torch.ones(n, S, dtype=torch.uint8, device=dev)
+    kmask[:, int(S * 0.95):] = 0
+    one = torch.empty(1, device=dev)
+    q, k, v = qkv
+    scale = d ** -0.5
+
+    def fwd():
+        return b200.volta_mma(q, k, v, bias, kmask, scale=scale, want_lse=False, lse=one)[0]
+
+    full = torch.empty(S, H, S, d, dtype=torch.bfloat16, device=dev) if world > 1 else None
+
+    def fwd_gather():
+        out = fwd()
+        if world > 1:
+            # rows are equal across ranks for S divisible by the world size
+            dist.all_gather_into_tensor(full, out)
+        return out
+
+    res = {}
+    for name, fn in (('fwd', fwd), ('fwd+all_gather', fwd_gather)):
+        if name != 'fwd' and world == 1:
+            continue
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        evs = []
+        for _ in range(steps):
+            flush.fill_(5)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            evs.append((e0, e1))
+        torch.cuda.synchronize()
+        ms = sum(x.elapsed_time(y) for x, y in evs) / steps
+        t = torch.tensor([ms], device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        tf = 4.0 * S * H * S * S * d / (ms * 1e-3) / 1e12
+        res[name] = {'ms': ms, 'TFLOP/s': tf, 'frac_bf16': tf / (pk['bf16_tflops'] * world)}
+    res['config'] = 'pair 2048x2048, H=4, d=32, fwd only (want_lse off), last 5%% masked, ' \
+                    'rows sharded over %d GPU(s)' % world
+    return res
+
+
 def run_e2e(args, torch, dist, b200, dev, world, q, k, v, bias, kmask, dout, scale):
     """The same step through the public API from pinned host buffers: inputs copied in and the
     gradients copied out inside the timed region."""
@@ -475,6 +556,8 @@ def main():
     ap.add_argument('--no-cpu', action='store_true', help='skip the cpu_baseline sample')
     ap.add_argument('--no-fusions', action='store_true', help='skip the pair-fusion lines')
     ap.add_argument('--no-e2e', action='store_true', help='skip the host-buffer end-to-end leg')
+    ap.add_argument('--no-inference', action='store_true',
+                    help='skip the large-protein inference leg (BASELINE configs[4])')
     ap.add_argument('--n-seq', type=int, default=N_SEQ,
                     help='sequences of the attention workload (smaller for profiling runs)')
     args = ap.parse_args()

@@ -8,15 +8,20 @@
 // carries dV through a masked key but dS does not). The design is this file's own:
 //
 //   * one CTA owns a 128-key tile of one (n, h): K and V stay in shared memory, dK and dV
-//     accumulate in tensor memory, so both come out bitwise deterministic;
-//   * it walks the queries 64 at a time; TMA brings Q, dout and the bias tile two stages deep;
-//   * S^T = K Q^T and dP^T = V dout^T are tcgen05 MMAs (M=128 keys, N=64 queries); thread t owns
-//     key t = TMEM lane t, forms P^T and dS^T in registers and writes them back over S^T and
-//     dP^T as 16-bit pairs, the A operands of dV += P^T dout and dK += dS^T q (A from TMEM);
-//   * dS is also stored MN-major in swizzled shared memory for dQ = dS k (M=64), whose fp32
-//     tile is added into a workspace accumulator with 16-byte vector atomics;
+//     accumulate in tensor memory over every query, so both come out bitwise deterministic;
+//   * warp roles: a TMA warp streams the 64-query steps (q, dout and the bias tile) two or
+//     three stages deep; an MMA warp issues every tcgen05 MMA; two softmax warpgroups take the
+//     steps alternately (ping-pong), each with its own S^T/dP^T columns in tensor memory and
+//     its own dS buffer, so one group's exponentials overlap the other group's MMAs;
+//   * S^T = K Q^T and dP^T = V dout^T (M=128 keys, N=64 queries); worker t owns key t = TMEM
+//     lane t, forms P^T and dS^T and writes them back over S^T and dP^T as 16-bit pairs, the
+//     A operands of dV += P^T dout and dK += dS^T q (A read from tensor memory);
+//   * dS also goes MN-major into swizzled shared memory for dQ = dS k (M=64), whose fp32 tile
+//     is added into the workspace accumulator with 16-byte vector atomics;
+//   * the bias is transposed once per call into the workspace as fp32 [H][Sk][Sq'] scaled by
+//     log2e, so a key's bias values arrive by TMA as one contiguous row (16-byte reads);
 //   * dBias gets dS by coalesced fp32 reductions (a warp covers 32 consecutive keys of a row).
-// Around it: a row-statistic kernel (delta), the zero fills, and the dQ conversion.
+// Around it: the row statistic (delta), the bias transpose, the zero fills, the dQ conversion.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -36,12 +41,10 @@ __device__ unsigned g_status;
 
 constexpr int kBK = 128;  // keys per CTA (= TMEM lanes)
 constexpr int kBQ = 64;   // queries per step
-constexpr int kThreads = 128;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kMaskedLogit = -1.0e4f;
 
 struct BwdParams {
-    const void* bias;
     const uint8_t* kmask;
     const float* lse;
     const float* delta;
@@ -64,318 +67,376 @@ struct BGeom {
     static constexpr int QATOM = kBQ * ROWB;  // one atom of a 64-row (query) tile
     static constexpr int KTILE = NA * KATOM;
     static constexpr int QTILE = NA * QATOM;
-    static constexpr int BIAS = kBQ * kBK * 2;  // two 64-key regions of 64 rows, 128B swizzle
-    static constexpr int DS = kBK * 128;        // dS, MN-major: 128 key rows of 64 queries
-    // TMEM columns: S^T [0,64), dP^T [64,128), dV, dK, dQ after them
-    static constexpr int DN = DP == 96 ? 96 : DP;
-    static constexpr uint32_t COLS_USED = 128 + 3 * DN;
-    static constexpr uint32_t TMEM_COLS = COLS_USED <= 256 ? 256 : 512;
+    static constexpr int BT = kBQ * kBK * 4;  // bias^T tile: two [128 keys][32 queries] fp32
+    static constexpr int DS = kBK * 128;      // dS, MN-major: 128 key rows of 64 queries
+    static constexpr int DN = DP;
+    static constexpr int NWG = DN <= 64 ? 2 : 1;  // softmax warpgroups (ping-pong)
+    static constexpr int NS = DN <= 64 ? 3 : 2;   // query-step stages
+    static constexpr int THREADS = NWG * 128 + 64;
+    // TMEM columns: group w's S^T at 128w, dP^T at 128w + 64; then dV, dK, one dQ per group
+    static constexpr int T_DV = NWG * 128;
+    static constexpr int T_DK = T_DV + DN;
+    static constexpr int T_DQ = T_DK + DN;
+    static constexpr int COLS = T_DQ + NWG * DN;
+    static constexpr uint32_t ALLOC = COLS <= 256 ? 256 : 512;
+    static_assert(COLS <= 512, "tensor memory");
 };
 
-template <int DP, bool BIAS_TMA>
+template <int DP>
 struct BSmem {
     using G = BGeom<DP>;
     static constexpr int K = 0;
     static constexpr int V = K + G::KTILE;
-    static constexpr int Q0 = V + G::KTILE;            // 2 stages
-    static constexpr int O0 = Q0 + 2 * G::QTILE;       // dout, 2 stages
-    static constexpr int DSB = O0 + 2 * G::QTILE;      // dS
-    static constexpr int B0 = DSB + G::DS;             // bias, 2 stages
-    static constexpr int STAT = B0 + (BIAS_TMA ? 2 * G::BIAS : 0);  // lse, delta: 2 stages
-    static constexpr int END = STAT + 2 * 2 * kBQ * 4;
+    static constexpr int STAGE = V + G::KTILE;               // NS x (Q, dO, bias^T)
+    static constexpr int STAGE_BYTES = 2 * G::QTILE + G::BT;
+    static constexpr int DSB = STAGE + G::NS * STAGE_BYTES;  // NWG dS buffers
+    static constexpr int STAT = DSB + G::NWG * G::DS;        // [NWG][2][lse, delta][64] fp32
+    static constexpr int END = STAT + G::NWG * 2 * 2 * kBQ * 4;
     static constexpr int BYTES = END + 1024;
+    static_assert(BYTES <= 227 * 1024, "shared memory");
 };
 
-template <typename T, int DP, bool BIAS_TMA, bool WANT_DBIAS>
-__global__ void __launch_bounds__(kThreads, 1)
+__device__ __forceinline__ void red_add_f32(float* p, float v) {
+    asm volatile("red.global.add.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
+}
+
+template <typename T, int DP, bool WANT_DBIAS>
+__global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                     const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
-                    const __grid_constant__ CUtensorMap tb, const BwdParams p) {
+                    const __grid_constant__ CUtensorMap tbt, const BwdParams p) {
     using G = BGeom<DP>;
-    using L = BSmem<DP, BIAS_TMA>;
+    using L = BSmem<DP>;
     using E = Elem<T>;
+    constexpr int NWG = G::NWG, NS = G::NS;
+    constexpr int MMA_WARP = 4 * NWG, TMA_WARP = MMA_WARP + 1;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    __shared__ uint64_t bar_kv, bar_full[2], bar_s, bar_mma;
+    __shared__ uint64_t kv_full, q_full[NS], q_empty[NS], s_full[2], p_ready[2], mma_done[2];
     __shared__ uint32_t tmem_base_sh;
     __shared__ int abort_flag;
 
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n = blockIdx.x, h = blockIdx.y, k0 = blockIdx.z * kBK;
-    const int key = k0 + tid;
     const int D = p.D;
     const int DN = (D + 15) & ~15;
     const int nqt = (p.Sq + kBQ - 1) / kBQ;
-    float* lse_s = reinterpret_cast<float*>(smem + L::STAT);          // [2][64]
-    float* delta_s = lse_s + 2 * kBQ;                                  // [2][64]
     const long long rowbase = ((long long)n * p.H + h) * p.Sq;
 
-    if (tid == 0) {
-        mbar_init(&bar_kv, 1);
-        mbar_init(&bar_full[0], 1);
-        mbar_init(&bar_full[1], 1);
-        mbar_init(&bar_s, 1);
-        mbar_init(&bar_mma, 1);
-        abort_flag = 0;
-        fence_mbar_init();
-    }
-    if (warp == 0) {
-        tmem_alloc(&tmem_base_sh, G::TMEM_COLS);
+    if (warp == MMA_WARP) {
+        if (lane == 0) {
+            mbar_init(&kv_full, 1);
+            for (int i = 0; i < NS; ++i) {
+                mbar_init(&q_full[i], 1);
+                mbar_init(&q_empty[i], 1);
+            }
+            for (int i = 0; i < 2; ++i) {
+                mbar_init(&s_full[i], 1);
+                mbar_init(&p_ready[i], 128);
+                mbar_init(&mma_done[i], 1);
+            }
+            abort_flag = 0;
+            fence_mbar_init();
+        }
+        __syncwarp();
+        tmem_alloc(&tmem_base_sh, G::ALLOC);
         tmem_relinquish();
     }
-    const auto load_stats = [&](int i) {
-        const int s = i & 1, q = i * kBQ + (tid & 63);
-        if (tid < 64) {
-            lse_s[s * kBQ + (tid & 63)] = q < p.Sq ? p.lse[rowbase + q] : INFINITY;
-        } else {
-            delta_s[s * kBQ + (tid & 63)] = q < p.Sq ? p.delta[rowbase + q] : 0.f;
-        }
-    };
-    load_stats(0);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tmem_base_sh;
-    const uint32_t t_st = tmem, t_dpt = tmem + 64;
-    const uint32_t t_dv = tmem + 128, t_dk = t_dv + G::DN, t_dq = t_dk + G::DN;
-    const uint32_t lane_base = tmem_lane_base(warp);
 
-    constexpr uint32_t STAGE_TX = 2 * G::QTILE + (BIAS_TMA ? G::BIAS : 0);
-    const auto load_tile = [&](int i) {
-        const int s = i & 1, q0 = i * kBQ;
-        mbar_arrive_expect_tx(&bar_full[s], STAGE_TX);
-        for (int a = 0; a < G::NA; ++a) {
-            tma_load_4d(smem + L::Q0 + s * G::QTILE + a * G::QATOM, &tq, &bar_full[s], a * G::AE,
-                        h, q0, n);
-            tma_load_4d(smem + L::O0 + s * G::QTILE + a * G::QATOM, &tdo, &bar_full[s],
-                        a * G::AE, h, q0, n);
+    if (warp == TMA_WARP) {
+        if (lane == 0) {
+            mbar_arrive_expect_tx(&kv_full, 2 * G::KTILE);
+            for (int a = 0; a < G::NA; ++a) {
+                tma_load_4d(smem + L::K + a * G::KATOM, &tk, &kv_full, a * G::AE, h, k0, n);
+                tma_load_4d(smem + L::V + a * G::KATOM, &tv, &kv_full, a * G::AE, h, k0, n);
+            }
+            for (int i = 0; i < nqt; ++i) {
+                const int s = i % NS, q0 = i * kBQ;
+                if (i >= NS) {
+                    mbar_wait(&q_empty[s], ((i - NS) / NS) & 1, &g_status, kStatusMmaWait,
+                              &abort_flag);
+                }
+                uint8_t* st = smem + L::STAGE + s * L::STAGE_BYTES;
+                mbar_arrive_expect_tx(&q_full[s], L::STAGE_BYTES);
+                for (int a = 0; a < G::NA; ++a) {
+                    tma_load_4d(st + a * G::QATOM, &tq, &q_full[s], a * G::AE, h, q0, n);
+                    tma_load_4d(st + G::QTILE + a * G::QATOM, &tdo, &q_full[s], a * G::AE, h, q0,
+                                n);
+                }
+                uint8_t* bt = st + 2 * G::QTILE;
+                tma_load_3d(bt, &tbt, &q_full[s], q0, k0, h);
+                tma_load_3d(bt + kBK * 128, &tbt, &q_full[s], q0 + 32, k0, h);
+            }
         }
-        if constexpr (BIAS_TMA) {
-            uint8_t* b = smem + L::B0 + s * G::BIAS;
-            tma_load_3d(b, &tb, &bar_full[s], k0, q0, h);
-            tma_load_3d(b + kBQ * 128, &tb, &bar_full[s], k0 + 64, q0, h);
-        }
-    };
-    if (tid == 0) {
-        mbar_arrive_expect_tx(&bar_kv, 2 * G::KTILE);
-        for (int a = 0; a < G::NA; ++a) {
-            tma_load_4d(smem + L::K + a * G::KATOM, &tk, &bar_kv, a * G::AE, h, k0, n);
-            tma_load_4d(smem + L::V + a * G::KATOM, &tv, &bar_kv, a * G::AE, h, k0, n);
-        }
-        load_tile(0);
-    }
-
-    const bool live = key < p.Sk && p.kmask[(long long)n * p.Sk + key] != 0;
-    const float qk_scale = p.scale * kLog2e;
-    const float masked = kMaskedLogit * kLog2e;
-    const uint32_t idesc_s = idesc_f16(E::kBf16, 128, kBQ, false, false);
-    const uint32_t idesc_acc = idesc_f16(E::kBf16, 128, DN, false, true);
-    const uint32_t idesc_dq = idesc_f16(E::kBf16, 64, DN, true, true);
-    const uint32_t k_base = smem_u32(smem + L::K), v_base = smem_u32(smem + L::V);
-    const uint32_t ds_base = smem_u32(smem + L::DSB);
-    const T* bias_g = reinterpret_cast<const T*>(p.bias) + (long long)h * p.Sq * p.Sk;
-
-    // dQ of step i: lanes 32w + r (r < 16) hold query row 16w + r (M=64 accumulator layout)
-    const auto flush_dq = [&](int i) {
-        const int q = i * kBQ + 16 * warp + lane;
-        for (int c = 0; c < DN; c += 16) {
-            uint32_t r[16];
-            tmem_ld16(t_dq + lane_base + c, r);
-            tmem_wait_ld();
-            if (lane < 16 && q < p.Sq) {
-                float* dst = p.dq_acc + (rowbase + q) * D + c;
+    } else if (warp == MMA_WARP) {
+        if (lane == 0) {
+            const uint32_t idesc_s = idesc_f16(E::kBf16, 128, kBQ, false, false);
+            const uint32_t idesc_acc = idesc_f16(E::kBf16, 128, DN, false, true);
+            const uint32_t idesc_dq = idesc_f16(E::kBf16, 64, DN, true, true);
+            const uint32_t k_base = smem_u32(smem + L::K), v_base = smem_u32(smem + L::V);
+            mbar_wait(&kv_full, 0, &g_status, kStatusTmaWait, &abort_flag);
+            // S^T and dP^T of step i into group (i % NWG)'s columns
+            const auto first_half = [&](int i) {
+                const int w = i % NWG, s = i % NS;
+                mbar_wait(&q_full[s], (i / NS) & 1, &g_status, kStatusTmaWait, &abort_flag);
+                if (i >= NWG) {
+                    mbar_wait(&mma_done[w], ((i - NWG) / NWG) & 1, &g_status, kStatusMmaWait,
+                              &abort_flag);
+                }
+                tc_fence_after();
+                const uint32_t st = smem_u32(smem + L::STAGE + s * L::STAGE_BYTES);
 #pragma unroll
-                for (int g = 0; g < 4; ++g) {
-                    if (c + 4 * g < D) {
-                        atomicAdd(reinterpret_cast<float4*>(dst + 4 * g),
-                                  make_float4(__uint_as_float(r[4 * g]) * p.scale,
-                                              __uint_as_float(r[4 * g + 1]) * p.scale,
-                                              __uint_as_float(r[4 * g + 2]) * p.scale,
-                                              __uint_as_float(r[4 * g + 3]) * p.scale));
+                for (int ks = 0; ks < DP / 16; ++ks) {
+                    const int a = (ks * 16) / G::AE, off = ((ks * 16) % G::AE) * 2;
+                    const uint64_t kd =
+                        smem_desc(k_base + a * G::KATOM + off, 16, 8 * G::ROWB, G::LAYOUT);
+                    const uint64_t vd =
+                        smem_desc(v_base + a * G::KATOM + off, 16, 8 * G::ROWB, G::LAYOUT);
+                    const uint64_t qd =
+                        smem_desc(st + a * G::QATOM + off, 16, 8 * G::ROWB, G::LAYOUT);
+                    const uint64_t od =
+                        smem_desc(st + G::QTILE + a * G::QATOM + off, 16, 8 * G::ROWB, G::LAYOUT);
+                    mma_ss(tmem + 128 * w, kd, qd, idesc_s, ks > 0);
+                    mma_ss(tmem + 128 * w + 64, vd, od, idesc_s, ks > 0);
+                }
+                mma_commit(&s_full[w]);
+            };
+            // dV, dK and dQ of step j once its group has written P^T, dS^T and dS
+            const auto second_half = [&](int j) {
+                const int w = j % NWG, s = j % NS;
+                mbar_wait(&p_ready[w], (j / NWG) & 1, &g_status, kStatusSyncWait, &abort_flag);
+                tc_fence_after();
+                const uint32_t st = smem_u32(smem + L::STAGE + s * L::STAGE_BYTES);
+#pragma unroll
+                for (int ks = 0; ks < kBQ / 16; ++ks) {
+                    const uint64_t od = smem_desc(st + G::QTILE + ks * 16 * G::ROWB, G::QATOM,
+                                                  8 * G::ROWB, G::LAYOUT);
+                    const uint64_t qd =
+                        smem_desc(st + ks * 16 * G::ROWB, G::QATOM, 8 * G::ROWB, G::LAYOUT);
+                    mma_ts(tmem + G::T_DV, tmem + 128 * w + ks * 8, od, idesc_acc,
+                           (j > 0 || ks > 0) ? 1u : 0u);
+                    mma_ts(tmem + G::T_DK, tmem + 128 * w + 64 + ks * 8, qd, idesc_acc,
+                           (j > 0 || ks > 0) ? 1u : 0u);
+                }
+                const uint32_t ds_base = smem_u32(smem + L::DSB + w * G::DS);
+#pragma unroll
+                for (int ks = 0; ks < kBK / 16; ++ks) {
+                    const uint64_t ad =
+                        smem_desc(ds_base + ks * 16 * 128, G::DS, 1024, kSwizzle128B);
+                    const uint64_t bd =
+                        smem_desc(k_base + ks * 16 * G::ROWB, G::KATOM, 8 * G::ROWB, G::LAYOUT);
+                    mma_ss(tmem + G::T_DQ + w * G::DN, ad, bd, idesc_dq, ks > 0 ? 1u : 0u);
+                }
+                mma_commit(&mma_done[w]);
+                mma_commit(&q_empty[s]);
+            };
+            for (int i = 0; i <= nqt; ++i) {
+                if constexpr (NWG == 2) {
+                    // the next step's S^T and dP^T go ahead of this step's accumulations
+                    if (i < nqt) {
+                        first_half(i);
+                    }
+                    if (i >= 1) {
+                        second_half(i - 1);
+                    }
+                } else {
+                    // one group: its columns are free only after the previous step's MMAs
+                    if (i >= 1) {
+                        second_half(i - 1);
+                    }
+                    if (i < nqt) {
+                        first_half(i);
                     }
                 }
             }
         }
-    };
-
-    for (int i = 0; i < nqt; ++i) {
-        const int s = i & 1, q0 = i * kBQ;
-        if (tid == 0) {
-            if (i > 0) {
-                mbar_wait(&bar_mma, (i - 1) & 1, &g_status, kStatusMmaWait, &abort_flag);
-            }
-            if (i + 1 < nqt) {
-                load_tile(i + 1);
-            }
-            if (i == 0) {
-                mbar_wait(&bar_kv, 0, &g_status, kStatusTmaWait, &abort_flag);
-            }
-            mbar_wait(&bar_full[s], (i >> 1) & 1, &g_status, kStatusTmaWait, &abort_flag);
-            tc_fence_after();
-            const uint32_t q_base = smem_u32(smem + L::Q0 + s * G::QTILE);
-            const uint32_t o_base = smem_u32(smem + L::O0 + s * G::QTILE);
-#pragma unroll
-            for (int ks = 0; ks < DP / 16; ++ks) {
-                const int a = (ks * 16) / G::AE, off = ((ks * 16) % G::AE) * 2;
-                const uint64_t kd = smem_desc(k_base + a * G::KATOM + off, 16, 8 * G::ROWB, G::LAYOUT);
-                const uint64_t vd = smem_desc(v_base + a * G::KATOM + off, 16, 8 * G::ROWB, G::LAYOUT);
-                const uint64_t qd = smem_desc(q_base + a * G::QATOM + off, 16, 8 * G::ROWB, G::LAYOUT);
-                const uint64_t od = smem_desc(o_base + a * G::QATOM + off, 16, 8 * G::ROWB, G::LAYOUT);
-                mma_ss(t_st, kd, qd, idesc_s, ks > 0);
-                mma_ss(t_dpt, vd, od, idesc_s, ks > 0);
-            }
-            mma_commit(&bar_s);
-        }
-        __syncwarp();
-        if (i > 0) {
-            // dQ of the previous step, before this step's dQ MMA reuses its columns
-            mbar_wait(&bar_mma, (i - 1) & 1, &g_status, kStatusMmaWait, &abort_flag);
-            tc_fence_after();
-            flush_dq(i - 1);
-        }
-        if (i + 1 < nqt) {
-            load_stats(i + 1);  // read after this step's barrier
-        }
-        mbar_wait(&bar_s, i & 1, &g_status, kStatusMmaWait, &abort_flag);
-        tc_fence_after();
-
-        float st[kBQ], dpt[kBQ];
-        {
-            uint32_t r[32];
-            tmem_ld32(t_st + lane_base, r);
-            tmem_wait_ld();
-#pragma unroll
-            for (int j = 0; j < 32; ++j) st[j] = __uint_as_float(r[j]);
-            tmem_ld32(t_st + lane_base + 32, r);
-            tmem_wait_ld();
-#pragma unroll
-            for (int j = 0; j < 32; ++j) st[32 + j] = __uint_as_float(r[j]);
-            tmem_ld32(t_dpt + lane_base, r);
-            tmem_wait_ld();
-#pragma unroll
-            for (int j = 0; j < 32; ++j) dpt[j] = __uint_as_float(r[j]);
-            tmem_ld32(t_dpt + lane_base + 32, r);
-            tmem_wait_ld();
-#pragma unroll
-            for (int j = 0; j < 32; ++j) dpt[32 + j] = __uint_as_float(r[j]);
-        }
-        const float* ls = lse_s + s * kBQ;
-        const float* dl = delta_s + s * kBQ;
-        const uint8_t* bstage = smem + L::B0 + s * G::BIAS;
-        const int kk = tid & 63;
-        const uint8_t* bregion = bstage + (tid >> 6) * (kBQ * 128);
-        uint8_t* ds_row = smem + L::DSB + tid * 128;
+    } else {
+        // softmax warpgroups: worker (wg, t) owns key k0 + t = TMEM lane t
+        const int wg = warp >> 2, t = ((warp & 3) << 5) | lane;
+        const int key = k0 + t;
+        const uint32_t lane_base = tmem_lane_base(warp);
+        const bool live = key < p.Sk && p.kmask[(long long)n * p.Sk + key] != 0;
+        const bool warp_live = __all_sync(0xffffffffu, live);
+        const float qk_scale = p.scale * kLog2e;
+        const float masked = kMaskedLogit * kLog2e;
+        float* stat = reinterpret_cast<float*>(smem + L::STAT) + wg * (2 * 2 * kBQ);
         float* dbias_col = p.dbias + (long long)h * p.Sq * p.Sk + key;
+        uint8_t* ds_row = smem + L::DSB + wg * G::DS + t * 128;
+        const uint32_t t_dq = tmem + G::T_DQ + wg * G::DN;
+        const uint32_t t_st = tmem + 128 * wg + lane_base, t_dp = t_st + 64;
 
+        // dQ of a step: lanes 32w + r (r < 16) hold query row 16w + r (M=64 layout)
+        const auto flush_dq = [&](int i) {
+            const int q = i * kBQ + 16 * (warp & 3) + lane;
+            for (int c = 0; c < DN; c += 16) {
+                uint32_t r[16];
+                tmem_ld16(t_dq + lane_base + c, r);
+                tmem_wait_ld();
+                if (lane < 16 && q < p.Sq) {
+                    float* dst = p.dq_acc + (rowbase + q) * D + c;
 #pragma unroll
-        for (int c = 0; c < kBQ / 16; ++c) {
-            uint32_t pw[8], dw[8];
-#pragma unroll
-            for (int jj = 0; jj < 16; jj += 2) {
-                float pv[2], dv[2];
-#pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                    const int j = 16 * c + jj + e;
-                    float b;
-                    if constexpr (BIAS_TMA) {
-                        const int phys = (kk >> 3) ^ (j & 7);
-                        b = E::to_f(*reinterpret_cast<const T*>(bregion + j * 128 + (phys << 4) +
-                                                                 (kk & 7) * 2));
-                    } else {
-                        const int q = q0 + j;
-                        b = (q < p.Sq && key < p.Sk) ? E::to_f(bias_g[(long long)q * p.Sk + key])
-                                                     : 0.f;
-                    }
-                    const float l2 = live ? fmaf(st[j], qk_scale, b * kLog2e) : masked;
-                    const float pp = ex2(l2 - ls[j]);
-                    const float g = live ? pp * (dpt[j] - dl[j]) : 0.f;
-                    pv[e] = pp;
-                    dv[e] = g;
-                    if constexpr (WANT_DBIAS) {
-                        if (g != 0.f) {
-                            atomicAdd(dbias_col + (long long)(q0 + j) * p.Sk, g);
+                    for (int g = 0; g < 4; ++g) {
+                        if (c + 4 * g < D) {
+                            atomicAdd(reinterpret_cast<float4*>(dst + 4 * g),
+                                      make_float4(__uint_as_float(r[4 * g]) * p.scale,
+                                                  __uint_as_float(r[4 * g + 1]) * p.scale,
+                                                  __uint_as_float(r[4 * g + 2]) * p.scale,
+                                                  __uint_as_float(r[4 * g + 3]) * p.scale));
                         }
                     }
                 }
-                pw[jj >> 1] = E::pack(pv[0], pv[1]);
-                dw[jj >> 1] = E::pack(dv[0], dv[1]);
             }
-            tmem_st8(t_st + lane_base + 8 * c, pw);
-            tmem_st8(t_dpt + lane_base + 8 * c, dw);
-            // dS row (this key): queries 16c..16c+15 are chunks 2c, 2c+1 of the 128-byte row
-            *reinterpret_cast<uint4*>(ds_row + (((2 * c) ^ (tid & 7)) << 4)) =
-                make_uint4(dw[0], dw[1], dw[2], dw[3]);
-            *reinterpret_cast<uint4*>(ds_row + (((2 * c + 1) ^ (tid & 7)) << 4)) =
-                make_uint4(dw[4], dw[5], dw[6], dw[7]);
-        }
-        tmem_wait_st();
-        fence_async_smem();
-        tc_fence_before();
-        __syncthreads();
+        };
 
-        if (tid == 0) {
-            tc_fence_after();
-            const uint32_t q_base = smem_u32(smem + L::Q0 + s * G::QTILE);
-            const uint32_t o_base = smem_u32(smem + L::O0 + s * G::QTILE);
+        // one 32-query half of a step: P^T, dS^T (TMEM), dS (shared), dBias (global)
+        const auto half_step = [&](auto fast, const uint8_t* brow, const float* lsh,
+                                   const float* dlh, int half, int q0, int jn) {
+            uint32_t sr[32], dr[32];
+            tmem_ld32(t_st + 32 * half, sr);
+            tmem_ld32(t_dp + 32 * half, dr);
+            tmem_wait_ld();
+            uint32_t pw[16], dw[16];
+            float* drow = dbias_col + (long long)(q0 + 32 * half) * p.Sk;
 #pragma unroll
-            for (int ks = 0; ks < kBQ / 16; ++ks) {
-                const uint64_t od =
-                    smem_desc(o_base + ks * 16 * G::ROWB, G::QATOM, 8 * G::ROWB, G::LAYOUT);
-                const uint64_t qd =
-                    smem_desc(q_base + ks * 16 * G::ROWB, G::QATOM, 8 * G::ROWB, G::LAYOUT);
-                mma_ts(t_dv, t_st + ks * 8, od, idesc_acc, (i > 0 || ks > 0) ? 1u : 0u);
-                mma_ts(t_dk, t_dpt + ks * 8, qd, idesc_acc, (i > 0 || ks > 0) ? 1u : 0u);
-            }
+            for (int c = 0; c < 8; ++c) {
+                const float4 b4 = *reinterpret_cast<const float4*>(brow + ((c ^ (t & 7)) << 4));
+                const float4 l4 = *reinterpret_cast<const float4*>(lsh + 4 * c);
+                const float4 d4 = *reinterpret_cast<const float4*>(dlh + 4 * c);
+                const float bb[4] = {b4.x, b4.y, b4.z, b4.w};
+                const float ll[4] = {l4.x, l4.y, l4.z, l4.w};
+                const float dd[4] = {d4.x, d4.y, d4.z, d4.w};
+                float pv[4], gv[4];
 #pragma unroll
-            for (int ks = 0; ks < kBK / 16; ++ks) {
-                const uint64_t ad =
-                    smem_desc(ds_base + ks * 16 * 128, G::DS, 1024, kSwizzle128B);
-                const uint64_t bd =
-                    smem_desc(k_base + ks * 16 * G::ROWB, G::KATOM, 8 * G::ROWB, G::LAYOUT);
-                mma_ss(t_dq, ad, bd, idesc_dq, ks > 0 ? 1u : 0u);
-            }
-            mma_commit(&bar_mma);
-        }
-    }
-
-    __syncwarp();
-    mbar_wait(&bar_mma, (nqt - 1) & 1, &g_status, kStatusMmaWait, &abort_flag);
-    tc_fence_after();
-    flush_dq(nqt - 1);
-    // dK (scaled) and dV rows of this key tile
-    T* dk_row = reinterpret_cast<T*>(p.dk) + (rowbase / p.Sq * p.Sk + key) * (long long)D;
-    T* dv_row = reinterpret_cast<T*>(p.dv) + (rowbase / p.Sq * p.Sk + key) * (long long)D;
-    for (int c = 0; c < DN; c += 16) {
-        uint32_t rk[16], rv[16];
-        tmem_ld16(t_dk + lane_base + c, rk);
-        tmem_ld16(t_dv + lane_base + c, rv);
-        tmem_wait_ld();
-        if (key < p.Sk) {
-#pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                const int c8 = c + 8 * half;
-                if (c8 < D) {
-                    uint4 wk, wv;
-                    uint32_t* pk = &wk.x;
-                    uint32_t* pv = &wv.x;
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        pk[e] = E::pack(__uint_as_float(rk[8 * half + 2 * e]) * p.scale,
-                                        __uint_as_float(rk[8 * half + 2 * e + 1]) * p.scale);
-                        pv[e] = E::pack(__uint_as_float(rv[8 * half + 2 * e]),
-                                        __uint_as_float(rv[8 * half + 2 * e + 1]));
+                for (int e = 0; e < 4; ++e) {
+                    const int j = 4 * c + e;
+                    if constexpr (decltype(fast)::value) {
+                        pv[e] = ex2(fmaf(__uint_as_float(sr[j]), qk_scale, bb[e]) - ll[e]);
+                        gv[e] = pv[e] * (__uint_as_float(dr[j]) - dd[e]);
+                    } else {
+                        const float l2 =
+                            live ? fmaf(__uint_as_float(sr[j]), qk_scale, bb[e]) : masked;
+                        pv[e] = ex2(l2 - ll[e]);
+                        gv[e] = live ? pv[e] * (__uint_as_float(dr[j]) - dd[e]) : 0.f;
                     }
-                    *reinterpret_cast<uint4*>(dk_row + c8) = wk;
-                    *reinterpret_cast<uint4*>(dv_row + c8) = wv;
+                }
+                pw[2 * c] = E::pack(pv[0], pv[1]);
+                pw[2 * c + 1] = E::pack(pv[2], pv[3]);
+                dw[2 * c] = E::pack(gv[0], gv[1]);
+                dw[2 * c + 1] = E::pack(gv[2], gv[3]);
+                if constexpr (WANT_DBIAS) {
+                    if (key < p.Sk) {
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            if (4 * c + e < jn) {
+                                red_add_f32(drow + (long long)(4 * c + e) * p.Sk, gv[e]);
+                            }
+                        }
+                    }
+                }
+            }
+            tmem_st16(t_st + 16 * half, pw);
+            tmem_st16(t_dp + 16 * half, dw);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const int chunk = 4 * half + c;
+                *reinterpret_cast<uint4*>(ds_row + ((chunk ^ (t & 7)) << 4)) =
+                    make_uint4(dw[4 * c], dw[4 * c + 1], dw[4 * c + 2], dw[4 * c + 3]);
+            }
+        };
+
+        int k = 0;
+        for (int i = wg; i < nqt; i += NWG, ++k) {
+            const int s = i % NS, q0 = i * kBQ, b = k & 1;
+            // this step's row statistics into the group's buffer b
+            float* ls = stat + b * (2 * kBQ);
+            float* dl = ls + kBQ;
+            {
+                const int q = q0 + (t & 63);
+                if (t < 64) {
+                    ls[t] = q < p.Sq ? p.lse[rowbase + q] : INFINITY;
+                } else {
+                    dl[t - 64] = q < p.Sq ? p.delta[rowbase + q] : 0.f;
+                }
+            }
+            named_sync(2 + wg, 128);
+            if (k >= 1) {
+                // this group's previous step: dQ out of tensor memory before it is reused
+                mbar_wait(&mma_done[wg], (k - 1) & 1, &g_status, kStatusMmaWait, &abort_flag);
+                tc_fence_after();
+                flush_dq(i - NWG);
+            }
+            mbar_wait(&q_full[s], (i / NS) & 1, &g_status, kStatusTmaWait, &abort_flag);
+            mbar_wait(&s_full[wg], k & 1, &g_status, kStatusMmaWait, &abort_flag);
+            tc_fence_after();
+            const uint8_t* bt = smem + L::STAGE + s * L::STAGE_BYTES + 2 * G::QTILE;
+            const int nq = min(kBQ, p.Sq - q0);
+#pragma unroll 1
+            for (int half = 0; half < 2; ++half) {
+                const uint8_t* brow = bt + half * (kBK * 128) + t * 128;
+                const int jn = min(32, nq - 32 * half);
+                if (warp_live) {
+                    half_step(std::true_type{}, brow, ls + 32 * half, dl + 32 * half, half, q0, jn);
+                } else {
+                    half_step(std::false_type{}, brow, ls + 32 * half, dl + 32 * half, half, q0,
+                              jn);
+                }
+            }
+            tmem_wait_st();
+            fence_async_smem();
+            tc_fence_before();
+            mbar_arrive(&p_ready[wg]);
+        }
+        if (k >= 1) {
+            mbar_wait(&mma_done[wg], (k - 1) & 1, &g_status, kStatusMmaWait, &abort_flag);
+            tc_fence_after();
+            flush_dq(wg + (k - 1) * NWG);
+        }
+        // dK (scaled) and dV once the last step's accumulations are done
+        const int last = nqt - 1;
+        mbar_wait(&mma_done[last % NWG], (last / NWG) & 1, &g_status, kStatusMmaWait,
+                  &abort_flag);
+        tc_fence_after();
+        const long long krow = ((long long)n * p.H + h) * p.Sk + key;
+        for (int which = 0; which < 2; ++which) {
+            if (NWG == 2 && which != wg) {
+                continue;
+            }
+            const uint32_t acc = tmem + (which == 0 ? G::T_DK : G::T_DV) + lane_base;
+            T* dst = reinterpret_cast<T*>(which == 0 ? p.dk : p.dv) + krow * D;
+            const float mul = which == 0 ? p.scale : 1.f;
+            for (int c = 0; c < DN; c += 16) {
+                uint32_t r[16];
+                tmem_ld16(acc + c, r);
+                tmem_wait_ld();
+                if (key < p.Sk) {
+#pragma unroll
+                    for (int hh = 0; hh < 2; ++hh) {
+                        const int c8 = c + 8 * hh;
+                        if (c8 < D) {
+                            uint4 w;
+                            uint32_t* pw = &w.x;
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                pw[e] = E::pack(__uint_as_float(r[8 * hh + 2 * e]) * mul,
+                                                __uint_as_float(r[8 * hh + 2 * e + 1]) * mul);
+                            }
+                            *reinterpret_cast<uint4*>(dst + c8) = w;
+                        }
+                    }
                 }
             }
         }
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) {
-        tmem_dealloc(tmem, G::TMEM_COLS);
+    if (warp == MMA_WARP) {
+        tc_fence_after();
+        tmem_dealloc(tmem, G::ALLOC);
     }
 }
 
@@ -402,6 +463,28 @@ __global__ void row_delta_kernel(const T* __restrict__ out, const T* __restrict_
         }
     }
     delta[r] = s;
+}
+
+// bt[h][k][q] = log2e * bias[h][q][k] in fp32, queries padded to Sqp with zeros; 32x32 tiles
+template <typename T>
+__global__ void bias_transpose_kernel(const T* __restrict__ bias, float* __restrict__ bt, int Sq,
+                                      int Sk, int Sqp) {
+    __shared__ float tile[32][33];
+    const int h = blockIdx.z, q0 = blockIdx.x * 32, k0 = blockIdx.y * 32;
+    const T* src = bias + (long long)h * Sq * Sk;
+    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+        const int q = q0 + r, k = k0 + threadIdx.x;
+        tile[r][threadIdx.x] =
+            (q < Sq && k < Sk) ? Elem<T>::to_f(src[(long long)q * Sk + k]) : 0.f;
+    }
+    __syncthreads();
+    float* dst = bt + (long long)h * Sk * Sqp;
+    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+        const int k = k0 + r, q = q0 + threadIdx.x;
+        if (k < Sk && q < Sqp) {
+            dst[(long long)k * Sqp + q] = tile[threadIdx.x][r] * kLog2e;
+        }
+    }
 }
 
 // dq = dq_acc rounded to 16 bits, 8 elements a thread
@@ -434,10 +517,25 @@ bool aligned16(const void* p) {
     return (reinterpret_cast<uintptr_t>(p) & 15) == 0;
 }
 
-template <typename T, int DP, bool BT, bool DB>
+// Workspace: dQ accumulator | row statistic | bias^T (fp32, queries padded to a multiple of 4),
+// each 256-byte aligned
+struct Workspace {
+    size_t dq, delta, bt, total;
+    static Workspace of(size_t N, size_t H, size_t Sq, size_t Sk, size_t D) {
+        Workspace w;
+        const size_t rows = N * H * Sq, sqp = (Sq + 3) & ~size_t(3);
+        w.dq = 0;
+        w.delta = align256(rows * D * sizeof(float));
+        w.bt = w.delta + align256(rows * sizeof(float));
+        w.total = w.bt + align256(H * Sk * sqp * sizeof(float));
+        return w;
+    }
+};
+
+template <typename T, int DP, bool DB>
 cudaError_t launch_main(cudaStream_t stream, const CUtensorMap* maps, const BwdParams& p) {
-    auto kern = attn_bwd_kernel<T, DP, BT, DB>;
-    const int smem = BSmem<DP, BT>::BYTES;
+    auto kern = attn_bwd_kernel<T, DP, DB>;
+    const int smem = BSmem<DP>::BYTES;
     static bool attr_done[kMaxDevices] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -450,33 +548,26 @@ cudaError_t launch_main(cudaStream_t stream, const CUtensorMap* maps, const BwdP
         attr_done[dev] = true;
     }
     const dim3 grid(p.N, p.H, (p.Sk + kBK - 1) / kBK);
-    kern<<<grid, kThreads, smem, stream>>>(maps[0], maps[1], maps[2], maps[3], maps[4], p);
+    kern<<<grid, BGeom<DP>::THREADS, smem, stream>>>(maps[0], maps[1], maps[2], maps[3], maps[4],
+                                                     p);
     return cudaGetLastError();
 }
 
 template <typename T, int DP>
-cudaError_t launch_dp(cudaStream_t stream, const CUtensorMap* maps, const BwdParams& p, bool bt,
-                      bool db) {
-    if (bt) {
-        return db ? launch_main<T, DP, true, true>(stream, maps, p)
-                  : launch_main<T, DP, true, false>(stream, maps, p);
-    }
-    return db ? launch_main<T, DP, false, true>(stream, maps, p)
-              : launch_main<T, DP, false, false>(stream, maps, p);
+cudaError_t launch_dp(cudaStream_t stream, const CUtensorMap* maps, const BwdParams& p, bool db) {
+    return db ? launch_main<T, DP, true>(stream, maps, p)
+              : launch_main<T, DP, false>(stream, maps, p);
 }
 
 template <typename T>
 cudaError_t run_backward(cudaStream_t stream, const CUtensorMap* maps, const BwdParams& p,
-                         const void* out, const void* dout, float* delta, void* dq,
-                         bool bias_tma, bool want_dbias) {
+                         const void* bias, float* bt, int Sqp, const void* out, const void* dout,
+                         float* delta, void* dq, bool want_dbias) {
     const long long rows = (long long)p.N * p.H * p.Sq;
     cudaError_t e;
     if ((e = cudaMemsetAsync(p.dbias, 0, sizeof(float) * (size_t)p.H * p.Sq * p.Sk, stream)) !=
         cudaSuccess) {
         return e;
-    }
-    if (rows == 0) {
-        return cudaSuccess;
     }
     if ((e = cudaMemsetAsync(p.dq_acc, 0, sizeof(float) * (size_t)rows * p.D, stream)) !=
         cudaSuccess) {
@@ -484,18 +575,19 @@ cudaError_t run_backward(cudaStream_t stream, const CUtensorMap* maps, const Bwd
     }
     row_delta_kernel<T><<<(unsigned)((rows + 255) / 256), 256, 0, stream>>>(
         static_cast<const T*>(out), static_cast<const T*>(dout), delta, rows, p.D);
+    const dim3 tgrid((Sqp + 31) / 32, (p.Sk + 31) / 32, p.H);
+    bias_transpose_kernel<T><<<tgrid, dim3(32, 8), 0, stream>>>(static_cast<const T*>(bias), bt,
+                                                                 p.Sq, p.Sk, Sqp);
     if ((e = cudaGetLastError()) != cudaSuccess) {
         return e;
     }
-    if (p.Sk > 0) {
-        const int DP = padded_dim(p.D);
-        e = DP == 16   ? launch_dp<T, 16>(stream, maps, p, bias_tma, want_dbias)
-            : DP == 32 ? launch_dp<T, 32>(stream, maps, p, bias_tma, want_dbias)
-            : DP == 64 ? launch_dp<T, 64>(stream, maps, p, bias_tma, want_dbias)
-                       : launch_dp<T, 96>(stream, maps, p, bias_tma, want_dbias);
-        if (e != cudaSuccess) {
-            return e;
-        }
+    const int DP = padded_dim(p.D);
+    e = DP == 16   ? launch_dp<T, 16>(stream, maps, p, want_dbias)
+        : DP == 32 ? launch_dp<T, 32>(stream, maps, p, want_dbias)
+        : DP == 64 ? launch_dp<T, 64>(stream, maps, p, want_dbias)
+                   : launch_dp<T, 96>(stream, maps, p, want_dbias);
+    if (e != cudaSuccess) {
+        return e;
     }
     const long long n8 = rows * p.D / 8;
     dq_convert_kernel<T><<<(unsigned)std::min<long long>((n8 + 255) / 256, 148 * 16), 256, 0,
@@ -522,8 +614,7 @@ extern "C" int cflk_volta_mma_bwd_workspace_size(int64_t N, int64_t H, int64_t S
     if (N < 0 || H < 0 || Sq < 0 || Sk < 0 || D < 0 || bytes == nullptr) {
         return fail(kInvalidArgument, "volta_mma_bwd: bad sizes");
     }
-    const size_t rows = (size_t)N * H * Sq;
-    *bytes = align256(rows * D * sizeof(float)) + align256(rows * sizeof(float));
+    *bytes = Workspace::of(N, H, Sq, Sk, D).total;
     return kOk;
 }
 
@@ -544,9 +635,8 @@ extern "C" int cflk_volta_mma_bwd(void* stream_, int dtype, const void* q, const
     if (D != 8 && D != 16 && D != 24 && D != 32 && D != 48 && D != 64 && D != 96) {
         return fail(kInvalidArgument, "volta_mma_bwd: unsupported head dim");
     }
-    size_t need = 0;
-    cflk_volta_mma_bwd_workspace_size(N, H, Sq, Sk, D, &need);
-    if (workspace_bytes < need || (need > 0 && workspace == nullptr) ||
+    const Workspace ws = Workspace::of(N, H, Sq, Sk, D);
+    if (workspace_bytes < ws.total || (ws.total > 0 && workspace == nullptr) ||
         (reinterpret_cast<uintptr_t>(workspace) & 255) != 0) {
         return fail(kInternal, "volta_mma_bwd: no scratch for the dQ accumulator");
     }
@@ -555,9 +645,11 @@ extern "C" int cflk_volta_mma_bwd(void* stream_, int dtype, const void* q, const
         return fail(kInvalidArgument, "volta_mma_bwd: buffers must be 16-byte aligned");
     }
     const size_t rows = (size_t)N * H * Sq;
-    float* dq_acc = static_cast<float*>(workspace);
-    float* delta = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
-                                            align256(rows * D * sizeof(float)));
+    uint8_t* wsb = static_cast<uint8_t*>(workspace);
+    float* dq_acc = reinterpret_cast<float*>(wsb + ws.dq);
+    float* delta = reinterpret_cast<float*>(wsb + ws.delta);
+    float* bt = reinterpret_cast<float*>(wsb + ws.bt);
+    const int Sqp = (int)((Sq + 3) & ~int64_t(3));
     if (H == 0 || Sq == 0 || Sk == 0 || N == 0) {
         // nothing to differentiate: zero what exists
         if (H > 0 && Sq > 0 && Sk > 0) {
@@ -588,25 +680,19 @@ extern "C" int cflk_volta_mma_bwd(void* stream_, int dtype, const void* q, const
         const uint32_t boxq[4] = {(uint32_t)AE, 1, (uint32_t)kBQ, 1};
         const uint32_t boxk[4] = {(uint32_t)AE, 1, (uint32_t)kBK, 1};
         const CUtensorMapSwizzle sw = swizzle_for_row(AE * 2);
+        const uint64_t dbt[3] = {(uint64_t)Sqp, (uint64_t)Sk, (uint64_t)H};
+        const uint64_t sbt[2] = {(uint64_t)Sqp, (uint64_t)Sk * (uint64_t)Sqp};
+        const uint32_t boxbt[3] = {32, (uint32_t)kBK, 1};
         if (!encode_tiled(&maps[0], tdt, 2, 4, q, dq4, sq4, boxq, sw) ||
             !encode_tiled(&maps[1], tdt, 2, 4, k, dk4, sk4, boxk, sw) ||
             !encode_tiled(&maps[2], tdt, 2, 4, v, dk4, sk4, boxk, sw) ||
-            !encode_tiled(&maps[3], tdt, 2, 4, dout, dq4, sq4, boxq, sw)) {
+            !encode_tiled(&maps[3], tdt, 2, 4, dout, dq4, sq4, boxq, sw) ||
+            !encode_tiled(&maps[4], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, 3, bt, dbt, sbt, boxbt,
+                          CU_TENSOR_MAP_SWIZZLE_128B)) {
             return fail(kInvalidArgument, "volta_mma_bwd: TMA descriptor rejected");
         }
     }
-    const bool bias_tma = Sk % 8 == 0 && aligned16(bias);
-    maps[4] = maps[0];
-    if (bias_tma) {
-        const uint64_t db[3] = {(uint64_t)Sk, (uint64_t)Sq, (uint64_t)H};
-        const uint64_t sb[2] = {(uint64_t)Sk, (uint64_t)(Sq * Sk)};
-        const uint32_t box[3] = {64, (uint32_t)kBQ, 1};
-        if (!encode_tiled(&maps[4], tdt, 2, 3, bias, db, sb, box, CU_TENSOR_MAP_SWIZZLE_128B)) {
-            return fail(kInvalidArgument, "volta_mma_bwd: TMA descriptor rejected (bias)");
-        }
-    }
     BwdParams p;
-    p.bias = bias;
     p.kmask = kmask;
     p.lse = lse;
     p.delta = delta;
@@ -621,11 +707,10 @@ extern "C" int cflk_volta_mma_bwd(void* stream_, int dtype, const void* q, const
     p.D = (int)D;
     p.scale = scale;
     const cudaError_t e =
-        dtype == kBF16
-            ? run_backward<__nv_bfloat16>(stream, maps, p, out, dout, delta, dq, bias_tma,
-                                          want_dbias != 0)
-            : run_backward<__half>(stream, maps, p, out, dout, delta, dq, bias_tma,
-                                   want_dbias != 0);
+        dtype == kBF16 ? run_backward<__nv_bfloat16>(stream, maps, p, bias, bt, Sqp, out, dout,
+                                                     delta, dq, want_dbias != 0)
+                       : run_backward<__half>(stream, maps, p, bias, bt, Sqp, out, dout, delta,
+                                              dq, want_dbias != 0);
     if (e != cudaSuccess) {
         return fail(kInternal, std::string("volta_mma_bwd launch: ") + cudaGetErrorString(e));
     }
@@ -638,11 +723,12 @@ extern "C" int cflk_volta_mma_bwd(void* stream_, int dtype, const void* q, const
 // Some callers of this library cannot allocate device memory: a plugin host that owns every
 // device allocation and hands a kernel only its inputs and outputs (no scratch allocator), or
 // latency-critical code that must not call cudaMalloc because it may synchronise the device.
-// For them the backward's scratch (the float32 dQ accumulator and the row statistic) lives in
-// this file-scope array instead, kNoAllocScratchBytes long. Every GPU that loads the library
-// holds the array until the process exits. All calls on a device share it and it keeps the last
-// call's contents: the backward zero-fills the accumulator itself on every call, and calls whose
-// kernels overlap on the GPU (different streams, no ordering) race on it.
+// For them the backward's scratch (the float32 dQ accumulator, the row statistic and the
+// transposed bias) lives in this file-scope array instead, kNoAllocScratchBytes long. Every GPU
+// that loads the library holds the array until the process exits. All calls on a device share
+// it and it keeps the last call's contents: the backward rewrites or zero-fills every part of it
+// on every call, and calls whose kernels overlap on the GPU (different streams, no ordering)
+// race on it.
 // ---------------------------------------------------------------------------------------------
 static constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
@@ -695,8 +781,8 @@ extern "C" int cflk_volta_mma_bwd_noalloc(void* stream, int dtype, const void* q
                           "volta_mma_bwd_noalloc: needs " + std::to_string(need) +
                               " bytes of scratch, the static scratch holds " +
                               std::to_string(kNoAllocScratchBytes) +
-                              " (N*H*Sq*(D+1)*4 bytes plus alignment); use cflk_volta_mma_bwd "
-                              "with a workspace");
+                              " (cflk_volta_mma_bwd_workspace_size: about 4*(N*H*Sq*(D+1) + "
+                              "H*Sk*Sq) bytes); use cflk_volta_mma_bwd with a workspace");
     }
     void* scratch = nullptr;
     rc = noalloc_scratch(&scratch);

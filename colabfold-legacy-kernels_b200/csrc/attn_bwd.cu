@@ -18,9 +18,13 @@
 //     A operands of dV += P^T dout and dK += dS^T q (A read from tensor memory);
 //   * dS also goes MN-major into swizzled shared memory for dQ = dS k (M=64), whose fp32 tile
 //     is added into the workspace accumulator with 16-byte vector atomics;
-//   * the bias is transposed once per call into the workspace as fp32 [H][Sk][Sq'] scaled by
-//     log2e, so a key's bias values arrive by TMA as one contiguous row (16-byte reads);
-//   * dBias gets dS by coalesced fp32 reductions (a warp covers 32 consecutive keys of a row).
+//   * the bias is transposed once per call into the workspace as f16 [H][Sk][Sq'] (exact for
+//     f16 input; bf16 values are kept exactly within f16's range and clamped to +-65504 beyond
+//     it), so a key's bias values arrive by TMA as one contiguous 128-byte row;
+//   * dBias: each group stages its step's fp32 dS tile [64 queries][128 keys] in shared memory
+//     and one thread hands it to TMA as a single bulk reduce-add into dBias (full-line L2
+//     reductions); where the dBias rows are not 16-byte multiples (Sk % 4 != 0) the workers add
+//     dS with coalesced fp32 reductions instead (a warp covers 32 consecutive keys of a row).
 // Around it: the row statistic (delta), the bias transpose, the zero fills, the dQ conversion.
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -67,11 +71,11 @@ struct BGeom {
     static constexpr int QATOM = kBQ * ROWB;  // one atom of a 64-row (query) tile
     static constexpr int KTILE = NA * KATOM;
     static constexpr int QTILE = NA * QATOM;
-    static constexpr int BT = kBQ * kBK * 4;  // bias^T tile: two [128 keys][32 queries] fp32
+    static constexpr int BT = kBQ * kBK * 2;  // bias^T tile: [128 keys][64 queries] f16
     static constexpr int DS = kBK * 128;      // dS, MN-major: 128 key rows of 64 queries
     static constexpr int DN = DP;
-    static constexpr int NWG = DN <= 64 ? 2 : 1;  // softmax warpgroups (ping-pong)
-    static constexpr int NS = DN <= 64 ? 3 : 2;   // query-step stages
+    static constexpr int NWG = DN <= 32 ? 2 : 1;  // softmax warpgroups (ping-pong)
+    static constexpr int NS = NWG == 2 ? 4 : 3;   // query-step stages
     static constexpr int THREADS = NWG * 128 + 64;
     // TMEM columns: group w's S^T at 128w, dP^T at 128w + 64; then dV, dK, one dQ per group
     static constexpr int T_DV = NWG * 128;
@@ -90,21 +94,47 @@ struct BSmem {
     static constexpr int STAGE = V + G::KTILE;               // NS x (Q, dO, bias^T)
     static constexpr int STAGE_BYTES = 2 * G::QTILE + G::BT;
     static constexpr int DSB = STAGE + G::NS * STAGE_BYTES;  // NWG dS buffers
-    static constexpr int STAT = DSB + G::NWG * G::DS;        // [NWG][2][lse, delta][64] fp32
+    static constexpr int RED = DSB + G::NWG * G::DS;         // NWG fp32 dS tiles [64][128]
+    static constexpr int STAT = RED + G::NWG * kBQ * kBK * 4;  // [NWG][2][lse, delta][64] fp32
     static constexpr int END = STAT + G::NWG * 2 * 2 * kBQ * 4;
     static constexpr int BYTES = END + 1024;
-    static_assert(BYTES <= 227 * 1024, "shared memory");
+    static_assert(BYTES + 256 <= 227 * 1024, "shared memory (dynamic + the static barriers)");
 };
 
-__device__ __forceinline__ void red_add_f32(float* p, float v) {
-    asm volatile("red.global.add.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
+// dBias modes
+enum DbiasMode : int { kDbiasNone = 0, kDbiasRed = 1, kDbiasTma = 2 };
+
+__device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, const void* src, int c0,
+                                                  int c1, int c2) {
+    asm volatile(
+        "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.bulk_group [%0, {%2, %3, %4}], "
+        "[%1];" ::"l"(map),
+        "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
 
-template <typename T, int DP, bool WANT_DBIAS>
+// until every bulk operation this thread committed has finished reading shared memory
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
+__device__ __forceinline__ void bulk_wait_all() {
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+// A fire-and-forget fp32 add (the result is unused, so it compiles to a reduction); unlike an
+// asm statement with a memory clobber it lets the compiler overlap it with neighbouring loads.
+__device__ __forceinline__ void red_add_f32(float* p, float v) {
+    atomicAdd(p, v);
+}
+
+template <typename T, int DP, int DBIAS>
 __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                     const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
-                    const __grid_constant__ CUtensorMap tbt, const BwdParams p) {
+                    const __grid_constant__ CUtensorMap tbt, const __grid_constant__ CUtensorMap tdb,
+                    const BwdParams p) {
     using G = BGeom<DP>;
     using L = BSmem<DP>;
     using E = Elem<T>;
@@ -118,7 +148,9 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
     __shared__ int abort_flag;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n = blockIdx.x, h = blockIdx.y, k0 = blockIdx.z * kBK;
+    // key tiles and heads vary fastest, so the CTAs in flight at once reduce into many different
+    // dBias tiles rather than all into the same one
+    const int k0 = blockIdx.x * kBK, h = blockIdx.y, n = blockIdx.z;
     const int D = p.D;
     const int DN = (D + 15) & ~15;
     const int nqt = (p.Sq + kBQ - 1) / kBQ;
@@ -170,7 +202,6 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
                 }
                 uint8_t* bt = st + 2 * G::QTILE;
                 tma_load_3d(bt, &tbt, &q_full[s], q0, k0, h);
-                tma_load_3d(bt + kBK * 128, &tbt, &q_full[s], q0 + 32, k0, h);
             }
         }
     } else if (warp == MMA_WARP) {
@@ -265,6 +296,7 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
         const float qk_scale = p.scale * kLog2e;
         const float masked = kMaskedLogit * kLog2e;
         float* stat = reinterpret_cast<float*>(smem + L::STAT) + wg * (2 * 2 * kBQ);
+        float* rbuf = reinterpret_cast<float*>(smem + L::RED) + wg * (kBQ * kBK);
         float* dbias_col = p.dbias + (long long)h * p.Sq * p.Sk + key;
         uint8_t* ds_row = smem + L::DSB + wg * G::DS + t * 128;
         const uint32_t t_dq = tmem + G::T_DQ + wg * G::DN;
@@ -304,10 +336,15 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
             float* drow = dbias_col + (long long)(q0 + 32 * half) * p.Sk;
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
-                const float4 b4 = *reinterpret_cast<const float4*>(brow + ((c ^ (t & 7)) << 4));
+                // queries 32 half + 4c .. +4: half of 16-byte chunk 4 half + c/2 of the key's row
+                const uint2 b2 = *reinterpret_cast<const uint2*>(
+                    brow + (((4 * half + (c >> 1)) ^ (t & 7)) << 4) + (c & 1) * 8);
+                const float2 b01 = __half22float2(*reinterpret_cast<const __half2*>(&b2.x));
+                const float2 b23 = __half22float2(*reinterpret_cast<const __half2*>(&b2.y));
                 const float4 l4 = *reinterpret_cast<const float4*>(lsh + 4 * c);
                 const float4 d4 = *reinterpret_cast<const float4*>(dlh + 4 * c);
-                const float bb[4] = {b4.x, b4.y, b4.z, b4.w};
+                const float bb[4] = {b01.x * kLog2e, b01.y * kLog2e, b23.x * kLog2e,
+                                     b23.y * kLog2e};
                 const float ll[4] = {l4.x, l4.y, l4.z, l4.w};
                 const float dd[4] = {d4.x, d4.y, d4.z, d4.w};
                 float pv[4], gv[4];
@@ -328,7 +365,12 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
                 pw[2 * c + 1] = E::pack(pv[2], pv[3]);
                 dw[2 * c] = E::pack(gv[0], gv[1]);
                 dw[2 * c + 1] = E::pack(gv[2], gv[3]);
-                if constexpr (WANT_DBIAS) {
+                if constexpr (DBIAS == kDbiasTma) {
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        rbuf[(32 * half + 4 * c + e) * kBK + t] = gv[e];
+                    }
+                } else if constexpr (DBIAS == kDbiasRed) {
                     if (key < p.Sk) {
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
@@ -349,21 +391,30 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
             }
         };
 
+        // row statistics of a step: thread t < 64 holds lse of query t, t >= 64 delta of t - 64;
+        // loaded one step ahead so that their latency hides behind the current step
+        const auto load_stat = [&](int i) {
+            const int q = i * kBQ + (t & 63);
+            if (i >= nqt || q >= p.Sq) {
+                return t < 64 ? INFINITY : 0.f;
+            }
+            return t < 64 ? p.lse[rowbase + q] : p.delta[rowbase + q];
+        };
+        float stat_next = load_stat(wg);
         int k = 0;
         for (int i = wg; i < nqt; i += NWG, ++k) {
             const int s = i % NS, q0 = i * kBQ, b = k & 1;
             // this step's row statistics into the group's buffer b
             float* ls = stat + b * (2 * kBQ);
             float* dl = ls + kBQ;
-            {
-                const int q = q0 + (t & 63);
-                if (t < 64) {
-                    ls[t] = q < p.Sq ? p.lse[rowbase + q] : INFINITY;
-                } else {
-                    dl[t - 64] = q < p.Sq ? p.delta[rowbase + q] : 0.f;
+            stat[b * (2 * kBQ) + t] = stat_next;
+            if constexpr (DBIAS == kDbiasTma) {
+                if (t == 0 && k >= 1) {
+                    bulk_wait_read();  // the previous step's reduce has read the dS tile
                 }
             }
             named_sync(2 + wg, 128);
+            stat_next = load_stat(i + NWG);
             if (k >= 1) {
                 // this group's previous step: dQ out of tensor memory before it is reused
                 mbar_wait(&mma_done[wg], (k - 1) & 1, &g_status, kStatusMmaWait, &abort_flag);
@@ -377,7 +428,7 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
             const int nq = min(kBQ, p.Sq - q0);
 #pragma unroll 1
             for (int half = 0; half < 2; ++half) {
-                const uint8_t* brow = bt + half * (kBK * 128) + t * 128;
+                const uint8_t* brow = bt + t * 128;
                 const int jn = min(32, nq - 32 * half);
                 if (warp_live) {
                     half_step(std::true_type{}, brow, ls + 32 * half, dl + 32 * half, half, q0, jn);
@@ -390,6 +441,18 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
             fence_async_smem();
             tc_fence_before();
             mbar_arrive(&p_ready[wg]);
+            if constexpr (DBIAS == kDbiasTma) {
+                // the whole fp32 dS tile in one bulk reduce-add (rows past Sq, keys past Sk clip)
+                named_sync(2 + wg, 128);
+                if (t == 0) {
+                    tma_reduce_add_3d(&tdb, rbuf, k0, q0, h);
+                }
+            }
+        }
+        if constexpr (DBIAS == kDbiasTma) {
+            if (t == 0) {
+                bulk_wait_all();
+            }
         }
         if (k >= 1) {
             mbar_wait(&mma_done[wg], (k - 1) & 1, &g_status, kStatusMmaWait, &abort_flag);
@@ -467,7 +530,7 @@ __global__ void row_delta_kernel(const T* __restrict__ out, const T* __restrict_
 
 // bt[h][k][q] = log2e * bias[h][q][k] in fp32, queries padded to Sqp with zeros; 32x32 tiles
 template <typename T>
-__global__ void bias_transpose_kernel(const T* __restrict__ bias, float* __restrict__ bt, int Sq,
+__global__ void bias_transpose_kernel(const T* __restrict__ bias, __half* __restrict__ bt, int Sq,
                                       int Sk, int Sqp) {
     __shared__ float tile[32][33];
     const int h = blockIdx.z, q0 = blockIdx.x * 32, k0 = blockIdx.y * 32;
@@ -478,11 +541,12 @@ __global__ void bias_transpose_kernel(const T* __restrict__ bias, float* __restr
             (q < Sq && k < Sk) ? Elem<T>::to_f(src[(long long)q * Sk + k]) : 0.f;
     }
     __syncthreads();
-    float* dst = bt + (long long)h * Sk * Sqp;
+    __half* dst = bt + (long long)h * Sk * Sqp;
     for (int r = threadIdx.y; r < 32; r += blockDim.y) {
         const int k = k0 + r, q = q0 + threadIdx.x;
         if (k < Sk && q < Sqp) {
-            dst[(long long)k * Sqp + q] = tile[threadIdx.x][r] * kLog2e;
+            dst[(long long)k * Sqp + q] =
+                __float2half_rn(fminf(fmaxf(tile[threadIdx.x][r], -65504.f), 65504.f));
         }
     }
 }
@@ -517,22 +581,22 @@ bool aligned16(const void* p) {
     return (reinterpret_cast<uintptr_t>(p) & 15) == 0;
 }
 
-// Workspace: dQ accumulator | row statistic | bias^T (fp32, queries padded to a multiple of 4),
+// Workspace: dQ accumulator | row statistic | bias^T (f16, queries padded to a multiple of 8),
 // each 256-byte aligned
 struct Workspace {
     size_t dq, delta, bt, total;
     static Workspace of(size_t N, size_t H, size_t Sq, size_t Sk, size_t D) {
         Workspace w;
-        const size_t rows = N * H * Sq, sqp = (Sq + 3) & ~size_t(3);
+        const size_t rows = N * H * Sq, sqp = (Sq + 7) & ~size_t(7);
         w.dq = 0;
         w.delta = align256(rows * D * sizeof(float));
         w.bt = w.delta + align256(rows * sizeof(float));
-        w.total = w.bt + align256(H * Sk * sqp * sizeof(float));
+        w.total = w.bt + align256(H * Sk * sqp * sizeof(__half));
         return w;
     }
 };
 
-template <typename T, int DP, bool DB>
+template <typename T, int DP, int DB>
 cudaError_t launch_main(cudaStream_t stream, const CUtensorMap* maps, const BwdParams& p) {
     auto kern = attn_bwd_kernel<T, DP, DB>;
     const int smem = BSmem<DP>::BYTES;
@@ -547,22 +611,23 @@ cudaError_t launch_main(cudaStream_t stream, const CUtensorMap* maps, const BwdP
         }
         attr_done[dev] = true;
     }
-    const dim3 grid(p.N, p.H, (p.Sk + kBK - 1) / kBK);
+    const dim3 grid((p.Sk + kBK - 1) / kBK, p.H, p.N);
     kern<<<grid, BGeom<DP>::THREADS, smem, stream>>>(maps[0], maps[1], maps[2], maps[3], maps[4],
-                                                     p);
+                                                     maps[5], p);
     return cudaGetLastError();
 }
 
 template <typename T, int DP>
-cudaError_t launch_dp(cudaStream_t stream, const CUtensorMap* maps, const BwdParams& p, bool db) {
-    return db ? launch_main<T, DP, true>(stream, maps, p)
-              : launch_main<T, DP, false>(stream, maps, p);
+cudaError_t launch_dp(cudaStream_t stream, const CUtensorMap* maps, const BwdParams& p, int db) {
+    return db == kDbiasTma   ? launch_main<T, DP, kDbiasTma>(stream, maps, p)
+           : db == kDbiasRed ? launch_main<T, DP, kDbiasRed>(stream, maps, p)
+                             : launch_main<T, DP, kDbiasNone>(stream, maps, p);
 }
 
 template <typename T>
 cudaError_t run_backward(cudaStream_t stream, const CUtensorMap* maps, const BwdParams& p,
-                         const void* bias, float* bt, int Sqp, const void* out, const void* dout,
-                         float* delta, void* dq, bool want_dbias) {
+                         const void* bias, __half* bt, int Sqp, const void* out, const void* dout,
+                         float* delta, void* dq, int dbias_mode) {
     const long long rows = (long long)p.N * p.H * p.Sq;
     cudaError_t e;
     if ((e = cudaMemsetAsync(p.dbias, 0, sizeof(float) * (size_t)p.H * p.Sq * p.Sk, stream)) !=
@@ -582,10 +647,10 @@ cudaError_t run_backward(cudaStream_t stream, const CUtensorMap* maps, const Bwd
         return e;
     }
     const int DP = padded_dim(p.D);
-    e = DP == 16   ? launch_dp<T, 16>(stream, maps, p, want_dbias)
-        : DP == 32 ? launch_dp<T, 32>(stream, maps, p, want_dbias)
-        : DP == 64 ? launch_dp<T, 64>(stream, maps, p, want_dbias)
-                   : launch_dp<T, 96>(stream, maps, p, want_dbias);
+    e = DP == 16   ? launch_dp<T, 16>(stream, maps, p, dbias_mode)
+        : DP == 32 ? launch_dp<T, 32>(stream, maps, p, dbias_mode)
+        : DP == 64 ? launch_dp<T, 64>(stream, maps, p, dbias_mode)
+                   : launch_dp<T, 96>(stream, maps, p, dbias_mode);
     if (e != cudaSuccess) {
         return e;
     }
@@ -648,8 +713,8 @@ extern "C" int cflk_volta_mma_bwd(void* stream_, int dtype, const void* q, const
     uint8_t* wsb = static_cast<uint8_t*>(workspace);
     float* dq_acc = reinterpret_cast<float*>(wsb + ws.dq);
     float* delta = reinterpret_cast<float*>(wsb + ws.delta);
-    float* bt = reinterpret_cast<float*>(wsb + ws.bt);
-    const int Sqp = (int)((Sq + 3) & ~int64_t(3));
+    __half* bt = reinterpret_cast<__half*>(wsb + ws.bt);
+    const int Sqp = (int)((Sq + 7) & ~int64_t(7));
     if (H == 0 || Sq == 0 || Sk == 0 || N == 0) {
         // nothing to differentiate: zero what exists
         if (H > 0 && Sq > 0 && Sk > 0) {
@@ -671,7 +736,7 @@ extern "C" int cflk_volta_mma_bwd(void* stream_, int dtype, const void* q, const
         dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     const int DP = padded_dim((int)D);
     const int AE = DP == 96 ? 32 : DP;
-    CUtensorMap maps[5];
+    CUtensorMap maps[6];
     {
         const uint64_t dq4[4] = {(uint64_t)D, (uint64_t)H, (uint64_t)Sq, (uint64_t)N};
         const uint64_t sq4[3] = {(uint64_t)(Sq * D), (uint64_t)D, (uint64_t)(H * Sq * D)};
@@ -682,14 +747,26 @@ extern "C" int cflk_volta_mma_bwd(void* stream_, int dtype, const void* q, const
         const CUtensorMapSwizzle sw = swizzle_for_row(AE * 2);
         const uint64_t dbt[3] = {(uint64_t)Sqp, (uint64_t)Sk, (uint64_t)H};
         const uint64_t sbt[2] = {(uint64_t)Sqp, (uint64_t)Sk * (uint64_t)Sqp};
-        const uint32_t boxbt[3] = {32, (uint32_t)kBK, 1};
+        const uint32_t boxbt[3] = {(uint32_t)kBQ, (uint32_t)kBK, 1};
         if (!encode_tiled(&maps[0], tdt, 2, 4, q, dq4, sq4, boxq, sw) ||
             !encode_tiled(&maps[1], tdt, 2, 4, k, dk4, sk4, boxk, sw) ||
             !encode_tiled(&maps[2], tdt, 2, 4, v, dk4, sk4, boxk, sw) ||
             !encode_tiled(&maps[3], tdt, 2, 4, dout, dq4, sq4, boxq, sw) ||
-            !encode_tiled(&maps[4], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, 3, bt, dbt, sbt, boxbt,
+            !encode_tiled(&maps[4], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, 3, bt, dbt, sbt, boxbt,
                           CU_TENSOR_MAP_SWIZZLE_128B)) {
             return fail(kInvalidArgument, "volta_mma_bwd: TMA descriptor rejected");
+        }
+    }
+    // dBias by TMA bulk reduce where its rows are 16-byte multiples, else by fp32 reductions
+    int dbias_mode = want_dbias ? kDbiasRed : kDbiasNone;
+    maps[5] = maps[4];
+    if (want_dbias && Sk % 4 == 0 && (reinterpret_cast<uintptr_t>(dbias) & 15) == 0) {
+        const uint64_t ddb[3] = {(uint64_t)Sk, (uint64_t)Sq, (uint64_t)H};
+        const uint64_t sdb[2] = {(uint64_t)Sk, (uint64_t)Sq * (uint64_t)Sk};
+        const uint32_t boxdb[3] = {(uint32_t)kBK, (uint32_t)kBQ, 1};
+        if (encode_tiled(&maps[5], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, 3, dbias, ddb, sdb, boxdb,
+                         CU_TENSOR_MAP_SWIZZLE_NONE)) {
+            dbias_mode = kDbiasTma;
         }
     }
     BwdParams p;
@@ -708,9 +785,9 @@ extern "C" int cflk_volta_mma_bwd(void* stream_, int dtype, const void* q, const
     p.scale = scale;
     const cudaError_t e =
         dtype == kBF16 ? run_backward<__nv_bfloat16>(stream, maps, p, bias, bt, Sqp, out, dout,
-                                                     delta, dq, want_dbias != 0)
+                                                     delta, dq, dbias_mode)
                        : run_backward<__half>(stream, maps, p, bias, bt, Sqp, out, dout, delta,
-                                              dq, want_dbias != 0);
+                                              dq, dbias_mode);
     if (e != cudaSuccess) {
         return fail(kInternal, std::string("volta_mma_bwd launch: ") + cudaGetErrorString(e));
     }
@@ -781,8 +858,8 @@ extern "C" int cflk_volta_mma_bwd_noalloc(void* stream, int dtype, const void* q
                           "volta_mma_bwd_noalloc: needs " + std::to_string(need) +
                               " bytes of scratch, the static scratch holds " +
                               std::to_string(kNoAllocScratchBytes) +
-                              " (cflk_volta_mma_bwd_workspace_size: about 4*(N*H*Sq*(D+1) + "
-                              "H*Sk*Sq) bytes); use cflk_volta_mma_bwd with a workspace");
+                              " (cflk_volta_mma_bwd_workspace_size: about 4*N*H*Sq*(D+1) + "
+                              "2*H*Sk*Sq bytes); use cflk_volta_mma_bwd with a workspace");
     }
     void* scratch = nullptr;
     rc = noalloc_scratch(&scratch);

@@ -62,8 +62,8 @@ def test_workspace_size():
                                                ctypes.c_int64(32), ctypes.byref(n)) == 0
     rows = 2 * 3 * 10
     align = lambda x: (x + 255) // 256 * 256
-    # dQ accumulator, row statistic, bias^T with the queries padded to a multiple of 4
-    assert n.value == align(rows * 32 * 4) + align(rows * 4) + align(3 * 7 * 12 * 4)
+    # dQ accumulator, row statistic, f16 bias^T with the queries padded to a multiple of 8
+    assert n.value == align(rows * 32 * 4) + align(rows * 4) + align(3 * 7 * 16 * 2)
 
 
 def test_resolver_capabilities():

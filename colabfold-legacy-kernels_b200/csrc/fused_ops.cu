@@ -25,8 +25,14 @@ using namespace fused;
 // ---------------------------------------------------------------------------------------------
 // the pipeline
 // ---------------------------------------------------------------------------------------------
-// Op supplies: T, Args (with M, w_bytes, param_floats, tmem_cols, nacc, eps), keep(), kOther,
-// X_BYTES, load_params, load_weights, load_x, issue_mma, prologue, epilogue, padding, Regs.
+// The accumulators live in a ring of kSlots blocks of kSlotCols tensor-memory columns: the MMA
+// warp fills block j+1.. while the workers drain block j, so neither side waits for a whole
+// tile. Op supplies: T, Args (M, w_bytes, param_floats, eps), keep(), kOther, X_BYTES,
+// RED_FLOATS, nblocks(), load_params, load_weights, load_x, issue_block, prologue,
+// epilogue_block, padding, Regs.
+constexpr int kSlots = 4;
+constexpr int kSlotCols = 128;
+
 template <class Op>
 __global__ void __launch_bounds__(kThreads, 1)
     row_tile_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tw0,
@@ -38,18 +44,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* ws = smem + 2 * Op::X_BYTES;
     float* sp = reinterpret_cast<float*>(ws + a.w_bytes);
     float* red = sp + a.param_floats;  // [Op::RED_FLOATS]
-    __shared__ uint64_t x_full[2], x_empty[2], a_ready[2], acc_full[2], acc_empty[2], w_full;
+    __shared__ uint64_t x_full[2], x_empty[2], a_ready[2], acc_full[kSlots], acc_empty[kSlots],
+        w_full;
     __shared__ uint32_t tmem_sh;
     __shared__ int abort_flag;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ntiles = (a.M + BM - 1) / BM;
+    const int nb = Op::nblocks(a);
     if (warp == kProducerWarp) {
         if (lane == 0) {
             for (int i = 0; i < 2; ++i) {
                 mbar_init(&x_full[i], 1);
                 mbar_init(&x_empty[i], 1);
                 mbar_init(&a_ready[i], kWorkers);
+            }
+            for (int i = 0; i < kSlots; ++i) {
                 mbar_init(&acc_full[i], 1);
                 mbar_init(&acc_empty[i], kWorkers);
             }
@@ -58,11 +68,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             fence_mbar_init();
         }
         __syncwarp();
-        tmem_alloc(&tmem_sh, a.tmem_cols * a.nacc <= 32    ? 32
-                             : a.tmem_cols * a.nacc <= 64  ? 64
-                             : a.tmem_cols * a.nacc <= 128 ? 128
-                             : a.tmem_cols * a.nacc <= 256 ? 256
-                                                           : 512);
+        tmem_alloc(&tmem_sh, kSlots * kSlotCols);
         tmem_relinquish();
     } else {
         Op::load_params(a, sp, threadIdx.x);
@@ -83,7 +89,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             return -1;
         };
-        int cur = blockIdx.x, pcur = blockIdx.x, c = 0, pc = 0;
+        int cur = blockIdx.x, pcur = blockIdx.x, c = 0, q = 0;
         if (lane == 0) {
             Op::load_weights(a, &tw0, &tw1, ws, &w_full);
         }
@@ -93,9 +99,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             }
             if (lane == 0) {
-                Op::load_x(a, &tx, xs0 + (pc & 1) * Op::X_BYTES, &x_full[pc & 1], m);
+                Op::load_x(a, &tx, xs0 + k * Op::X_BYTES, &x_full[k], m);
             }
-            ++pc;
         }
         bool weights_ready = false;
         while (true) {
@@ -103,22 +108,28 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (m < 0) {
                 break;
             }
-            const int s = c & 1, r = c % a.nacc;
+            const int s = c & 1;
             if (lane == 0) {
                 if (!weights_ready) {
                     mbar_wait(&w_full, 0, &g_status, kStatusTmaWait, &abort_flag);
                     weights_ready = true;
                 }
                 mbar_wait(&a_ready[s], (c >> 1) & 1, &g_status, kStatusSyncWait, &abort_flag);
-                if (c >= a.nacc) {
-                    mbar_wait(&acc_empty[r], ((c - a.nacc) / a.nacc) & 1, &g_status,
-                              kStatusSyncWait, &abort_flag);
-                }
                 tc_fence_after();
-                Op::issue_mma(a, smem_u32(xs0 + s * Op::X_BYTES), smem_u32(ws),
-                              tmem + r * a.tmem_cols);
-                mma_commit(&acc_full[r]);
+                for (int j = 0; j < nb; ++j, ++q) {
+                    const int slot = q % kSlots;
+                    if (q >= kSlots) {
+                        mbar_wait(&acc_empty[slot], ((q - kSlots) / kSlots) & 1, &g_status,
+                                  kStatusSyncWait, &abort_flag);
+                        tc_fence_after();
+                    }
+                    Op::issue_block(a, smem_u32(xs0 + s * Op::X_BYTES), smem_u32(ws),
+                                    tmem + slot * kSlotCols, j);
+                    mma_commit(&acc_full[slot]);
+                }
                 mma_commit(&x_empty[s]);
+            } else {
+                q += nb;
             }
             __syncwarp();
             const int m2 = next(pcur);
@@ -127,7 +138,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mbar_wait(&x_empty[s], (c >> 1) & 1, &g_status, kStatusMmaWait, &abort_flag);
                     Op::load_x(a, &tx, xs0 + s * Op::X_BYTES, &x_full[s], m2);
                 }
-                ++pc;
             }
             __syncwarp();
             ++c;
@@ -136,7 +146,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int g = warp >> 2, t = ((warp & 3) << 5) | lane;
         const uint32_t lane_base = tmem_lane_base(warp);
         typename Op::Regs regs;
-        int c = 0;
+        int c = 0, q = 0;
         for (int cursor = blockIdx.x; cursor < ntiles; cursor += gridDim.x) {
             const int m0 = cursor * BM;
             const int work = tile_work(Op::keep(a), a.M, m0, Op::kOther);
@@ -147,17 +157,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (work == kSkip) {
                 continue;
             }
-            const int s = c & 1, r = c % a.nacc;
+            const int s = c & 1;
             uint8_t* stage = xs0 + s * Op::X_BYTES;
             mbar_wait(&x_full[s], (c >> 1) & 1, &g_status, kStatusTmaWait, &abort_flag);
             Op::prologue(a, stage, sp, red, t, g, m0, regs);
             fence_async_smem();
             mbar_arrive(&a_ready[s]);
-            mbar_wait(&acc_full[r], (c / a.nacc) & 1, &g_status, kStatusMmaWait, &abort_flag);
-            tc_fence_after();
-            Op::epilogue(a, tmem + r * a.tmem_cols + lane_base, sp, t, g, m0, regs);
-            tc_fence_before();
-            mbar_arrive(&acc_empty[r]);
+            for (int j = 0; j < nb; ++j, ++q) {
+                const int slot = q % kSlots;
+                mbar_wait(&acc_full[slot], (q / kSlots) & 1, &g_status, kStatusMmaWait,
+                          &abort_flag);
+                tc_fence_after();
+                Op::epilogue_block(a, tmem + slot * kSlotCols + lane_base, sp, t, g, m0, j, regs);
+                tc_fence_before();
+                mbar_arrive(&acc_empty[slot]);
+            }
             ++c;
         }
     }
@@ -165,11 +179,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     if (warp == kProducerWarp) {
         tc_fence_after();
-        tmem_dealloc(tmem, a.tmem_cols * a.nacc <= 32    ? 32
-                           : a.tmem_cols * a.nacc <= 64  ? 64
-                           : a.tmem_cols * a.nacc <= 128 ? 128
-                           : a.tmem_cols * a.nacc <= 256 ? 256
-                                                         : 512);
+        tmem_dealloc(tmem, kSlots * kSlotCols);
     }
 }
 
@@ -227,7 +237,7 @@ struct LnGdpOp {
         const T *x, *wpT, *bp, *wgT, *bg, *mask;
         const float *scale, *offset;
         T *left, *right;
-        int M, w_bytes, param_floats, tmem_cols, nacc;
+        int M, w_bytes, param_floats;
         float eps;
     };
     struct Regs {};
@@ -253,40 +263,39 @@ struct LnGdpOp {
                                   uint64_t* bar, int m0) {
         load_rows_tile(tx, dst, bar, K, m0);
     }
-    static __device__ void issue_mma(const Args& a, uint32_t xa, uint32_t wa, uint32_t acc) {
-        for (int mat = 0; mat < 2; ++mat) {
-            for (int n0 = 0; n0 < P; n0 += 256) {
-                const int N = P - n0 < 256 ? P - n0 : 256;
-                mma_rows(acc + mat * P + n0, xa, wa + mat * P * K * 2, P, K, n0, N, E::kBf16,
-                         false);
-            }
-        }
+    // block j: output channels [64j, 64j+64) of the P; the projection in the slot's columns
+    // [0, 64), the gate in [64, 128)
+    static __device__ int nblocks(const Args&) { return P / 64; }
+    static __device__ void issue_block(const Args& a, uint32_t xa, uint32_t wa, uint32_t acc,
+                                       int j) {
+        mma_rows(acc, xa, wa, P, K, 64 * j, 64, E::kBf16, false);
+        mma_rows(acc + 64, xa, wa + P * K * 2, P, K, 64 * j, 64, E::kBf16, false);
     }
     static __device__ void prologue(const Args& a, uint8_t* stage, const float* sp, float* red,
                                     int t, int g, int m0, Regs&) {
         ln_rows_half<T, K>(stage, t, g, sp, sp + K, a.eps, red, nullptr, nullptr);
     }
-    static __device__ void epilogue(const Args& a, uint32_t acc, const float* sp, int t, int g,
-                                    int m0, Regs&) {
+    // worker half g: channels 64j + 32g + [0, 32), into left or right (channel major)
+    static __device__ void epilogue_block(const Args& a, uint32_t acc, const float* sp, int t,
+                                          int g, int m0, int j, Regs&) {
         const int m = m0 + t;
-        const float mv = m < a.M ? fmaxf(E::to_f(a.mask[m]), 0.f) : 0.f;
-        T* out = g == 0 ? a.left : a.right;
-        const float* bp = sp + 2 * K + g * CI;
-        const float* bg = sp + 2 * K + P + g * CI;
-#pragma unroll 1
-        for (int c0 = 0; c0 < CI; c0 += 16) {
-            uint32_t pr[16], gr[16];
-            tmem_ld16(acc + g * CI + c0, pr);
-            tmem_ld16(acc + P + g * CI + c0, gr);
-            tmem_wait_ld();
-            if (m < a.M) {
+        const int ch0 = 64 * j + 32 * g;
+        uint32_t pr[32], gr[32];
+        tmem_ld32(acc + 32 * g, pr);
+        tmem_ld32(acc + 64 + 32 * g, gr);
+        tmem_wait_ld();
+        if (m >= a.M) {
+            return;
+        }
+        const float mv = fmaxf(E::to_f(a.mask[m]), 0.f);
+        T* out = ch0 < CI ? a.left + (long long)ch0 * a.M : a.right + (long long)(ch0 - CI) * a.M;
+        const float* bp = sp + 2 * K + ch0;
+        const float* bg = sp + 2 * K + P + ch0;
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const float pv = __uint_as_float(pr[j]) + bp[c0 + j];
-                    const float gv = __uint_as_float(gr[j]) + bg[c0 + j];
-                    out[(long long)(c0 + j) * a.M + m] = E::from_f(mv * pv * sigmoid_fast(gv));
-                }
-            }
+        for (int i = 0; i < 32; ++i) {
+            const float pv = __uint_as_float(pr[i]) + bp[i];
+            const float gv = __uint_as_float(gr[i]) + bg[i];
+            out[(long long)i * a.M + m] = E::from_f(mv * pv * sigmoid_fast(gv));
         }
     }
     static __device__ void padding(const Args& a, int m0, int t, int g) {
@@ -318,7 +327,7 @@ struct ProjOp {
         const float *scale, *offset;
         T *out, *bias;
         int M, n, ldp, heads;
-        int w_bytes, param_floats, tmem_cols, nacc;
+        int w_bytes, param_floats;
         float eps;
     };
     struct Regs {};
@@ -347,11 +356,12 @@ struct ProjOp {
                                   uint64_t* bar, int m0) {
         load_rows_tile(tx, dst, bar, K, m0);
     }
-    static __device__ void issue_mma(const Args& a, uint32_t xa, uint32_t wa, uint32_t acc) {
-        for (int n0 = 0; n0 < a.n; n0 += 256) {
-            const int N = a.n - n0 < 256 ? a.n - n0 : 256;
-            mma_rows(acc + n0, xa, wa, a.n, K, n0, N, E::kBf16, false);
-        }
+    // block j: output columns [128j, 128j + 128) (the last one 64 wide when n % 128 == 64)
+    static __device__ int nblocks(const Args& a) { return (a.n + 127) / 128; }
+    static __device__ void issue_block(const Args& a, uint32_t xa, uint32_t wa, uint32_t acc,
+                                       int j) {
+        const int n0 = 128 * j, N = a.n - n0 < 128 ? a.n - n0 : 128;
+        mma_rows(acc, xa, wa, a.n, K, n0, N, E::kBf16, false);
     }
     static __device__ void prologue(const Args& a, uint8_t* stage, const float* sp, float* red,
                                     int t, int g, int m0, Regs&) {
@@ -380,13 +390,16 @@ struct ProjOp {
             }
         }
     }
-    static __device__ void epilogue(const Args& a, uint32_t acc, const float* sp, int t, int g,
-                                    int m0, Regs&) {
+    // worker half g: columns 128j + g w/2 + [0, w/2) of the block's width w
+    static __device__ void epilogue_block(const Args& a, uint32_t acc, const float* sp, int t,
+                                          int g, int m0, int j, Regs&) {
         const int m = m0 + t;
-        const int half = a.n / 2;
-        const float* b = sp + 2 * K;
-        T* orow = a.out + (long long)m * a.ldp;
-        const T* rrow = a.residual != nullptr ? a.residual + (long long)m * a.ldp : nullptr;
+        const int width = a.n - 128 * j < 128 ? a.n - 128 * j : 128;
+        const int half = width / 2;
+        const float* b = sp + 2 * K + 128 * j;
+        T* orow = a.out + (long long)m * a.ldp + 128 * j;
+        const T* rrow =
+            a.residual != nullptr ? a.residual + (long long)m * a.ldp + 128 * j : nullptr;
 #pragma unroll 1
         for (int c0 = g * half; c0 < (g + 1) * half; c0 += 16) {
             uint32_t r[16];
@@ -458,7 +471,7 @@ struct TrimulOp {
         const T *x, *woT, *bo, *wgT, *bg, *keep;
         const float *in_scale, *in_offset, *ln_scale, *ln_offset;
         T* out;
-        int M, w_bytes, param_floats, tmem_cols, nacc;
+        int M, w_bytes, param_floats;
         float eps;
     };
     struct Regs {};
@@ -488,9 +501,13 @@ struct TrimulOp {
                                   uint64_t* bar, int m0) {
         load_rows_tile(tx, dst + XOFF, bar, CA, m0);
     }
-    static __device__ void issue_mma(const Args& a, uint32_t xa, uint32_t wa, uint32_t acc) {
-        mma_rows(acc, xa, wa, O, C, 0, O, E::kBf16, false);
-        mma_rows(acc + O, xa + XOFF, wa + O * C * 2, O, CA, 0, O, E::kBf16, false);
+    // block j: output channels [64j, 64j+64); LN(x_cm^T) wo in the slot's columns [0, 64),
+    // LN_in(x) wg in [64, 128)
+    static __device__ int nblocks(const Args&) { return O / 64; }
+    static __device__ void issue_block(const Args& a, uint32_t xa, uint32_t wa, uint32_t acc,
+                                       int j) {
+        mma_rows(acc, xa, wa, O, C, 64 * j, 64, E::kBf16, false);
+        mma_rows(acc + 64, xa + XOFF, wa + O * C * 2, O, CA, 64 * j, 64, E::kBf16, false);
     }
     static __device__ void prologue(const Args& a, uint8_t* stage, const float* sp, float* red,
                                     int t, int g, int m0, Regs&) {
@@ -538,18 +555,19 @@ struct TrimulOp {
         // then LN_in(x) in place on the TMA-loaded x atoms
         ln_rows_half<T, CA>(stage + XOFF, t, g, sp, sp + CA, a.eps, red, nullptr, nullptr);
     }
-    static __device__ void epilogue(const Args& a, uint32_t acc, const float* sp, int t, int g,
-                                    int m0, Regs&) {
+    // worker half g: channels 64j + 32g + [0, 32)
+    static __device__ void epilogue_block(const Args& a, uint32_t acc, const float* sp, int t,
+                                          int g, int m0, int j, Regs&) {
         const int m = m0 + t;
-        const float* bo = sp + 2 * CA + 2 * C;
+        const float* bo = sp + 2 * CA + 2 * C + 64 * j;
         const float* bg = bo + O;
-        T* orow = a.out + (long long)m * O;
-        const T* xrow = a.x + (long long)m * CA;
+        T* orow = a.out + (long long)m * O + 64 * j;
+        const T* xrow = a.x + (long long)m * CA + 64 * j;
 #pragma unroll 1
-        for (int c0 = g * (O / 2); c0 < (g + 1) * (O / 2); c0 += 16) {
+        for (int c0 = 32 * g; c0 < 32 * g + 32; c0 += 16) {
             uint32_t ro[16], rg[16];
             tmem_ld16(acc + c0, ro);
-            tmem_ld16(acc + O + c0, rg);
+            tmem_ld16(acc + 64 + c0, rg);
             tmem_wait_ld();
             if (m < a.M) {
                 float v[16];
@@ -1066,8 +1084,6 @@ cudaError_t ln_gdp_typed(cudaStream_t stream, int dtype, const void* x, const fl
     a.M = M;
     a.w_bytes = 2 * Op::P * K * 2;
     a.param_floats = 2 * K + 2 * Op::P;
-    a.tmem_cols = 2 * Op::P;
-    a.nacc = 2 * Op::P <= 256 ? 2 : 1;
     a.eps = eps;
     return launch_op<Op>(stream, tx, tw0, tw1, a);
 }
@@ -1106,8 +1122,6 @@ cudaError_t proj_typed(cudaStream_t stream, int dtype, const void* x, const floa
     a.heads = heads;
     a.w_bytes = n * K * 2;
     a.param_floats = 2 * K + n + 8 * K;
-    a.tmem_cols = n > 0 ? n : 32;
-    a.nacc = n <= 256 ? 2 : 1;
     a.eps = eps;
     return launch_op<Op>(stream, tx, tw0, tw0, a);
 }
@@ -1141,8 +1155,6 @@ cudaError_t trimul_typed(cudaStream_t stream, int dtype, const float* x_cm, cons
     a.M = M;
     a.w_bytes = (O * C + O * CA) * 2;
     a.param_floats = 2 * CA + 2 * C + 2 * O;
-    a.tmem_cols = 2 * O;
-    a.nacc = 2;
     a.eps = eps;
     return launch_op<Op>(stream, tx, tw0, tw1, a);
 }

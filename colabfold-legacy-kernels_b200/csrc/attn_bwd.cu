@@ -7,24 +7,31 @@
 // as colabfold-legacy-kernels computes them (cuda/volta_mma_attn_bwd.cu:84-383, where P still
 // carries dV through a masked key but dS does not). The design is this file's own:
 //
-//   * one CTA owns a 128-key tile of one (n, h): K and V stay in shared memory, dK and dV
-//     accumulate in tensor memory over every query, so both come out bitwise deterministic;
-//   * warp roles: a TMA warp streams the 64-query steps (q, dout and the bias tile) two or
-//     three stages deep; an MMA warp issues every tcgen05 MMA; two softmax warpgroups take the
-//     steps alternately (ping-pong), each with its own S^T/dP^T columns in tensor memory and
-//     its own dS buffer, so one group's exponentials overlap the other group's MMAs;
+//   * persistent CTAs, one per SM, each looping over work items (a 128-key tile of one (n, h)):
+//     K and V of an item stay in shared memory (two buffers, so the next item's tiles load
+//     while this one runs) and dK, dV accumulate in tensor memory over every query (two sets,
+//     so one item's are stored while the next accumulates); both come out bitwise
+//     deterministic;
+//   * warp roles: a TMA warp streams the 64-query steps (q, dout and the bias tile) three
+//     stages deep; MMA warp A issues S^T, dP^T and dQ, MMA warp B dV and dK (each issuing
+//     thread has its own MMA pipeline, so the two overlap); softmax warpgroups in step sets
+//     that take the steps alternately (ping-pong), each set with its own S^T/dP^T columns in
+//     tensor memory and its own dS buffer, so one set's exponentials overlap the other set's
+//     MMAs; the two warpgroups of a set take the two 32-query halves of its step;
 //   * S^T = K Q^T and dP^T = V dout^T (M=128 keys, N=64 queries); worker t owns key t = TMEM
-//     lane t, forms P^T and dS^T and writes them back over S^T and dP^T as 16-bit pairs, the
-//     A operands of dV += P^T dout and dK += dS^T q (A read from tensor memory);
+//     lane t, forms P^T and dS^T and writes them back over its own S^T and dP^T columns as
+//     16-bit pairs, the A operands of dV += P^T dout and dK += dS^T q (A read from TMEM);
 //   * dS also goes MN-major into swizzled shared memory for dQ = dS k (M=64), whose fp32 tile
 //     is added into the workspace accumulator with 16-byte vector atomics;
 //   * the bias is transposed once per call into the workspace as f16 [H][Sk][Sq'] (exact for
 //     f16 input; bf16 values are kept exactly within f16's range and clamped to +-65504 beyond
 //     it), so a key's bias values arrive by TMA as one contiguous 128-byte row;
-//   * dBias: each group stages its step's fp32 dS tile [64 queries][128 keys] in shared memory
-//     and one thread hands it to TMA as a single bulk reduce-add into dBias (full-line L2
-//     reductions); where the dBias rows are not 16-byte multiples (Sk % 4 != 0) the workers add
-//     dS with coalesced fp32 reductions instead (a warp covers 32 consecutive keys of a row).
+//   * dBias: each warpgroup stages its half-step's fp32 dS rows [32 queries][128 keys] in
+//     shared memory and one thread hands them to TMA as a single bulk reduce-add into dBias
+//     (full-line L2 reductions); an item's query steps start at a step that depends on its
+//     sequence, so concurrent items reduce into different rows. Where the dBias rows are not
+//     16-byte multiples (Sk % 4 != 0) the workers add dS with coalesced fp32 reductions
+//     instead (a warp covers 32 consecutive keys of a row).
 // Around it: the row statistic (delta), the bias transpose, the zero fills, the dQ conversion.
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -74,14 +81,23 @@ struct BGeom {
     static constexpr int BT = kBQ * kBK * 2;  // bias^T tile: [128 keys][64 queries] f16
     static constexpr int DS = kBK * 128;      // dS, MN-major: 128 key rows of 64 queries
     static constexpr int DN = DP;
-    static constexpr int NWG = DN <= 32 ? 2 : 1;  // softmax warpgroups (ping-pong)
-    static constexpr int NS = NWG == 2 ? 4 : 3;   // query-step stages
-    static constexpr int THREADS = NWG * 128 + 64;
-    // TMEM columns: group w's S^T at 128w, dP^T at 128w + 64; then dV, dK, one dQ per group
-    static constexpr int T_DV = NWG * 128;
-    static constexpr int T_DK = T_DV + DN;
-    static constexpr int T_DQ = T_DK + DN;
-    static constexpr int COLS = T_DQ + NWG * DN;
+    // Step sets: consecutive 64-query steps alternate between NP sets (ping-pong). A set is two
+    // softmax warpgroups, one per 32-query half of its step.
+    static constexpr int NP = DN <= 32 ? 2 : 1;
+    static constexpr int NWG = 2 * NP;
+    static constexpr int MMA_A = 4 * NWG;    // warp issuing S^T, dP^T and dQ
+    static constexpr int MMA_B = MMA_A + 1;  // warp issuing dV and dK
+    static constexpr int TMA_WARP = MMA_A + 2;
+    static constexpr int THREADS = NWG * 128 + 96;
+    // K/V buffers in shared memory and dK/dV accumulator sets in tensor memory: two of each, so
+    // that a CTA loads its next key tile and starts its MMAs while it stores the previous one
+    static constexpr int KVB = DP == 96 ? 1 : 2;
+    static constexpr int NB = DP == 96 ? 1 : 2;
+    static constexpr int NS = NP == 2 ? 3 : DP == 96 ? 2 : 3;  // query-step stages
+    // TMEM columns: set w's S^T at 128w, dP^T at 128w + 64; then NB x (dV, dK); one dQ per set
+    static constexpr int T_ACC = NP * 128;
+    static constexpr int T_DQ = T_ACC + NB * 2 * DN;
+    static constexpr int COLS = T_DQ + NP * DN;
     static constexpr uint32_t ALLOC = COLS <= 256 ? 256 : 512;
     static_assert(COLS <= 512, "tensor memory");
 };
@@ -89,16 +105,15 @@ struct BGeom {
 template <int DP>
 struct BSmem {
     using G = BGeom<DP>;
-    static constexpr int K = 0;
-    static constexpr int V = K + G::KTILE;
-    static constexpr int STAGE = V + G::KTILE;               // NS x (Q, dO, bias^T)
+    static constexpr int KV = 0;                             // KVB x (K, V)
+    static constexpr int STAGE = KV + G::KVB * 2 * G::KTILE;  // NS x (Q, dO, bias^T)
     static constexpr int STAGE_BYTES = 2 * G::QTILE + G::BT;
-    static constexpr int DSB = STAGE + G::NS * STAGE_BYTES;  // NWG dS buffers
-    static constexpr int RED = DSB + G::NWG * G::DS;         // NWG fp32 dS tiles [64][128]
-    static constexpr int STAT = RED + G::NWG * kBQ * kBK * 4;  // [NWG][2][lse, delta][64] fp32
-    static constexpr int END = STAT + G::NWG * 2 * 2 * kBQ * 4;
+    static constexpr int DSB = STAGE + G::NS * STAGE_BYTES;  // one dS buffer per set
+    static constexpr int RED = DSB + G::NP * G::DS;          // one fp32 dS tile [64][128] per set
+    static constexpr int STAT = RED + G::NP * kBQ * kBK * 4;   // [NWG][2][lse, delta][32] fp32
+    static constexpr int END = STAT + G::NWG * 2 * 2 * 32 * 4;
     static constexpr int BYTES = END + 1024;
-    static_assert(BYTES + 256 <= 227 * 1024, "shared memory (dynamic + the static barriers)");
+    static_assert(BYTES + 512 <= 227 * 1024, "shared memory (dynamic + the static barriers)");
 };
 
 // dBias modes
@@ -129,6 +144,58 @@ __device__ __forceinline__ void red_add_f32(float* p, float v) {
     atomicAdd(p, v);
 }
 
+// Where global step gi of a CTA lies: its work item (key tile, head, sequence) and query step.
+// A CTA takes items blockIdx.x, blockIdx.x + gridDim.x, ... (key tiles fastest, then heads,
+// then sequences) and runs every item's nqt query steps in turn. The query steps of an item
+// start at one that depends on its sequence, so the CTAs of different sequences running at once
+// reduce into different dBias rows.
+struct StepPos {
+    int k0, h, n, q0;
+    long long rowbase;  // (n * H + h) * Sq
+};
+
+// The position of local step i of the CTA's item j (divisions: once per item)
+__device__ __forceinline__ StepPos item_pos(const BwdParams& p, int nkt, int j) {
+    const int u = (int)blockIdx.x + j * (int)gridDim.x;
+    const int rest = u / nkt;
+    StepPos s;
+    s.k0 = (u - rest * nkt) * kBK;
+    s.h = rest % p.H;
+    s.n = rest / p.H;
+    s.q0 = 0;
+    s.rowbase = ((long long)s.n * p.H + s.h) * p.Sq;
+    return s;
+}
+
+__device__ __forceinline__ int rotated_q0(int n, int nqt, int i) {
+    const int r = n % nqt;
+    return (i + r < nqt ? i + r : i + r - nqt) * kBQ;
+}
+
+// A walk over global steps gi = j * nqt + i in strides of `by` (by <= nqt is not required)
+struct StepCursor {
+    int gi, j, i;
+    StepPos pos;
+    __device__ __forceinline__ void start(const BwdParams& p, int nkt, int nqt, int g) {
+        gi = g;
+        j = g / nqt;
+        i = g - j * nqt;
+        pos = item_pos(p, nkt, j);
+        pos.q0 = rotated_q0(pos.n, nqt, i);
+    }
+    __device__ __forceinline__ void advance(const BwdParams& p, int nkt, int nqt, int by) {
+        gi += by;
+        i += by;
+        if (i >= nqt) {
+            const int dj = i / nqt;
+            j += dj;
+            i -= dj * nqt;
+            pos = item_pos(p, nkt, j);
+        }
+        pos.q0 = rotated_q0(pos.n, nqt, i);
+    }
+};
+
 template <typename T, int DP, int DBIAS>
 __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
@@ -138,35 +205,44 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
     using G = BGeom<DP>;
     using L = BSmem<DP>;
     using E = Elem<T>;
-    constexpr int NWG = G::NWG, NS = G::NS;
-    constexpr int MMA_WARP = 4 * NWG, TMA_WARP = MMA_WARP + 1;
+    constexpr int NP = G::NP, NS = G::NS, KVB = G::KVB, NB = G::NB;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    __shared__ uint64_t kv_full, q_full[NS], q_empty[NS], s_full[2], p_ready[2], mma_done[2];
+    __shared__ uint64_t kv_full[KVB], kv_empty[KVB], q_full[NS], q_empty[NS], s_full[NP],
+        p_ready[NP], ts_done[NP], dq_done[NP], acc_full[NB], acc_empty[NB];
     __shared__ uint32_t tmem_base_sh;
     __shared__ int abort_flag;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // key tiles and heads vary fastest, so the CTAs in flight at once reduce into many different
-    // dBias tiles rather than all into the same one
-    const int k0 = blockIdx.x * kBK, h = blockIdx.y, n = blockIdx.z;
     const int D = p.D;
     const int DN = (D + 15) & ~15;
+    const int nkt = (p.Sk + kBK - 1) / kBK;
     const int nqt = (p.Sq + kBQ - 1) / kBQ;
-    const long long rowbase = ((long long)n * p.H + h) * p.Sq;
+    const int nitems = nkt * p.H * p.N;  // the host keeps nitems * nqt below 2^31
+    const int J = nitems > (int)blockIdx.x ? (nitems - 1 - (int)blockIdx.x) / (int)gridDim.x + 1
+                                           : 0;
+    const int total = J * nqt;  // this CTA's query steps
 
-    if (warp == MMA_WARP) {
+    if (warp == G::MMA_A) {
         if (lane == 0) {
-            mbar_init(&kv_full, 1);
+            for (int i = 0; i < KVB; ++i) {
+                mbar_init(&kv_full[i], 1);
+                mbar_init(&kv_empty[i], 1);
+            }
             for (int i = 0; i < NS; ++i) {
                 mbar_init(&q_full[i], 1);
-                mbar_init(&q_empty[i], 1);
+                mbar_init(&q_empty[i], 2);  // both MMA warps read a stage
             }
-            for (int i = 0; i < 2; ++i) {
+            for (int i = 0; i < NP; ++i) {
                 mbar_init(&s_full[i], 1);
-                mbar_init(&p_ready[i], 128);
-                mbar_init(&mma_done[i], 1);
+                mbar_init(&p_ready[i], 256);
+                mbar_init(&ts_done[i], 1);
+                mbar_init(&dq_done[i], 1);
+            }
+            for (int i = 0; i < NB; ++i) {
+                mbar_init(&acc_full[i], 1);
+                mbar_init(&acc_empty[i], G::NWG * 128);
             }
             abort_flag = 0;
             fence_mbar_init();
@@ -180,46 +256,64 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
     tc_fence_after();
     const uint32_t tmem = tmem_base_sh;
 
-    if (warp == TMA_WARP) {
+    if (warp == G::TMA_WARP) {
         if (lane == 0) {
-            mbar_arrive_expect_tx(&kv_full, 2 * G::KTILE);
-            for (int a = 0; a < G::NA; ++a) {
-                tma_load_4d(smem + L::K + a * G::KATOM, &tk, &kv_full, a * G::AE, h, k0, n);
-                tma_load_4d(smem + L::V + a * G::KATOM, &tv, &kv_full, a * G::AE, h, k0, n);
-            }
-            for (int i = 0; i < nqt; ++i) {
-                const int s = i % NS, q0 = i * kBQ;
-                if (i >= NS) {
-                    mbar_wait(&q_empty[s], ((i - NS) / NS) & 1, &g_status, kStatusMmaWait,
+            for (int j = 0; j < J; ++j) {
+                const StepPos it = item_pos(p, nkt, j);
+                const int kb = j % KVB;
+                if (j >= KVB) {
+                    mbar_wait(&kv_empty[kb], ((j - KVB) / KVB) & 1, &g_status, kStatusMmaWait,
                               &abort_flag);
                 }
-                uint8_t* st = smem + L::STAGE + s * L::STAGE_BYTES;
-                mbar_arrive_expect_tx(&q_full[s], L::STAGE_BYTES);
+                uint8_t* kv = smem + L::KV + kb * 2 * G::KTILE;
+                mbar_arrive_expect_tx(&kv_full[kb], 2 * G::KTILE);
                 for (int a = 0; a < G::NA; ++a) {
-                    tma_load_4d(st + a * G::QATOM, &tq, &q_full[s], a * G::AE, h, q0, n);
-                    tma_load_4d(st + G::QTILE + a * G::QATOM, &tdo, &q_full[s], a * G::AE, h, q0,
-                                n);
+                    tma_load_4d(kv + a * G::KATOM, &tk, &kv_full[kb], a * G::AE, it.h, it.k0,
+                                it.n);
+                    tma_load_4d(kv + G::KTILE + a * G::KATOM, &tv, &kv_full[kb], a * G::AE, it.h,
+                                it.k0, it.n);
                 }
-                uint8_t* bt = st + 2 * G::QTILE;
-                tma_load_3d(bt, &tbt, &q_full[s], q0, k0, h);
+                for (int i = 0; i < nqt; ++i) {
+                    const int gi = j * nqt + i;
+                    StepPos sp = it;
+                    sp.q0 = rotated_q0(it.n, nqt, i);
+                    const int s = gi % NS;
+                    if (gi >= NS) {
+                        mbar_wait(&q_empty[s], ((gi - NS) / NS) & 1, &g_status, kStatusMmaWait,
+                                  &abort_flag);
+                    }
+                    uint8_t* st = smem + L::STAGE + s * L::STAGE_BYTES;
+                    mbar_arrive_expect_tx(&q_full[s], L::STAGE_BYTES);
+                    for (int a = 0; a < G::NA; ++a) {
+                        tma_load_4d(st + a * G::QATOM, &tq, &q_full[s], a * G::AE, sp.h, sp.q0,
+                                    sp.n);
+                        tma_load_4d(st + G::QTILE + a * G::QATOM, &tdo, &q_full[s], a * G::AE,
+                                    sp.h, sp.q0, sp.n);
+                    }
+                    tma_load_3d(st + 2 * G::QTILE, &tbt, &q_full[s], sp.q0, sp.k0, sp.h);
+                }
             }
         }
-    } else if (warp == MMA_WARP) {
+    } else if (warp == G::MMA_A) {
         if (lane == 0) {
             const uint32_t idesc_s = idesc_f16(E::kBf16, 128, kBQ, false, false);
-            const uint32_t idesc_acc = idesc_f16(E::kBf16, 128, DN, false, true);
             const uint32_t idesc_dq = idesc_f16(E::kBf16, 64, DN, true, true);
-            const uint32_t k_base = smem_u32(smem + L::K), v_base = smem_u32(smem + L::V);
-            mbar_wait(&kv_full, 0, &g_status, kStatusTmaWait, &abort_flag);
-            // S^T and dP^T of step i into group (i % NWG)'s columns
-            const auto first_half = [&](int i) {
-                const int w = i % NWG, s = i % NS;
-                mbar_wait(&q_full[s], (i / NS) & 1, &g_status, kStatusTmaWait, &abort_flag);
-                if (i >= NWG) {
-                    mbar_wait(&mma_done[w], ((i - NWG) / NWG) & 1, &g_status, kStatusMmaWait,
+            // S^T = K Q^T and dP^T = V dO^T of step gi into set (gi % NP)'s columns, once the dV
+            // and dK MMAs of that set's previous step have read its P^T and dS^T
+            const auto issue_s = [&](int gi, int j, int i) {
+                const int w = gi % NP, s = gi % NS, kb = j % KVB;
+                if (i == 0) {
+                    mbar_wait(&kv_full[kb], (j / KVB) & 1, &g_status, kStatusTmaWait,
+                              &abort_flag);
+                }
+                mbar_wait(&q_full[s], (gi / NS) & 1, &g_status, kStatusTmaWait, &abort_flag);
+                if (gi >= NP) {
+                    mbar_wait(&ts_done[w], ((gi - NP) / NP) & 1, &g_status, kStatusMmaWait,
                               &abort_flag);
                 }
                 tc_fence_after();
+                const uint32_t k_base = smem_u32(smem + L::KV + kb * 2 * G::KTILE);
+                const uint32_t v_base = k_base + G::KTILE;
                 const uint32_t st = smem_u32(smem + L::STAGE + s * L::STAGE_BYTES);
 #pragma unroll
                 for (int ks = 0; ks < DP / 16; ++ks) {
@@ -236,24 +330,15 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
                     mma_ss(tmem + 128 * w + 64, vd, od, idesc_s, ks > 0);
                 }
                 mma_commit(&s_full[w]);
+                mma_commit(&q_empty[s]);
             };
-            // dV, dK and dQ of step j once its group has written P^T, dS^T and dS
-            const auto second_half = [&](int j) {
-                const int w = j % NWG, s = j % NS;
-                mbar_wait(&p_ready[w], (j / NWG) & 1, &g_status, kStatusSyncWait, &abort_flag);
+            // dQ = dS K (M = 64 queries) of step gj once its set has written dS; the item's last
+            // dQ releases its K/V buffer
+            const auto issue_dq = [&](int gj, int j, int i) {
+                const int w = gj % NP, kb = j % KVB;
+                mbar_wait(&p_ready[w], (gj / NP) & 1, &g_status, kStatusSyncWait, &abort_flag);
                 tc_fence_after();
-                const uint32_t st = smem_u32(smem + L::STAGE + s * L::STAGE_BYTES);
-#pragma unroll
-                for (int ks = 0; ks < kBQ / 16; ++ks) {
-                    const uint64_t od = smem_desc(st + G::QTILE + ks * 16 * G::ROWB, G::QATOM,
-                                                  8 * G::ROWB, G::LAYOUT);
-                    const uint64_t qd =
-                        smem_desc(st + ks * 16 * G::ROWB, G::QATOM, 8 * G::ROWB, G::LAYOUT);
-                    mma_ts(tmem + G::T_DV, tmem + 128 * w + ks * 8, od, idesc_acc,
-                           (j > 0 || ks > 0) ? 1u : 0u);
-                    mma_ts(tmem + G::T_DK, tmem + 128 * w + 64 + ks * 8, qd, idesc_acc,
-                           (j > 0 || ks > 0) ? 1u : 0u);
-                }
+                const uint32_t k_base = smem_u32(smem + L::KV + kb * 2 * G::KTILE);
                 const uint32_t ds_base = smem_u32(smem + L::DSB + w * G::DS);
 #pragma unroll
                 for (int ks = 0; ks < kBK / 16; ++ks) {
@@ -263,54 +348,96 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
                         smem_desc(k_base + ks * 16 * G::ROWB, G::KATOM, 8 * G::ROWB, G::LAYOUT);
                     mma_ss(tmem + G::T_DQ + w * G::DN, ad, bd, idesc_dq, ks > 0 ? 1u : 0u);
                 }
-                mma_commit(&mma_done[w]);
-                mma_commit(&q_empty[s]);
+                mma_commit(&dq_done[w]);
+                if (i == nqt - 1) {
+                    mma_commit(&kv_empty[kb]);
+                }
             };
-            for (int i = 0; i <= nqt; ++i) {
-                if constexpr (NWG == 2) {
-                    // the next step's S^T and dP^T go ahead of this step's accumulations
-                    if (i < nqt) {
-                        first_half(i);
+            int pj = 0, pi = 0;  // the previous step
+            for (int j = 0, gi = 0; j < J; ++j) {
+                for (int i = 0; i < nqt; ++i, ++gi) {
+                    if constexpr (NP == 2) {
+                        // the next step's S^T and dP^T go ahead of this step's dQ
+                        issue_s(gi, j, i);
+                        if (gi >= 1) {
+                            issue_dq(gi - 1, pj, pi);
+                        }
+                    } else {
+                        if (gi >= 1) {
+                            issue_dq(gi - 1, pj, pi);
+                        }
+                        issue_s(gi, j, i);
                     }
-                    if (i >= 1) {
-                        second_half(i - 1);
-                    }
-                } else {
-                    // one group: its columns are free only after the previous step's MMAs
-                    if (i >= 1) {
-                        second_half(i - 1);
-                    }
-                    if (i < nqt) {
-                        first_half(i);
-                    }
+                    pj = j;
+                    pi = i;
+                }
+            }
+            if (total >= 1) {
+                issue_dq(total - 1, pj, pi);
+            }
+        }
+    } else if (warp == G::MMA_B) {
+        if (lane == 0) {
+            // dV += P^T dO and dK += dS^T Q, A read from tensor memory: the 16-bit P^T (dS^T) of
+            // queries [32 hf, 32 hf + 32) sits in columns [32 hf, 32 hf + 16) of S^T (dP^T)
+            const uint32_t idesc_acc = idesc_f16(E::kBf16, 128, DN, false, true);
+            for (int gi = 0, j = 0, i = 0; gi < total; ++gi) {
+                const int w = gi % NP, s = gi % NS, db = j % NB;
+                if (i == 0 && j >= NB) {
+                    // the accumulators of item j - NB have been stored
+                    mbar_wait(&acc_empty[db], ((j - NB) / NB) & 1, &g_status, kStatusSyncWait,
+                              &abort_flag);
+                }
+                mbar_wait(&q_full[s], (gi / NS) & 1, &g_status, kStatusTmaWait, &abort_flag);
+                mbar_wait(&p_ready[w], (gi / NP) & 1, &g_status, kStatusSyncWait, &abort_flag);
+                tc_fence_after();
+                const uint32_t st = smem_u32(smem + L::STAGE + s * L::STAGE_BYTES);
+                const uint32_t t_dv = tmem + G::T_ACC + db * 2 * G::DN, t_dk = t_dv + G::DN;
+#pragma unroll
+                for (int ks = 0; ks < kBQ / 16; ++ks) {
+                    const uint32_t acol = 8 * ks + 16 * (ks >> 1);
+                    const uint64_t od = smem_desc(st + G::QTILE + ks * 16 * G::ROWB, G::QATOM,
+                                                  8 * G::ROWB, G::LAYOUT);
+                    const uint64_t qd =
+                        smem_desc(st + ks * 16 * G::ROWB, G::QATOM, 8 * G::ROWB, G::LAYOUT);
+                    mma_ts(t_dv, tmem + 128 * w + acol, od, idesc_acc, (i > 0 || ks > 0) ? 1u : 0u);
+                    mma_ts(t_dk, tmem + 128 * w + 64 + acol, qd, idesc_acc,
+                           (i > 0 || ks > 0) ? 1u : 0u);
+                }
+                mma_commit(&ts_done[w]);
+                mma_commit(&q_empty[s]);
+                if (i == nqt - 1) {
+                    mma_commit(&acc_full[db]);
+                }
+                if (++i == nqt) {
+                    i = 0;
+                    ++j;
                 }
             }
         }
     } else {
-        // softmax warpgroups: worker (wg, t) owns key k0 + t = TMEM lane t
-        const int wg = warp >> 2, t = ((warp & 3) << 5) | lane;
-        const int key = k0 + t;
+        // softmax warpgroups: worker (wg, t) owns key k0 + t = TMEM lane t, for the queries
+        // [32 hf, 32 hf + 32) of the steps of set `set`
+        const int wg = warp >> 2, set = wg >> 1, hf = wg & 1, t = ((warp & 3) << 5) | lane;
         const uint32_t lane_base = tmem_lane_base(warp);
-        const bool live = key < p.Sk && p.kmask[(long long)n * p.Sk + key] != 0;
-        const bool warp_live = __all_sync(0xffffffffu, live);
         const float qk_scale = p.scale * kLog2e;
         const float masked = kMaskedLogit * kLog2e;
-        float* stat = reinterpret_cast<float*>(smem + L::STAT) + wg * (2 * 2 * kBQ);
-        float* rbuf = reinterpret_cast<float*>(smem + L::RED) + wg * (kBQ * kBK);
-        float* dbias_col = p.dbias + (long long)h * p.Sq * p.Sk + key;
-        uint8_t* ds_row = smem + L::DSB + wg * G::DS + t * 128;
-        const uint32_t t_dq = tmem + G::T_DQ + wg * G::DN;
-        const uint32_t t_st = tmem + 128 * wg + lane_base, t_dp = t_st + 64;
+        float* stat = reinterpret_cast<float*>(smem + L::STAT) + wg * (2 * 2 * 32);
+        float* rbuf = reinterpret_cast<float*>(smem + L::RED) + set * (kBQ * kBK) + hf * 32 * kBK;
+        uint8_t* ds_row = smem + L::DSB + set * G::DS + t * 128;
+        const uint32_t t_dq = tmem + G::T_DQ + set * G::DN;
+        const uint32_t t_st = tmem + 128 * set + lane_base + 32 * hf, t_dp = t_st + 64;
 
-        // dQ of a step: lanes 32w + r (r < 16) hold query row 16w + r (M=64 layout)
-        const auto flush_dq = [&](int i) {
-            const int q = i * kBQ + 16 * (warp & 3) + lane;
-            for (int c = 0; c < DN; c += 16) {
+        // dQ of a step: lanes 32w + r (r < 16) hold query row 16w + r (M=64 layout); the two
+        // warpgroups of the set take alternate 16-column chunks
+        const auto flush_dq = [&](const StepPos& sp) {
+            const int q = sp.q0 + 16 * (warp & 3) + lane;
+            for (int c = 16 * hf; c < DN; c += 32) {
                 uint32_t r[16];
                 tmem_ld16(t_dq + lane_base + c, r);
                 tmem_wait_ld();
                 if (lane < 16 && q < p.Sq) {
-                    float* dst = p.dq_acc + (rowbase + q) * D + c;
+                    float* dst = p.dq_acc + (sp.rowbase + q) * D + c;
 #pragma unroll
                     for (int g = 0; g < 4; ++g) {
                         if (c + 4 * g < D) {
@@ -325,154 +452,21 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
             }
         };
 
-        // one 32-query half of a step: P^T, dS^T (TMEM), dS (shared), dBias (global)
-        const auto half_step = [&](auto fast, const uint8_t* brow, const float* lsh,
-                                   const float* dlh, int half, int q0, int jn) {
-            uint32_t sr[32], dr[32];
-            tmem_ld32(t_st + 32 * half, sr);
-            tmem_ld32(t_dp + 32 * half, dr);
-            tmem_wait_ld();
-            uint32_t pw[16], dw[16];
-            float* drow = dbias_col + (long long)(q0 + 32 * half) * p.Sk;
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                // queries 32 half + 4c .. +4: half of 16-byte chunk 4 half + c/2 of the key's row
-                const uint2 b2 = *reinterpret_cast<const uint2*>(
-                    brow + (((4 * half + (c >> 1)) ^ (t & 7)) << 4) + (c & 1) * 8);
-                const float2 b01 = __half22float2(*reinterpret_cast<const __half2*>(&b2.x));
-                const float2 b23 = __half22float2(*reinterpret_cast<const __half2*>(&b2.y));
-                const float4 l4 = *reinterpret_cast<const float4*>(lsh + 4 * c);
-                const float4 d4 = *reinterpret_cast<const float4*>(dlh + 4 * c);
-                const float bb[4] = {b01.x * kLog2e, b01.y * kLog2e, b23.x * kLog2e,
-                                     b23.y * kLog2e};
-                const float ll[4] = {l4.x, l4.y, l4.z, l4.w};
-                const float dd[4] = {d4.x, d4.y, d4.z, d4.w};
-                float pv[4], gv[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int j = 4 * c + e;
-                    if constexpr (decltype(fast)::value) {
-                        pv[e] = ex2(fmaf(__uint_as_float(sr[j]), qk_scale, bb[e]) - ll[e]);
-                        gv[e] = pv[e] * (__uint_as_float(dr[j]) - dd[e]);
-                    } else {
-                        const float l2 =
-                            live ? fmaf(__uint_as_float(sr[j]), qk_scale, bb[e]) : masked;
-                        pv[e] = ex2(l2 - ll[e]);
-                        gv[e] = live ? pv[e] * (__uint_as_float(dr[j]) - dd[e]) : 0.f;
-                    }
-                }
-                pw[2 * c] = E::pack(pv[0], pv[1]);
-                pw[2 * c + 1] = E::pack(pv[2], pv[3]);
-                dw[2 * c] = E::pack(gv[0], gv[1]);
-                dw[2 * c + 1] = E::pack(gv[2], gv[3]);
-                if constexpr (DBIAS == kDbiasTma) {
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        rbuf[(32 * half + 4 * c + e) * kBK + t] = gv[e];
-                    }
-                } else if constexpr (DBIAS == kDbiasRed) {
-                    if (key < p.Sk) {
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            if (4 * c + e < jn) {
-                                red_add_f32(drow + (long long)(4 * c + e) * p.Sk, gv[e]);
-                            }
-                        }
-                    }
-                }
-            }
-            tmem_st16(t_st + 16 * half, pw);
-            tmem_st16(t_dp + 16 * half, dw);
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                const int chunk = 4 * half + c;
-                *reinterpret_cast<uint4*>(ds_row + ((chunk ^ (t & 7)) << 4)) =
-                    make_uint4(dw[4 * c], dw[4 * c + 1], dw[4 * c + 2], dw[4 * c + 3]);
-            }
-        };
-
-        // row statistics of a step: thread t < 64 holds lse of query t, t >= 64 delta of t - 64;
-        // loaded one step ahead so that their latency hides behind the current step
-        const auto load_stat = [&](int i) {
-            const int q = i * kBQ + (t & 63);
-            if (i >= nqt || q >= p.Sq) {
-                return t < 64 ? INFINITY : 0.f;
-            }
-            return t < 64 ? p.lse[rowbase + q] : p.delta[rowbase + q];
-        };
-        float stat_next = load_stat(wg);
-        int k = 0;
-        for (int i = wg; i < nqt; i += NWG, ++k) {
-            const int s = i % NS, q0 = i * kBQ, b = k & 1;
-            // this step's row statistics into the group's buffer b
-            float* ls = stat + b * (2 * kBQ);
-            float* dl = ls + kBQ;
-            stat[b * (2 * kBQ) + t] = stat_next;
-            if constexpr (DBIAS == kDbiasTma) {
-                if (t == 0 && k >= 1) {
-                    bulk_wait_read();  // the previous step's reduce has read the dS tile
-                }
-            }
-            named_sync(2 + wg, 128);
-            stat_next = load_stat(i + NWG);
-            if (k >= 1) {
-                // this group's previous step: dQ out of tensor memory before it is reused
-                mbar_wait(&mma_done[wg], (k - 1) & 1, &g_status, kStatusMmaWait, &abort_flag);
-                tc_fence_after();
-                flush_dq(i - NWG);
-            }
-            mbar_wait(&q_full[s], (i / NS) & 1, &g_status, kStatusTmaWait, &abort_flag);
-            mbar_wait(&s_full[wg], k & 1, &g_status, kStatusMmaWait, &abort_flag);
+        // dK (scaled) and dV of item e out of accumulator set e % NB: warpgroup wg takes dK
+        // (even) or dV (odd) and every NP-th 16-column chunk of it
+        const auto store_acc = [&](int e) {
+            const int db = e % NB;
+            mbar_wait(&acc_full[db], (e / NB) & 1, &g_status, kStatusMmaWait, &abort_flag);
             tc_fence_after();
-            const uint8_t* bt = smem + L::STAGE + s * L::STAGE_BYTES + 2 * G::QTILE;
-            const int nq = min(kBQ, p.Sq - q0);
-#pragma unroll 1
-            for (int half = 0; half < 2; ++half) {
-                const uint8_t* brow = bt + t * 128;
-                const int jn = min(32, nq - 32 * half);
-                if (warp_live) {
-                    half_step(std::true_type{}, brow, ls + 32 * half, dl + 32 * half, half, q0, jn);
-                } else {
-                    half_step(std::false_type{}, brow, ls + 32 * half, dl + 32 * half, half, q0,
-                              jn);
-                }
-            }
-            tmem_wait_st();
-            fence_async_smem();
-            tc_fence_before();
-            mbar_arrive(&p_ready[wg]);
-            if constexpr (DBIAS == kDbiasTma) {
-                // the whole fp32 dS tile in one bulk reduce-add (rows past Sq, keys past Sk clip)
-                named_sync(2 + wg, 128);
-                if (t == 0) {
-                    tma_reduce_add_3d(&tdb, rbuf, k0, q0, h);
-                }
-            }
-        }
-        if constexpr (DBIAS == kDbiasTma) {
-            if (t == 0) {
-                bulk_wait_all();
-            }
-        }
-        if (k >= 1) {
-            mbar_wait(&mma_done[wg], (k - 1) & 1, &g_status, kStatusMmaWait, &abort_flag);
-            tc_fence_after();
-            flush_dq(wg + (k - 1) * NWG);
-        }
-        // dK (scaled) and dV once the last step's accumulations are done
-        const int last = nqt - 1;
-        mbar_wait(&mma_done[last % NWG], (last / NWG) & 1, &g_status, kStatusMmaWait,
-                  &abort_flag);
-        tc_fence_after();
-        const long long krow = ((long long)n * p.H + h) * p.Sk + key;
-        for (int which = 0; which < 2; ++which) {
-            if (NWG == 2 && which != wg) {
-                continue;
-            }
-            const uint32_t acc = tmem + (which == 0 ? G::T_DK : G::T_DV) + lane_base;
+            const StepPos it = item_pos(p, nkt, e);
+            const int key = it.k0 + t;
+            const long long krow = ((long long)it.n * p.H + it.h) * p.Sk + key;
+            const int which = wg & 1;
+            const uint32_t acc = tmem + G::T_ACC + db * 2 * G::DN + (which == 0 ? G::DN : 0) +
+                                 lane_base;
             T* dst = reinterpret_cast<T*>(which == 0 ? p.dk : p.dv) + krow * D;
             const float mul = which == 0 ? p.scale : 1.f;
-            for (int c = 0; c < DN; c += 16) {
+            for (int c = 16 * (wg >> 1); c < DN; c += 16 * NP) {
                 uint32_t r[16];
                 tmem_ld16(acc + c, r);
                 tmem_wait_ld();
@@ -484,20 +478,197 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
                             uint4 w;
                             uint32_t* pw = &w.x;
 #pragma unroll
-                            for (int e = 0; e < 4; ++e) {
-                                pw[e] = E::pack(__uint_as_float(r[8 * hh + 2 * e]) * mul,
-                                                __uint_as_float(r[8 * hh + 2 * e + 1]) * mul);
+                            for (int e2 = 0; e2 < 4; ++e2) {
+                                pw[e2] = E::pack(__uint_as_float(r[8 * hh + 2 * e2]) * mul,
+                                                 __uint_as_float(r[8 * hh + 2 * e2 + 1]) * mul);
                             }
                             *reinterpret_cast<uint4*>(dst + c8) = w;
                         }
                     }
                 }
             }
+            tc_fence_before();
+            mbar_arrive(&acc_empty[db]);
+        };
+
+        // per-item state of this worker's key
+        int cur_item = -1;
+        bool live = false, warp_live = false;
+        float* dbias_col = nullptr;
+
+        // this warpgroup's 32 queries of a step, in two chunks of 16: P^T, dS^T (TMEM, packed
+        // over the chunk's own S^T/dP^T columns), dS (shared), dBias
+        const auto half_step = [&](auto fast, const uint8_t* brow, const float* lsh,
+                                   const float* dlh, int q0, int jn, int key) {
+            float* drow = dbias_col + (long long)(q0 + 32 * hf) * p.Sk;
+#pragma unroll
+            for (int cc = 0; cc < 2; ++cc) {
+                uint32_t sr[16], dr[16];
+                tmem_ld16(t_st + 16 * cc, sr);
+                tmem_ld16(t_dp + 16 * cc, dr);
+                tmem_wait_ld();
+                uint32_t pw[8], dw[8];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const int qc = 16 * cc + 4 * c;  // query offset within the half
+                    // queries 32 hf + qc .. +4: half of 16-byte chunk 4 hf + qc/8 of the key's row
+                    const uint2 b2 = *reinterpret_cast<const uint2*>(
+                        brow + (((4 * hf + (qc >> 3)) ^ (t & 7)) << 4) + (c & 1) * 8);
+                    const float2 b01 = __half22float2(*reinterpret_cast<const __half2*>(&b2.x));
+                    const float2 b23 = __half22float2(*reinterpret_cast<const __half2*>(&b2.y));
+                    const float4 l4 = *reinterpret_cast<const float4*>(lsh + qc);
+                    const float4 d4 = *reinterpret_cast<const float4*>(dlh + qc);
+                    // log2e * bias - lse, one FMA per element
+                    const float bl[4] = {fmaf(b01.x, kLog2e, -l4.x), fmaf(b01.y, kLog2e, -l4.y),
+                                         fmaf(b23.x, kLog2e, -l4.z), fmaf(b23.y, kLog2e, -l4.w)};
+                    const float ll[4] = {l4.x, l4.y, l4.z, l4.w};
+                    const float dd[4] = {d4.x, d4.y, d4.z, d4.w};
+                    float pv[4], gv[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int j = 4 * c + e;
+                        if constexpr (decltype(fast)::value) {
+                            pv[e] = ex2(fmaf(__uint_as_float(sr[j]), qk_scale, bl[e]));
+                            gv[e] = pv[e] * (__uint_as_float(dr[j]) - dd[e]);
+                        } else {
+                            const float l2 = live ? fmaf(__uint_as_float(sr[j]), qk_scale, bl[e])
+                                                  : masked - ll[e];
+                            pv[e] = ex2(l2);
+                            gv[e] = live ? pv[e] * (__uint_as_float(dr[j]) - dd[e]) : 0.f;
+                        }
+                    }
+                    pw[2 * c] = E::pack(pv[0], pv[1]);
+                    pw[2 * c + 1] = E::pack(pv[2], pv[3]);
+                    dw[2 * c] = E::pack(gv[0], gv[1]);
+                    dw[2 * c + 1] = E::pack(gv[2], gv[3]);
+                    if constexpr (DBIAS == kDbiasTma) {
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            rbuf[(qc + e) * kBK + t] = gv[e];
+                        }
+                    } else if constexpr (DBIAS == kDbiasRed) {
+                        if (key < p.Sk) {
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                if (qc + e < jn) {
+                                    red_add_f32(drow + (long long)(qc + e) * p.Sk, gv[e]);
+                                }
+                            }
+                        }
+                    }
+                }
+                tmem_st8(t_st + 8 * cc, pw);
+                tmem_st8(t_dp + 8 * cc, dw);
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    const int chunk = 4 * hf + 2 * cc + c;
+                    *reinterpret_cast<uint4*>(ds_row + ((chunk ^ (t & 7)) << 4)) =
+                        make_uint4(dw[4 * c], dw[4 * c + 1], dw[4 * c + 2], dw[4 * c + 3]);
+                }
+            }
+        };
+
+        // row statistics of this warpgroup's 32 queries: thread t < 32 holds lse of query t,
+        // 32 <= t < 64 delta of query t - 32; loaded one step ahead to hide their latency
+        const auto load_stat = [&](const StepCursor& c) {
+            if (c.gi >= total) {
+                return t < 32 ? INFINITY : 0.f;
+            }
+            const StepPos& sp = c.pos;
+            const int q = sp.q0 + 32 * hf + (t & 31);
+            if (q >= p.Sq) {
+                return t < 32 ? INFINITY : 0.f;
+            }
+            return t < 32 ? p.lse[sp.rowbase + q] : p.delta[sp.rowbase + q];
+        };
+        // cur: this step; nxt: this set's next step (its statistics are prefetched); prev: the
+        // set's previous step (its dQ is flushed at the start of this one)
+        StepCursor cur, nxt;
+        cur.start(p, nkt, nqt, set);
+        nxt = cur;
+        nxt.advance(p, nkt, nqt, NP);
+        StepPos prev = cur.pos;
+        float stat_next = t < 64 ? load_stat(cur) : 0.f;
+        int k = 0, stored = 0;  // this set's steps so far; items whose dK/dV this group stored
+        for (; cur.gi < total; ++k) {
+            const int gi = cur.gi, s = gi % NS, b = k & 1, j = cur.j;
+            const StepPos sp = cur.pos;
+            // this step's row statistics into the warpgroup's buffer b
+            float* ls = stat + b * 64;
+            float* dl = ls + 32;
+            if (t < 64) {
+                stat[b * 64 + t] = stat_next;
+            }
+            if constexpr (DBIAS == kDbiasTma) {
+                if (t == 0 && k >= 1) {
+                    bulk_wait_read();  // the previous step's reduce has read the dS rows
+                }
+            }
+            named_sync(1 + wg, 128);
+            if (t < 64) {
+                stat_next = load_stat(nxt);
+            }
+            if (k >= 1) {
+                // this set's previous step: dQ out of tensor memory before it is reused
+                mbar_wait(&dq_done[set], (k - 1) & 1, &g_status, kStatusMmaWait, &abort_flag);
+                tc_fence_after();
+                flush_dq(prev);
+            }
+            if (j != cur_item) {
+                cur_item = j;
+                const int key = sp.k0 + t;
+                live = key < p.Sk && p.kmask[(long long)sp.n * p.Sk + key] != 0;
+                warp_live = __all_sync(0xffffffffu, live);
+                dbias_col = p.dbias + (long long)sp.h * p.Sq * p.Sk + key;
+            }
+            mbar_wait(&q_full[s], (gi / NS) & 1, &g_status, kStatusTmaWait, &abort_flag);
+            mbar_wait(&s_full[set], k & 1, &g_status, kStatusMmaWait, &abort_flag);
+            tc_fence_after();
+            const uint8_t* brow = smem + L::STAGE + s * L::STAGE_BYTES + 2 * G::QTILE + t * 128;
+            const int jn = min(32, p.Sq - sp.q0 - 32 * hf);
+            if (warp_live) {
+                half_step(std::true_type{}, brow, ls, dl, sp.q0, jn, sp.k0 + t);
+            } else {
+                half_step(std::false_type{}, brow, ls, dl, sp.q0, jn, sp.k0 + t);
+            }
+            tmem_wait_st();
+            fence_async_smem();
+            tc_fence_before();
+            mbar_arrive(&p_ready[set]);
+            if constexpr (DBIAS == kDbiasTma) {
+                // this warpgroup's 32 fp32 dS rows in one bulk reduce-add (rows past Sq and
+                // keys past Sk clip)
+                named_sync(1 + wg, 128);
+                if (t == 0 && jn > 0) {
+                    tma_reduce_add_3d(&tdb, rbuf, sp.k0, sp.q0 + 32 * hf, sp.h);
+                }
+            }
+            // the accumulators of the items before this one: their last MMAs were issued a
+            // step ago, so they are done or nearly so
+            while (stored < j) {
+                store_acc(stored++);
+            }
+            prev = sp;
+            cur = nxt;
+            nxt.advance(p, nkt, nqt, NP);
+        }
+        if constexpr (DBIAS == kDbiasTma) {
+            if (t == 0) {
+                bulk_wait_all();
+            }
+        }
+        if (k >= 1) {
+            mbar_wait(&dq_done[set], (k - 1) & 1, &g_status, kStatusMmaWait, &abort_flag);
+            tc_fence_after();
+            flush_dq(prev);
+        }
+        while (stored < J) {
+            store_acc(stored++);
         }
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == MMA_WARP) {
+    if (warp == G::MMA_A) {
         tc_fence_after();
         tmem_dealloc(tmem, G::ALLOC);
     }
@@ -611,7 +782,14 @@ cudaError_t launch_main(cudaStream_t stream, const CUtensorMap* maps, const BwdP
         }
         attr_done[dev] = true;
     }
-    const dim3 grid((p.Sk + kBK - 1) / kBK, p.H, p.N);
+    // persistent: one CTA per SM, each looping over work items
+    static int sms[kMaxDevices] = {};
+    if (dev < kMaxDevices && sms[dev] == 0) {
+        cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    }
+    const int nsm = dev < kMaxDevices && sms[dev] > 0 ? sms[dev] : 148;
+    const long long items = (long long)((p.Sk + kBK - 1) / kBK) * p.H * p.N;  // < 2^31 / nqt
+    const dim3 grid((unsigned)std::min<long long>(items, nsm));
     kern<<<grid, BGeom<DP>::THREADS, smem, stream>>>(maps[0], maps[1], maps[2], maps[3], maps[4],
                                                      maps[5], p);
     return cudaGetLastError();
@@ -700,6 +878,9 @@ extern "C" int cflk_volta_mma_bwd(void* stream_, int dtype, const void* q, const
     if (D != 8 && D != 16 && D != 24 && D != 32 && D != 48 && D != 64 && D != 96) {
         return fail(kInvalidArgument, "volta_mma_bwd: unsupported head dim");
     }
+    if (((Sk + kBK - 1) / kBK) * H * N * ((Sq + kBQ - 1) / kBQ) >= (int64_t(1) << 31)) {
+        return fail(kInvalidArgument, "volta_mma_bwd: more than 2^31 (key tile, query step) pairs");
+    }
     const Workspace ws = Workspace::of(N, H, Sq, Sk, D);
     if (workspace_bytes < ws.total || (ws.total > 0 && workspace == nullptr) ||
         (reinterpret_cast<uintptr_t>(workspace) & 255) != 0) {
@@ -763,7 +944,7 @@ extern "C" int cflk_volta_mma_bwd(void* stream_, int dtype, const void* q, const
     if (want_dbias && Sk % 4 == 0 && (reinterpret_cast<uintptr_t>(dbias) & 15) == 0) {
         const uint64_t ddb[3] = {(uint64_t)Sk, (uint64_t)Sq, (uint64_t)H};
         const uint64_t sdb[2] = {(uint64_t)Sk, (uint64_t)Sq * (uint64_t)Sk};
-        const uint32_t boxdb[3] = {(uint32_t)kBK, (uint32_t)kBQ, 1};
+        const uint32_t boxdb[3] = {(uint32_t)kBK, (uint32_t)(kBQ / 2), 1};
         if (encode_tiled(&maps[5], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, 3, dbias, ddb, sdb, boxdb,
                          CU_TENSOR_MAP_SWIZZLE_NONE)) {
             dbias_mode = kDbiasTma;

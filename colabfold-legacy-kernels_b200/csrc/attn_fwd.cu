@@ -44,7 +44,8 @@ constexpr int kBQ = 128;   // query rows per CTA (= TMEM lanes)
 constexpr int kBK = 128;   // keys per tile
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kMaskedLogit = -1.0e4f;
-constexpr float kRescaleThreshold = 8.0f;  // log2 units: P stays below 2^8 between rescales
+constexpr float kRescaleThreshold = 8.0f;
+constexpr int kFmaExpEvery = 4;  // share of a row's exponentials computed on the FMA pipe  // log2 units: P stays below 2^8 between rescales
 
 struct FwdParams {
     const void* bias;
@@ -107,6 +108,28 @@ struct Smem {
     static constexpr int BYTES = END + 1024;  // slack for the 1024-byte alignment
     static_assert(BYTES + 256 <= 227 * 1024, "shared memory");
 };
+
+// 2^a for two lanes on the FMA pipe instead of the special-function unit, which the other
+// exponentials of a row keep busy. Range reduction a = n + f with n = rint(a) (adding and
+// subtracting 1.5 * 2^23 rounds to an integer that lands in the low mantissa bits), 2^f on
+// [-0.5, 0.5] by a cubic fitted here by weighted least squares to the relative error (at most
+// 7.5e-5 in fp32, far below the 16-bit rounding of P), and 2^n added into the exponent field.
+// a is clamped below at -125 (2^-125 stands in for 0: it is under every P that matters by more
+// than a bf16 ulp); a never exceeds the lazy-rescale threshold.
+__device__ __forceinline__ float2 ex2_fma(float a0, float a1) {
+    constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+    const uint64_t a = pk2(fmaxf(a0, -125.f), fmaxf(a1, -125.f));
+    const uint64_t t = add2(a, pk2(kRound, kRound));
+    const uint64_t n = add2(t, pk2(-kRound, -kRound));
+    const uint64_t f = fma2(n, pk2(-1.f, -1.f), a);
+    uint64_t q = fma2(f, pk2(0.05517160892486572f, 0.05517160892486572f),
+                      pk2(0.2426111102104187f, 0.2426111102104187f));
+    q = fma2(q, f, pk2(0.6932609677314758f, 0.6932609677314758f));
+    q = fma2(q, f, pk2(0.9999280571937561f, 0.9999280571937561f));
+    const float2 tf = upk2(t), qf = upk2(q);
+    return make_float2(__int_as_float(__float_as_int(qf.x) + (__float_as_int(tf.x) << 23)),
+                       __int_as_float(__float_as_int(qf.y) + (__float_as_int(tf.y) << 23)));
+}
 
 // 8 consecutive 16-bit values of the bias tile row r, keys [8i, 8i+8): region i/8, chunk i%8
 __device__ __forceinline__ uint4 bias_chunk(const uint8_t* stage, int r, int i) {
@@ -491,12 +514,22 @@ __global__ void __launch_bounds__(Geometry<DP>::THREADS, 1)
                 const bool all_live = (lw.x & lw.y & lw.z & lw.w) == 0xffffffffu;
 
                 // logits of this row, scale q.k + bias (natural units; log2e is applied with
-                // the max subtracted), computed two at a time
+                // the max subtracted), computed two at a time over the loaded S in place
                 float sv[kBK];
+                {
+                    uint32_t* sr = reinterpret_cast<uint32_t*>(sv);
+#pragma unroll
+                    for (int cc = 0; cc < 4; ++cc) {
+                        tmem_ld32(t_s + 32 * cc,
+                                  *reinterpret_cast<uint32_t(*)[32]>(sr + 32 * cc));
+                    }
+                    tmem_wait_ld();
+                    // all of S is in registers: the next S may overwrite it
+                    tc_fence_before();
+                    mbar_arrive(&bar.s_free[w]);
+                }
 #pragma unroll
                 for (int cc = 0; cc < 4; ++cc) {
-                    uint32_t r[32];
-                    tmem_ld32(t_s + 32 * cc, r);
                     uint32_t bw[16];
                     if constexpr (BIAS_TMA) {
                         const uint8_t* stage = smem + L::STAGE + st * L::STAGE_BYTES + L::KV_BYTES;
@@ -520,17 +553,10 @@ __global__ void __launch_bounds__(Geometry<DP>::THREADS, 1)
                             bw[i] = lo | (hi << 16);
                         }
                     }
-                    tmem_wait_ld();
-                    if (cc == 3) {
-                        // all of S is in registers: the next S may overwrite it
-                        tc_fence_before();
-                        mbar_arrive(&bar.s_free[w]);
-                    }
 #pragma unroll
                     for (int i = 0; i < 16; ++i) {
                         const float2 b = E::unpack(bw[i]);
-                        const float2 y = upk2(fma2(pk2(__uint_as_float(r[2 * i]),
-                                                       __uint_as_float(r[2 * i + 1])),
+                        const float2 y = upk2(fma2(pk2(sv[32 * cc + 2 * i], sv[32 * cc + 2 * i + 1]),
                                                    scale2, pk2(b.x, b.y)));
                         sv[32 * cc + 2 * i] = y.x;
                         sv[32 * cc + 2 * i + 1] = y.y;
@@ -543,12 +569,20 @@ __global__ void __launch_bounds__(Geometry<DP>::THREADS, 1)
                         sv[i] = lv ? sv[i] : (i < n_in ? kMaskedLogit : -INFINITY);
                     }
                 }
-                float m_tile = sv[0];
+                // row max in a tree of eight partial maxima (short dependency chains)
+                float mp[8];
 #pragma unroll
-                for (int i = 1; i + 1 < kBK; i += 2) {
-                    m_tile = max3(m_tile, sv[i], sv[i + 1]);
+                for (int a = 0; a < 8; ++a) {
+                    mp[a] = max3(sv[16 * a], sv[16 * a + 1], sv[16 * a + 2]);
+#pragma unroll
+                    for (int i = 3; i < 15; i += 2) {
+                        mp[a] = max3(mp[a], sv[16 * a + i], sv[16 * a + i + 1]);
+                    }
+                    mp[a] = fmaxf(mp[a], sv[16 * a + 15]);
                 }
-                m_tile = fmaxf(m_tile, sv[kBK - 1]) * kLog2e;  // log2 units
+                const float m_tile =
+                    max3(max3(mp[0], mp[1], mp[2]), max3(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7])) *
+                    kLog2e;  // log2 units
 
                 if (c > 0) {
                     // the previous PV is done: P's columns are free and O is final
@@ -579,7 +613,7 @@ __global__ void __launch_bounds__(Geometry<DP>::THREADS, 1)
 
                 // P = exp2(log2e y - m) as 16-bit pairs in P's columns
                 const uint64_t neg_m2 = pk2(-m_run, -m_run);
-                uint64_t l2 = pk2(0.f, 0.f);
+                uint64_t l2[4];  // four partial sums (short dependency chains)
 #pragma unroll
                 for (int cc = 0; cc < 4; ++cc) {
                     uint32_t pw[16];
@@ -587,13 +621,22 @@ __global__ void __launch_bounds__(Geometry<DP>::THREADS, 1)
                     for (int i = 0; i < 16; ++i) {
                         const float2 a = upk2(fma2(
                             pk2(sv[32 * cc + 2 * i], sv[32 * cc + 2 * i + 1]), log2e2, neg_m2));
-                        const float e0 = ex2(a.x), e1 = ex2(a.y);
-                        l2 = add2(l2, pk2(e0, e1));
+                        // one pair in kFmaExpEvery on the FMA pipe, the rest on the MUFU
+                        float e0, e1;
+                        if (i % kFmaExpEvery == kFmaExpEvery - 1) {
+                            const float2 e = ex2_fma(a.x, a.y);
+                            e0 = e.x;
+                            e1 = e.y;
+                        } else {
+                            e0 = ex2(a.x);
+                            e1 = ex2(a.y);
+                        }
+                        l2[i & 3] = cc == 0 && i < 4 ? pk2(e0, e1) : add2(l2[i & 3], pk2(e0, e1));
                         pw[i] = E::pack(e0, e1);
                     }
                     tmem_st16(t_p + 16 * cc, pw);
                 }
-                const float2 lt = upk2(l2);
+                const float2 lt = upk2(add2(add2(l2[0], l2[1]), add2(l2[2], l2[3])));
                 l_run += lt.x + lt.y;
                 tmem_wait_st();
                 tc_fence_before();

@@ -743,10 +743,22 @@ cudaError_t launch_typed(cudaStream_t stream, const CUtensorMap& tq, const CUten
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < kMaxDevices && !attr_done[dev]) {
-        const cudaError_t e =
+        cudaError_t e =
             cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) {
             return e;
+        }
+        // the warpgroups' register hand-off must fit what the kernel is launched with, or a
+        // setmaxnreg.inc would wait for registers that never come: refuse instead
+        using G = Geometry<DP>;
+        if constexpr (G::NSEQ == 2) {
+            cudaFuncAttributes fa;
+            if ((e = cudaFuncGetAttributes(&fa, kern)) != cudaSuccess) {
+                return e;
+            }
+            if (fa.numRegs * G::THREADS < (int)(2 * 128 * G::SOFTMAX_REGS + 128 * G::OTHER_REGS)) {
+                return cudaErrorInvalidConfiguration;
+            }
         }
         attr_done[dev] = true;
     }

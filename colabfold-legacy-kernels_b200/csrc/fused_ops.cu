@@ -25,18 +25,17 @@ using namespace fused;
 // ---------------------------------------------------------------------------------------------
 // the pipeline
 // ---------------------------------------------------------------------------------------------
-// The accumulators live in a ring of kSlots blocks of kSlotCols tensor-memory columns: the MMA
+// The accumulators live in a ring of Op::kSlots blocks of Op::kSlotCols tensor-memory columns: the MMA
 // warp fills block j+1.. while the workers drain block j, so neither side waits for a whole
 // tile. Op supplies: T, Args (M, w_bytes, param_floats, eps), keep(), kOther, X_BYTES,
 // RED_FLOATS, nblocks(), load_params, load_weights, load_x, issue_block, prologue,
-// epilogue_block, padding, Regs.
-constexpr int kSlots = 4;
-constexpr int kSlotCols = 128;
+// epilogue_block, prefetch_block, padding, Regs.
 
 template <class Op>
 __global__ void __launch_bounds__(kThreads, 1)
     row_tile_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tw0,
                     const __grid_constant__ CUtensorMap tw1, const typename Op::Args a) {
+    constexpr int kSlots = Op::kSlots, kSlotCols = Op::kSlotCols;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -145,7 +144,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         const int g = warp >> 2, t = ((warp & 3) << 5) | lane;
         const uint32_t lane_base = tmem_lane_base(warp);
-        typename Op::Regs regs;
+        typename Op::Regs regs{};
         int c = 0, q = 0;
         for (int cursor = blockIdx.x; cursor < ntiles; cursor += gridDim.x) {
             const int m0 = cursor * BM;
@@ -165,6 +164,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_arrive(&a_ready[s]);
             for (int j = 0; j < nb; ++j, ++q) {
                 const int slot = q % kSlots;
+                // global inputs of the block's epilogue start loading before the MMA wait
+                Op::prefetch_block(a, t, g, m0, j, regs);
                 mbar_wait(&acc_full[slot], (q / kSlots) & 1, &g_status, kStatusMmaWait,
                           &abort_flag);
                 tc_fence_after();
@@ -222,6 +223,18 @@ __device__ __forceinline__ void mma_rows(uint32_t d, uint32_t a_base, uint32_t w
     }
 }
 
+// D[128 x 128] = W[c0, c0 + 128) A^T for W [rows][K] staged by load_weight and the row tile A:
+// the transposed product, TMEM lanes are output channels and columns are the tile's rows
+__device__ __forceinline__ void mma_cols(uint32_t d, uint32_t w_base, int rows, int c0,
+                                         uint32_t a_base, int K, bool bf16) {
+    const uint32_t id = idesc_f16(bf16, 128, 128, false, false);
+    for (int k = 0; k < K / 16; ++k) {
+        const int at = k >> 2, off = (k & 3) * 32;
+        mma_ss(d, desc_k128(w_base + at * rows * 128 + c0 * 128 + off),
+               desc_k128(a_base + at * ATOM + off), id, k > 0 ? 1u : 0u);
+    }
+}
+
 // ---------------------------------------------------------------------------------------------
 // VoltaLnGdp: left/right [CI, M] = max(mask, 0) * (y wp + bp) * sigmoid(y wg + bg), y = LN(x)
 // ---------------------------------------------------------------------------------------------
@@ -232,15 +245,23 @@ struct LnGdpOp {
     static constexpr int P = 2 * CI;
     static constexpr int X_BYTES = K * BM * 2;
     static constexpr float kOther = 0.f;
-    static constexpr int RED_FLOATS = 4 * BM;
+    // LN sums, then the tile's row mask max(mask, 0) in two buffers (tile parity)
+    static constexpr int RED_FLOATS = 4 * BM + 2 * BM;
+    // the outputs are channel major, so the product is computed transposed (lanes = channels):
+    // a block is 128 channels, the projection in the slot's columns [0, 128) and the gate in
+    // [128, 256), one column per row of the tile
+    static constexpr int kSlots = 2, kSlotCols = 256;
     struct Args {
         const T *x, *wpT, *bp, *wgT, *bg, *mask;
         const float *scale, *offset;
         T *left, *right;
-        int M, w_bytes, param_floats;
+        int M, w_bytes, param_floats, vec_store;
         float eps;
     };
-    struct Regs {};
+    struct Regs {
+        const float* maskv;  // this tile's row mask (shared memory)
+        int parity;
+    };
     static __device__ const T* keep(const Args& a) { return a.mask; }
     // scale [K], offset [K], bp [P], bg [P]
     static __device__ void load_params(const Args& a, float* sp, int tid) {
@@ -263,39 +284,73 @@ struct LnGdpOp {
                                   uint64_t* bar, int m0) {
         load_rows_tile(tx, dst, bar, K, m0);
     }
-    // block j: output channels [64j, 64j+64) of the P; the projection in the slot's columns
-    // [0, 64), the gate in [64, 128)
-    static __device__ int nblocks(const Args&) { return P / 64; }
+    // block j: output channels [128j, 128j + 128) of the P
+    static __device__ int nblocks(const Args&) { return P / 128; }
     static __device__ void issue_block(const Args& a, uint32_t xa, uint32_t wa, uint32_t acc,
                                        int j) {
-        mma_rows(acc, xa, wa, P, K, 64 * j, 64, E::kBf16, false);
-        mma_rows(acc + 64, xa, wa + P * K * 2, P, K, 64 * j, 64, E::kBf16, false);
+        mma_cols(acc, wa, P, 128 * j, xa, K, E::kBf16);
+        mma_cols(acc + 128, wa + P * K * 2, P, 128 * j, xa, K, E::kBf16);
     }
     static __device__ void prologue(const Args& a, uint8_t* stage, const float* sp, float* red,
-                                    int t, int g, int m0, Regs&) {
+                                    int t, int g, int m0, Regs& regs) {
+        // the row mask of the tile, visible to all workers after the LayerNorm's barriers;
+        // two buffers, as the epilogue of the previous tile may still read the other one
+        float* mv = red + 4 * BM + regs.parity * BM;
+        if (g == 0) {
+            const int m = m0 + t;
+            mv[t] = m < a.M ? fmaxf(E::to_f(a.mask[m]), 0.f) : 0.f;
+        }
+        regs.maskv = mv;
+        regs.parity ^= 1;
         ln_rows_half<T, K>(stage, t, g, sp, sp + K, a.eps, red, nullptr, nullptr);
     }
-    // worker half g: channels 64j + 32g + [0, 32), into left or right (channel major)
+    static __device__ void prefetch_block(const Args&, int, int, int, int, Regs&) {}
+    // worker (g, t): channel 128j + t (TMEM lane t), the tile's rows [64g, 64g + 64) in two
+    // runs of 32, each stored as 64 contiguous bytes of the channel-major output
     static __device__ void epilogue_block(const Args& a, uint32_t acc, const float* sp, int t,
-                                          int g, int m0, int j, Regs&) {
-        const int m = m0 + t;
-        const int ch0 = 64 * j + 32 * g;
-        uint32_t pr[32], gr[32];
-        tmem_ld32(acc + 32 * g, pr);
-        tmem_ld32(acc + 64 + 32 * g, gr);
-        tmem_wait_ld();
-        if (m >= a.M) {
-            return;
-        }
-        const float mv = fmaxf(E::to_f(a.mask[m]), 0.f);
-        T* out = ch0 < CI ? a.left + (long long)ch0 * a.M : a.right + (long long)(ch0 - CI) * a.M;
-        const float* bp = sp + 2 * K + ch0;
-        const float* bg = sp + 2 * K + P + ch0;
+                                          int g, int m0, int j, Regs& regs) {
+        const int ch = 128 * j + t;
+        const float bpv = sp[2 * K + ch], bgv = sp[2 * K + P + ch];
+        T* out = ch < CI ? a.left + (long long)ch * a.M : a.right + (long long)(ch - CI) * a.M;
+#pragma unroll 1
+        for (int cc = 0; cc < 2; ++cc) {
+            const int r0 = 64 * g + 32 * cc;
+            uint32_t pr[32], gr[32];
+            tmem_ld32(acc + r0, pr);
+            tmem_ld32(acc + 128 + r0, gr);
+            tmem_wait_ld();
+            const int m = m0 + r0;
+            if (m >= a.M) {
+                continue;
+            }
+            uint32_t w[16];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-            const float pv = __uint_as_float(pr[i]) + bp[i];
-            const float gv = __uint_as_float(gr[i]) + bg[i];
-            out[(long long)i * a.M + m] = E::from_f(mv * pv * sigmoid_fast(gv));
+            for (int q = 0; q < 8; ++q) {
+                const float4 mk = *reinterpret_cast<const float4*>(regs.maskv + r0 + 4 * q);
+                const float mm[4] = {mk.x, mk.y, mk.z, mk.w};
+                float o[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int i = 4 * q + e;
+                    o[e] = mm[e] * (__uint_as_float(pr[i]) + bpv) *
+                           sigmoid_fast(__uint_as_float(gr[i]) + bgv);
+                }
+                w[2 * q] = E::pack(o[0], o[1]);
+                w[2 * q + 1] = E::pack(o[2], o[3]);
+            }
+            if (a.vec_store && m + 32 <= a.M) {
+                uint4* dst = reinterpret_cast<uint4*>(out + m);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    dst[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+                }
+            } else {
+                for (int i = 0; i < 32 && m + i < a.M; ++i) {
+                    const uint32_t ww = w[i >> 1];
+                    const uint16_t hv = (i & 1) ? (uint16_t)(ww >> 16) : (uint16_t)(ww & 0xffffu);
+                    reinterpret_cast<uint16_t*>(out)[m + i] = hv;
+                }
+            }
         }
     }
     static __device__ void padding(const Args& a, int m0, int t, int g) {
@@ -319,6 +374,7 @@ template <typename T_, int K, bool LN>
 struct ProjOp {
     using T = T_;
     using E = Elem<T>;
+    static constexpr int kSlots = 4, kSlotCols = 128;
     static constexpr int X_BYTES = K * BM * 2;
     static constexpr float kOther = -1.f;
     static constexpr int RED_FLOATS = 4 * BM + 16 * BM;  // LN sums + per-head halves
@@ -330,7 +386,9 @@ struct ProjOp {
         int w_bytes, param_floats;
         float eps;
     };
-    struct Regs {};
+    struct Regs {
+        uint4 res[8];  // the residual part of the next block (up to 64 columns)
+    };
     static __device__ const T* keep(const Args& a) { return a.keep; }
     // scale [K], offset [K], b [n], wb [8][K]
     static __device__ void load_params(const Args& a, float* sp, int tid) {
@@ -390,30 +448,53 @@ struct ProjOp {
             }
         }
     }
+    // the residual of worker half g's columns of block j, loaded ahead of the MMA wait
+    static __device__ void prefetch_block(const Args& a, int t, int g, int m0, int j,
+                                          Regs& regs) {
+        const int m = m0 + t;
+        if (a.residual == nullptr || m >= a.M) {
+            return;
+        }
+        const int width = a.n - 128 * j < 128 ? a.n - 128 * j : 128;
+        const int half = width / 2;
+        const uint4* rr = reinterpret_cast<const uint4*>(a.residual + (long long)m * a.ldp +
+                                                         128 * j + g * half);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            if (8 * i < half) {
+                regs.res[i] = rr[i];
+            }
+        }
+    }
     // worker half g: columns 128j + g w/2 + [0, w/2) of the block's width w
     static __device__ void epilogue_block(const Args& a, uint32_t acc, const float* sp, int t,
-                                          int g, int m0, int j, Regs&) {
+                                          int g, int m0, int j, Regs& regs) {
         const int m = m0 + t;
         const int width = a.n - 128 * j < 128 ? a.n - 128 * j : 128;
         const int half = width / 2;
         const float* b = sp + 2 * K + 128 * j;
         T* orow = a.out + (long long)m * a.ldp + 128 * j;
-        const T* rrow =
-            a.residual != nullptr ? a.residual + (long long)m * a.ldp + 128 * j : nullptr;
-#pragma unroll 1
-        for (int c0 = g * half; c0 < (g + 1) * half; c0 += 16) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int c0 = g * half + 16 * i;
+            if (16 * i >= half) {
+                break;
+            }
             uint32_t r[16];
             tmem_ld16(acc + c0, r);
             tmem_wait_ld();
             if (m < a.M) {
                 float v[16];
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    v[j] = __uint_as_float(r[j]) + b[c0 + j];
+                for (int q = 0; q < 4; ++q) {
+                    const float4 bb = *reinterpret_cast<const float4*>(b + c0 + 4 * q);
+                    v[4 * q] = __uint_as_float(r[4 * q]) + bb.x;
+                    v[4 * q + 1] = __uint_as_float(r[4 * q + 1]) + bb.y;
+                    v[4 * q + 2] = __uint_as_float(r[4 * q + 2]) + bb.z;
+                    v[4 * q + 3] = __uint_as_float(r[4 * q + 3]) + bb.w;
                 }
-                if (rrow != nullptr) {
-                    const uint4 q0 = *reinterpret_cast<const uint4*>(rrow + c0);
-                    const uint4 q1 = *reinterpret_cast<const uint4*>(rrow + c0 + 8);
+                if (a.residual != nullptr) {
+                    const uint4 q0 = regs.res[2 * i], q1 = regs.res[2 * i + 1];
                     const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
                     for (int e = 0; e < 8; ++e) {
@@ -462,6 +543,7 @@ template <typename T_, int C, int CA, int O, bool ADD>
 struct TrimulOp {
     using T = T_;
     using E = Elem<T>;
+    static constexpr int kSlots = 4, kSlotCols = 128;
     static constexpr int X_BYTES = (C + CA) * BM * 2;
     static constexpr int XOFF = C * BM * 2;  // x's atoms after Y's
     static constexpr float kOther = -1.f;
@@ -474,7 +556,9 @@ struct TrimulOp {
         int M, w_bytes, param_floats;
         float eps;
     };
-    struct Regs {};
+    struct Regs {
+        uint4 res[4];  // x of worker half g's 32 channels of the next block (add_input)
+    };
     static __device__ const T* keep(const Args& a) { return a.keep; }
     // in_scale [CA], in_offset [CA], ln_scale [C], ln_offset [C], bo [O], bg [O]
     static __device__ void load_params(const Args& a, float* sp, int tid) {
@@ -555,14 +639,28 @@ struct TrimulOp {
         // then LN_in(x) in place on the TMA-loaded x atoms
         ln_rows_half<T, CA>(stage + XOFF, t, g, sp, sp + CA, a.eps, red, nullptr, nullptr);
     }
+    // x of worker half g's channels of block j (add_input), loaded ahead of the MMA wait
+    static __device__ void prefetch_block(const Args& a, int t, int g, int m0, int j,
+                                          Regs& regs) {
+        const int m = m0 + t;
+        if constexpr (ADD) {
+            if (m < a.M) {
+                const uint4* xr =
+                    reinterpret_cast<const uint4*>(a.x + (long long)m * CA + 64 * j + 32 * g);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    regs.res[i] = xr[i];
+                }
+            }
+        }
+    }
     // worker half g: channels 64j + 32g + [0, 32)
     static __device__ void epilogue_block(const Args& a, uint32_t acc, const float* sp, int t,
-                                          int g, int m0, int j, Regs&) {
+                                          int g, int m0, int j, Regs& regs) {
         const int m = m0 + t;
         const float* bo = sp + 2 * CA + 2 * C + 64 * j;
         const float* bg = bo + O;
         T* orow = a.out + (long long)m * O + 64 * j;
-        const T* xrow = a.x + (long long)m * CA + 64 * j;
 #pragma unroll 1
         for (int c0 = 32 * g; c0 < 32 * g + 32; c0 += 16) {
             uint32_t ro[16], rg[16];
@@ -577,8 +675,8 @@ struct TrimulOp {
                            sigmoid_fast(__uint_as_float(rg[j]) + bg[c0 + j]);
                 }
                 if constexpr (ADD) {
-                    const uint4 q0 = *reinterpret_cast<const uint4*>(xrow + c0);
-                    const uint4 q1 = *reinterpret_cast<const uint4*>(xrow + c0 + 8);
+                    const int ri = (c0 - 32 * g) / 8;
+                    const uint4 q0 = regs.res[ri], q1 = regs.res[ri + 1];
                     const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
                     for (int e = 0; e < 8; ++e) {
@@ -1084,6 +1182,8 @@ cudaError_t ln_gdp_typed(cudaStream_t stream, int dtype, const void* x, const fl
     a.M = M;
     a.w_bytes = 2 * Op::P * K * 2;
     a.param_floats = 2 * K + 2 * Op::P;
+    a.vec_store = M % 8 == 0 && (reinterpret_cast<uintptr_t>(left) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(right) & 15) == 0;
     a.eps = eps;
     return launch_op<Op>(stream, tx, tw0, tw1, a);
 }

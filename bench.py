@@ -318,7 +318,11 @@ def run_ours(args):
                 'kernel': 'VoltaMmaBwd (attn_bwd_kernel + row_delta + dq_convert + fills)',
                 'bound': 'tensor', 'achieved': bwd_tf, 'peak': peak,
                 'peak_kind': pk_kind + ' burst bf16', 'unit': 'TFLOP/s',
-                'frac': bwd_tf / peak, 'traffic': None},
+                'frac': bwd_tf / peak, 'traffic': BWD_DRAM_BYTES_PER_SEQ * n_local,
+                'traffic_unit': 'bytes per launch',
+                'traffic_source': 'ncu dram__bytes_read.sum + dram__bytes_write.sum of '
+                                  'attn_bwd_kernel at N_seq=64 (144.6 MB), scaled by the '
+                                  'sequences processed'},
             'kernels': {'fwd_ms': fwd_ms, 'fwd_tflops': fwd_tf, 'fwd_frac': fwd_tf / peak,
                         'bwd_ms': bwd_ms, 'bwd_tflops': bwd_tf, 'bwd_frac': bwd_tf / peak,
                         'sequences_per_gpu': n_local},
@@ -426,6 +430,11 @@ def bench_fusions(torch, b200, dev, rank, world, steps, warmup, flush, pk):
         raise RuntimeError('a fused kernel reported a wait that gave up')
     return res_out
 
+
+# DRAM bytes (read + written) of one attn_bwd_kernel launch per sequence of the headline shape,
+# from one ncu capture at N_seq=64 (144.56 MB / 64); the full-size launch is too large to capture
+# under the profiling size rule and its traffic grows with the sequences processed
+BWD_DRAM_BYTES_PER_SEQ = 144.56e6 / 64
 
 BIG_RES, BIG_H = 2048, 4
 

@@ -422,6 +422,7 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
         const uint32_t lane_base = tmem_lane_base(warp);
         const float qk_scale = p.scale * kLog2e;
         const float masked = kMaskedLogit * kLog2e;
+        const uint64_t qk2 = pk2(qk_scale, qk_scale), log2e2 = pk2(kLog2e, kLog2e);
         float* stat = reinterpret_cast<float*>(smem + L::STAT) + wg * (2 * 2 * 32);
         float* rbuf = reinterpret_cast<float*>(smem + L::RED) + set * (kBQ * kBK) + hf * 32 * kBK;
         uint8_t* ds_row = smem + L::DSB + set * G::DS + t * 128;
@@ -516,25 +517,48 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
                         brow + (((4 * hf + (qc >> 3)) ^ (t & 7)) << 4) + (c & 1) * 8);
                     const float2 b01 = __half22float2(*reinterpret_cast<const __half2*>(&b2.x));
                     const float2 b23 = __half22float2(*reinterpret_cast<const __half2*>(&b2.y));
+                    // the statistics are stored negated: -lse and -delta
                     const float4 l4 = *reinterpret_cast<const float4*>(lsh + qc);
                     const float4 d4 = *reinterpret_cast<const float4*>(dlh + qc);
-                    // log2e * bias - lse, one FMA per element
-                    const float bl[4] = {fmaf(b01.x, kLog2e, -l4.x), fmaf(b01.y, kLog2e, -l4.y),
-                                         fmaf(b23.x, kLog2e, -l4.z), fmaf(b23.y, kLog2e, -l4.w)};
-                    const float ll[4] = {l4.x, l4.y, l4.z, l4.w};
-                    const float dd[4] = {d4.x, d4.y, d4.z, d4.w};
                     float pv[4], gv[4];
+                    if constexpr (decltype(fast)::value) {
+                        // two queries an instruction (paired fp32): log2e bias - lse,
+                        // + scale log2e s, exp2, dS = P (dP - delta)
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int j = 4 * c + e;
-                        if constexpr (decltype(fast)::value) {
-                            pv[e] = ex2(fmaf(__uint_as_float(sr[j]), qk_scale, bl[e]));
-                            gv[e] = pv[e] * (__uint_as_float(dr[j]) - dd[e]);
-                        } else {
+                        for (int e = 0; e < 4; e += 2) {
+                            const int j = 4 * c + e;
+                            const float2 bb = e == 0 ? b01 : b23;
+                            const uint64_t nl = e == 0 ? pk2(l4.x, l4.y) : pk2(l4.z, l4.w);
+                            const uint64_t nd = e == 0 ? pk2(d4.x, d4.y) : pk2(d4.z, d4.w);
+                            const uint64_t bl = fma2(pk2(bb.x, bb.y), log2e2, nl);
+                            const float2 x = upk2(fma2(
+                                pk2(__uint_as_float(sr[j]), __uint_as_float(sr[j + 1])), qk2, bl));
+                            float2 pp;
+                            if (c == 3 && e == 2) {
+                                pp = ex2_fma(x.x, x.y);  // one pair in eight on the FMA pipe
+                            } else {
+                                pp = make_float2(ex2(x.x), ex2(x.y));
+                            }
+                            const float2 gg = upk2(mul2(
+                                pk2(pp.x, pp.y),
+                                add2(pk2(__uint_as_float(dr[j]), __uint_as_float(dr[j + 1])), nd)));
+                            pv[e] = pp.x;
+                            pv[e + 1] = pp.y;
+                            gv[e] = gg.x;
+                            gv[e + 1] = gg.y;
+                        }
+                    } else {
+                        const float bl[4] = {fmaf(b01.x, kLog2e, l4.x), fmaf(b01.y, kLog2e, l4.y),
+                                             fmaf(b23.x, kLog2e, l4.z), fmaf(b23.y, kLog2e, l4.w)};
+                        const float nl[4] = {l4.x, l4.y, l4.z, l4.w};
+                        const float nd[4] = {d4.x, d4.y, d4.z, d4.w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const int j = 4 * c + e;
                             const float l2 = live ? fmaf(__uint_as_float(sr[j]), qk_scale, bl[e])
-                                                  : masked - ll[e];
+                                                  : masked + nl[e];
                             pv[e] = ex2(l2);
-                            gv[e] = live ? pv[e] * (__uint_as_float(dr[j]) - dd[e]) : 0.f;
+                            gv[e] = live ? pv[e] * (__uint_as_float(dr[j]) + nd[e]) : 0.f;
                         }
                     }
                     pw[2 * c] = E::pack(pv[0], pv[1]);
@@ -568,18 +592,20 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
             }
         };
 
-        // row statistics of this warpgroup's 32 queries: thread t < 32 holds lse of query t,
-        // 32 <= t < 64 delta of query t - 32; loaded one step ahead to hide their latency
+        // row statistics of this warpgroup's 32 queries, negated: thread t < 32 holds -lse of
+        // query t, 32 <= t < 64 -delta of query t - 32; loaded one step ahead to hide their
+        // latency
         const auto load_stat = [&](const StepCursor& c) {
+            // negated: -lse (-inf past Sq, so P = 0 there) and -delta
             if (c.gi >= total) {
-                return t < 32 ? INFINITY : 0.f;
+                return t < 32 ? -INFINITY : 0.f;
             }
             const StepPos& sp = c.pos;
             const int q = sp.q0 + 32 * hf + (t & 31);
             if (q >= p.Sq) {
-                return t < 32 ? INFINITY : 0.f;
+                return t < 32 ? -INFINITY : 0.f;
             }
-            return t < 32 ? p.lse[sp.rowbase + q] : p.delta[sp.rowbase + q];
+            return -(t < 32 ? p.lse[sp.rowbase + q] : p.delta[sp.rowbase + q]);
         };
         // cur: this step; nxt: this set's next step (its statistics are prefetched); prev: the
         // set's previous step (its dQ is flushed at the start of this one)

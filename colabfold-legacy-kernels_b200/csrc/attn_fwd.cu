@@ -109,28 +109,6 @@ struct Smem {
     static_assert(BYTES + 256 <= 227 * 1024, "shared memory");
 };
 
-// 2^a for two lanes on the FMA pipe instead of the special-function unit, which the other
-// exponentials of a row keep busy. Range reduction a = n + f with n = rint(a) (adding and
-// subtracting 1.5 * 2^23 rounds to an integer that lands in the low mantissa bits), 2^f on
-// [-0.5, 0.5] by a cubic fitted here by weighted least squares to the relative error (at most
-// 7.5e-5 in fp32, far below the 16-bit rounding of P), and 2^n added into the exponent field.
-// a is clamped below at -125 (2^-125 stands in for 0: it is under every P that matters by more
-// than a bf16 ulp); a never exceeds the lazy-rescale threshold.
-__device__ __forceinline__ float2 ex2_fma(float a0, float a1) {
-    constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
-    const uint64_t a = pk2(fmaxf(a0, -125.f), fmaxf(a1, -125.f));
-    const uint64_t t = add2(a, pk2(kRound, kRound));
-    const uint64_t n = add2(t, pk2(-kRound, -kRound));
-    const uint64_t f = fma2(n, pk2(-1.f, -1.f), a);
-    uint64_t q = fma2(f, pk2(0.05517160892486572f, 0.05517160892486572f),
-                      pk2(0.2426111102104187f, 0.2426111102104187f));
-    q = fma2(q, f, pk2(0.6932609677314758f, 0.6932609677314758f));
-    q = fma2(q, f, pk2(0.9999280571937561f, 0.9999280571937561f));
-    const float2 tf = upk2(t), qf = upk2(q);
-    return make_float2(__int_as_float(__float_as_int(qf.x) + (__float_as_int(tf.x) << 23)),
-                       __int_as_float(__float_as_int(qf.y) + (__float_as_int(tf.y) << 23)));
-}
-
 // 8 consecutive 16-bit values of the bias tile row r, keys [8i, 8i+8): region i/8, chunk i%8
 __device__ __forceinline__ uint4 bias_chunk(const uint8_t* stage, int r, int i) {
     const uint8_t* region = stage + (i >> 3) * (kBQ * 128);

@@ -661,8 +661,7 @@ struct TrimulOp {
         const float* bo = sp + 2 * CA + 2 * C + 64 * j;
         const float* bg = bo + O;
         T* orow = a.out + (long long)m * O + 64 * j;
-#pragma unroll 1
-        for (int c0 = 32 * g; c0 < 32 * g + 32; c0 += 16) {
+        const auto chunk = [&](int c0) {
             uint32_t ro[16], rg[16];
             tmem_ld16(acc + c0, ro);
             tmem_ld16(acc + 64 + c0, rg);
@@ -692,6 +691,18 @@ struct TrimulOp {
                 }
                 *reinterpret_cast<uint4*>(orow + c0) = make_uint4(w[0], w[1], w[2], w[3]);
                 *reinterpret_cast<uint4*>(orow + c0 + 8) = make_uint4(w[4], w[5], w[6], w[7]);
+            }
+        };
+        // unrolled where the registers allow (C = 128 keeps a wider prologue state)
+        if constexpr (C <= 64) {
+#pragma unroll
+            for (int c0 = 32 * g; c0 < 32 * g + 32; c0 += 16) {
+                chunk(c0);
+            }
+        } else {
+#pragma unroll 1
+            for (int c0 = 32 * g; c0 < 32 * g + 32; c0 += 16) {
+                chunk(c0);
             }
         }
     }

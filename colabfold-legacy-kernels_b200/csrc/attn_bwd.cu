@@ -13,7 +13,7 @@
 //     so one item's are stored while the next accumulates); both come out bitwise
 //     deterministic;
 //   * warp roles: a TMA warp streams the 64-query steps (q, dout and the bias tile) three
-//     stages deep; MMA warp A issues S^T, dP^T and dQ, MMA warp B dV and dK (each issuing
+//     stages deep; MMA warp A issues S^T and dP^T, MMA warp B dQ, dV and dK (each issuing
 //     thread has its own MMA pipeline, so the two overlap); softmax warpgroups in step sets
 //     that take the steps alternately (ping-pong), each set with its own S^T/dP^T columns in
 //     tensor memory and its own dS buffer, so one set's exponentials overlap the other set's
@@ -57,8 +57,8 @@ constexpr float kMaskedLogit = -1.0e4f;
 
 struct BwdParams {
     const uint8_t* kmask;
-    const float* lse;
-    const float* delta;
+    const float* nlse;   // -lse, [N,H,Sq]
+    const float* ndelta; // -delta
     float* dq_acc;  // [N,H,Sq,D] fp32, zeroed
     void* dk;
     void* dv;
@@ -85,8 +85,8 @@ struct BGeom {
     // softmax warpgroups, one per 32-query half of its step.
     static constexpr int NP = DN <= 32 ? 2 : 1;
     static constexpr int NWG = 2 * NP;
-    static constexpr int MMA_A = 4 * NWG;    // warp issuing S^T, dP^T and dQ
-    static constexpr int MMA_B = MMA_A + 1;  // warp issuing dV and dK
+    static constexpr int MMA_A = 4 * NWG;    // warp issuing S^T and dP^T
+    static constexpr int MMA_B = MMA_A + 1;  // warp issuing dQ, dV and dK
     static constexpr int TMA_WARP = MMA_A + 2;
     static constexpr int THREADS = NWG * 128 + 96;
     // K/V buffers in shared memory and dK/dV accumulator sets in tensor memory: two of each, so
@@ -107,13 +107,22 @@ struct BSmem {
     using G = BGeom<DP>;
     static constexpr int KV = 0;                             // KVB x (K, V)
     static constexpr int STAGE = KV + G::KVB * 2 * G::KTILE;  // NS x (Q, dO, bias^T)
-    static constexpr int STAGE_BYTES = 2 * G::QTILE + G::BT;
+    // a stage: Q, dO, bias^T, then the step's negated row statistics (-lse[64], -delta[64])
+    static constexpr int STAT_OFF = 2 * G::QTILE + G::BT;
+    // a multiple of 1024 bytes: every stage's 128-byte-swizzled tiles, and the dS buffers after
+    // the stages, need 1024-byte-aligned bases (the swizzle follows the address bits)
+    static constexpr int STAGE_BYTES = (STAT_OFF + 2 * kBQ * 4 + 1023) / 1024 * 1024;
+    static constexpr int STAGE_TX = STAT_OFF;  // bytes the TMA copies bring
     static constexpr int DSB = STAGE + G::NS * STAGE_BYTES;  // one dS buffer per set
-    static constexpr int RED = DSB + G::NP * G::DS;          // one fp32 dS tile [64][128] per set
-    static constexpr int STAT = RED + G::NP * kBQ * kBK * 4;   // [NWG][2][lse, delta][32] fp32
-    static constexpr int END = STAT + G::NWG * 2 * 2 * 32 * 4;
+    // fp32 dS staged for the dBias reduce: per set, per warp of its two warpgroups, the warp's
+    // 32 keys of its warpgroup's 32 queries, [32 queries][32 keys]
+    static constexpr int RED = DSB + G::NP * G::DS;
+    static constexpr int END = RED + G::NP * kBQ * kBK * 4;
     static constexpr int BYTES = END + 1024;
     static_assert(BYTES + 512 <= 227 * 1024, "shared memory (dynamic + the static barriers)");
+    static_assert(STAGE % 1024 == 0 && STAGE_BYTES % 1024 == 0 && DSB % 1024 == 0 &&
+                      RED % 1024 == 0,
+                  "1024-byte-aligned swizzled tiles");
 };
 
 // dBias modes
@@ -231,7 +240,7 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
                 mbar_init(&kv_empty[i], 1);
             }
             for (int i = 0; i < NS; ++i) {
-                mbar_init(&q_full[i], 1);
+                mbar_init(&q_full[i], 32);  // the TMA warp's 32 lanes (statistics, copies)
                 mbar_init(&q_empty[i], 2);  // both MMA warps read a stage
             }
             for (int i = 0; i < NP; ++i) {
@@ -257,33 +266,56 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
     const uint32_t tmem = tmem_base_sh;
 
     if (warp == G::TMA_WARP) {
-        if (lane == 0) {
+        // the whole warp: lane 0 issues the copies, every lane stages two of the step's row
+        // statistics and arrives on the stage's barrier (released with its own stores)
+        {
             for (int j = 0; j < J; ++j) {
                 const StepPos it = item_pos(p, nkt, j);
                 const int kb = j % KVB;
-                if (j >= KVB) {
-                    mbar_wait(&kv_empty[kb], ((j - KVB) / KVB) & 1, &g_status, kStatusMmaWait,
-                              &abort_flag);
-                }
-                uint8_t* kv = smem + L::KV + kb * 2 * G::KTILE;
-                mbar_arrive_expect_tx(&kv_full[kb], 2 * G::KTILE);
-                for (int a = 0; a < G::NA; ++a) {
-                    tma_load_4d(kv + a * G::KATOM, &tk, &kv_full[kb], a * G::AE, it.h, it.k0,
-                                it.n);
-                    tma_load_4d(kv + G::KTILE + a * G::KATOM, &tv, &kv_full[kb], a * G::AE, it.h,
-                                it.k0, it.n);
+                if (lane == 0) {
+                    if (j >= KVB) {
+                        mbar_wait(&kv_empty[kb], ((j - KVB) / KVB) & 1, &g_status,
+                                  kStatusMmaWait, &abort_flag);
+                    }
+                    uint8_t* kv = smem + L::KV + kb * 2 * G::KTILE;
+                    mbar_arrive_expect_tx(&kv_full[kb], 2 * G::KTILE);
+                    for (int a = 0; a < G::NA; ++a) {
+                        tma_load_4d(kv + a * G::KATOM, &tk, &kv_full[kb], a * G::AE, it.h, it.k0,
+                                    it.n);
+                        tma_load_4d(kv + G::KTILE + a * G::KATOM, &tv, &kv_full[kb], a * G::AE,
+                                    it.h, it.k0, it.n);
+                    }
                 }
                 for (int i = 0; i < nqt; ++i) {
                     const int gi = j * nqt + i;
                     StepPos sp = it;
                     sp.q0 = rotated_q0(it.n, nqt, i);
                     const int s = gi % NS;
+                    // the statistics load ahead of the wait for the stage
+                    float sv[4];
+#pragma unroll
+                    for (int r = 0; r < 2; ++r) {
+                        const int q = sp.q0 + 32 * r + lane;
+                        const bool in = q < p.Sq;
+                        sv[2 * r] = in ? p.nlse[sp.rowbase + q] : -INFINITY;  // P = 0 past Sq
+                        sv[2 * r + 1] = in ? p.ndelta[sp.rowbase + q] : 0.f;
+                    }
                     if (gi >= NS) {
                         mbar_wait(&q_empty[s], ((gi - NS) / NS) & 1, &g_status, kStatusMmaWait,
                                   &abort_flag);
                     }
                     uint8_t* st = smem + L::STAGE + s * L::STAGE_BYTES;
-                    mbar_arrive_expect_tx(&q_full[s], L::STAGE_BYTES);
+                    float* stat = reinterpret_cast<float*>(st + L::STAT_OFF);
+#pragma unroll
+                    for (int r = 0; r < 2; ++r) {
+                        stat[32 * r + lane] = sv[2 * r];
+                        stat[kBQ + 32 * r + lane] = sv[2 * r + 1];
+                    }
+                    if (lane != 0) {
+                        mbar_arrive(&q_full[s]);
+                        continue;
+                    }
+                    mbar_arrive_expect_tx(&q_full[s], L::STAGE_TX);
                     for (int a = 0; a < G::NA; ++a) {
                         tma_load_4d(st + a * G::QATOM, &tq, &q_full[s], a * G::AE, sp.h, sp.q0,
                                     sp.n);
@@ -297,7 +329,6 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
     } else if (warp == G::MMA_A) {
         if (lane == 0) {
             const uint32_t idesc_s = idesc_f16(E::kBf16, 128, kBQ, false, false);
-            const uint32_t idesc_dq = idesc_f16(E::kBf16, 64, DN, true, true);
             // S^T = K Q^T and dP^T = V dO^T of step gi into set (gi % NP)'s columns, once the dV
             // and dK MMAs of that set's previous step have read its P^T and dS^T
             const auto issue_s = [&](int gi, int j, int i) {
@@ -332,48 +363,10 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
                 mma_commit(&s_full[w]);
                 mma_commit(&q_empty[s]);
             };
-            // dQ = dS K (M = 64 queries) of step gj once its set has written dS; the item's last
-            // dQ releases its K/V buffer
-            const auto issue_dq = [&](int gj, int j, int i) {
-                const int w = gj % NP, kb = j % KVB;
-                mbar_wait(&p_ready[w], (gj / NP) & 1, &g_status, kStatusSyncWait, &abort_flag);
-                tc_fence_after();
-                const uint32_t k_base = smem_u32(smem + L::KV + kb * 2 * G::KTILE);
-                const uint32_t ds_base = smem_u32(smem + L::DSB + w * G::DS);
-#pragma unroll
-                for (int ks = 0; ks < kBK / 16; ++ks) {
-                    const uint64_t ad =
-                        smem_desc(ds_base + ks * 16 * 128, G::DS, 1024, kSwizzle128B);
-                    const uint64_t bd =
-                        smem_desc(k_base + ks * 16 * G::ROWB, G::KATOM, 8 * G::ROWB, G::LAYOUT);
-                    mma_ss(tmem + G::T_DQ + w * G::DN, ad, bd, idesc_dq, ks > 0 ? 1u : 0u);
-                }
-                mma_commit(&dq_done[w]);
-                if (i == nqt - 1) {
-                    mma_commit(&kv_empty[kb]);
-                }
-            };
-            int pj = 0, pi = 0;  // the previous step
             for (int j = 0, gi = 0; j < J; ++j) {
                 for (int i = 0; i < nqt; ++i, ++gi) {
-                    if constexpr (NP == 2) {
-                        // the next step's S^T and dP^T go ahead of this step's dQ
-                        issue_s(gi, j, i);
-                        if (gi >= 1) {
-                            issue_dq(gi - 1, pj, pi);
-                        }
-                    } else {
-                        if (gi >= 1) {
-                            issue_dq(gi - 1, pj, pi);
-                        }
-                        issue_s(gi, j, i);
-                    }
-                    pj = j;
-                    pi = i;
+                    issue_s(gi, j, i);
                 }
-            }
-            if (total >= 1) {
-                issue_dq(total - 1, pj, pi);
             }
         }
     } else if (warp == G::MMA_B) {
@@ -381,6 +374,7 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
             // dV += P^T dO and dK += dS^T Q, A read from tensor memory: the 16-bit P^T (dS^T) of
             // queries [32 hf, 32 hf + 32) sits in columns [32 hf, 32 hf + 16) of S^T (dP^T)
             const uint32_t idesc_acc = idesc_f16(E::kBf16, 128, DN, false, true);
+            const uint32_t idesc_dq = idesc_f16(E::kBf16, 64, DN, true, true);
             for (int gi = 0, j = 0, i = 0; gi < total; ++gi) {
                 const int w = gi % NP, s = gi % NS, db = j % NB;
                 if (i == 0 && j >= NB) {
@@ -391,6 +385,26 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
                 mbar_wait(&q_full[s], (gi / NS) & 1, &g_status, kStatusTmaWait, &abort_flag);
                 mbar_wait(&p_ready[w], (gi / NP) & 1, &g_status, kStatusSyncWait, &abort_flag);
                 tc_fence_after();
+                // dQ = dS K (M = 64 queries) first, the MMA its set flushes next; the item's
+                // last one releases the K/V buffer (the item's S^T/dP^T MMAs finished before
+                // its last dS existed)
+                {
+                    const int kb = j % KVB;
+                    const uint32_t k_base = smem_u32(smem + L::KV + kb * 2 * G::KTILE);
+                    const uint32_t ds_base = smem_u32(smem + L::DSB + w * G::DS);
+#pragma unroll
+                    for (int ks = 0; ks < kBK / 16; ++ks) {
+                        const uint64_t ad =
+                            smem_desc(ds_base + ks * 16 * 128, G::DS, 1024, kSwizzle128B);
+                        const uint64_t bd = smem_desc(k_base + ks * 16 * G::ROWB, G::KATOM,
+                                                      8 * G::ROWB, G::LAYOUT);
+                        mma_ss(tmem + G::T_DQ + w * G::DN, ad, bd, idesc_dq, ks > 0 ? 1u : 0u);
+                    }
+                    mma_commit(&dq_done[w]);
+                    if (i == nqt - 1) {
+                        mma_commit(&kv_empty[kb]);
+                    }
+                }
                 const uint32_t st = smem_u32(smem + L::STAGE + s * L::STAGE_BYTES);
                 const uint32_t t_dv = tmem + G::T_ACC + db * 2 * G::DN, t_dk = t_dv + G::DN;
 #pragma unroll
@@ -423,8 +437,9 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
         const float qk_scale = p.scale * kLog2e;
         const float masked = kMaskedLogit * kLog2e;
         const uint64_t qk2 = pk2(qk_scale, qk_scale), log2e2 = pk2(kLog2e, kLog2e);
-        float* stat = reinterpret_cast<float*>(smem + L::STAT) + wg * (2 * 2 * 32);
-        float* rbuf = reinterpret_cast<float*>(smem + L::RED) + set * (kBQ * kBK) + hf * 32 * kBK;
+        // this warp's fp32 dS staging for the dBias reduce: [32 queries][its 32 keys]
+        float* rbuf = reinterpret_cast<float*>(smem + L::RED) + set * (kBQ * kBK) +
+                      (4 * hf + (warp & 3)) * (32 * 32);
         uint8_t* ds_row = smem + L::DSB + set * G::DS + t * 128;
         const uint32_t t_dq = tmem + G::T_DQ + set * G::DN;
         const uint32_t t_st = tmem + 128 * set + lane_base + 32 * hf, t_dp = t_st + 64;
@@ -568,7 +583,7 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
                     if constexpr (DBIAS == kDbiasTma) {
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
-                            rbuf[(qc + e) * kBK + t] = gv[e];
+                            rbuf[(qc + e) * 32 + lane] = gv[e];
                         }
                     } else if constexpr (DBIAS == kDbiasRed) {
                         if (key < p.Sk) {
@@ -592,47 +607,22 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
             }
         };
 
-        // row statistics of this warpgroup's 32 queries, negated: thread t < 32 holds -lse of
-        // query t, 32 <= t < 64 -delta of query t - 32; loaded one step ahead to hide their
-        // latency
-        const auto load_stat = [&](const StepCursor& c) {
-            // negated: -lse (-inf past Sq, so P = 0 there) and -delta
-            if (c.gi >= total) {
-                return t < 32 ? -INFINITY : 0.f;
-            }
-            const StepPos& sp = c.pos;
-            const int q = sp.q0 + 32 * hf + (t & 31);
-            if (q >= p.Sq) {
-                return t < 32 ? -INFINITY : 0.f;
-            }
-            return -(t < 32 ? p.lse[sp.rowbase + q] : p.delta[sp.rowbase + q]);
-        };
-        // cur: this step; nxt: this set's next step (its statistics are prefetched); prev: the
-        // set's previous step (its dQ is flushed at the start of this one)
+        // cur: this step; nxt: this set's next step; prev: the set's previous step (its dQ is
+        // flushed at the start of this one)
         StepCursor cur, nxt;
         cur.start(p, nkt, nqt, set);
         nxt = cur;
         nxt.advance(p, nkt, nqt, NP);
         StepPos prev = cur.pos;
-        float stat_next = t < 64 ? load_stat(cur) : 0.f;
         int k = 0, stored = 0;  // this set's steps so far; items whose dK/dV this group stored
         for (; cur.gi < total; ++k) {
-            const int gi = cur.gi, s = gi % NS, b = k & 1, j = cur.j;
+            const int gi = cur.gi, s = gi % NS, j = cur.j;
             const StepPos sp = cur.pos;
-            // this step's row statistics into the warpgroup's buffer b
-            float* ls = stat + b * 64;
-            float* dl = ls + 32;
-            if (t < 64) {
-                stat[b * 64 + t] = stat_next;
-            }
             if constexpr (DBIAS == kDbiasTma) {
-                if (t == 0 && k >= 1) {
-                    bulk_wait_read();  // the previous step's reduce has read the dS rows
+                if (lane == 0 && k >= 1) {
+                    bulk_wait_read();  // this warp's previous reduce has read its dS rows
                 }
-            }
-            named_sync(1 + wg, 128);
-            if (t < 64) {
-                stat_next = load_stat(nxt);
+                __syncwarp();
             }
             if (k >= 1) {
                 // this set's previous step: dQ out of tensor memory before it is reused
@@ -650,7 +640,11 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
             mbar_wait(&q_full[s], (gi / NS) & 1, &g_status, kStatusTmaWait, &abort_flag);
             mbar_wait(&s_full[set], k & 1, &g_status, kStatusMmaWait, &abort_flag);
             tc_fence_after();
-            const uint8_t* brow = smem + L::STAGE + s * L::STAGE_BYTES + 2 * G::QTILE + t * 128;
+            const uint8_t* stage = smem + L::STAGE + s * L::STAGE_BYTES;
+            const uint8_t* brow = stage + 2 * G::QTILE + t * 128;
+            // the step's negated row statistics, staged by the TMA warp
+            const float* ls = reinterpret_cast<const float*>(stage + L::STAT_OFF) + 32 * hf;
+            const float* dl = ls + kBQ;
             const int jn = min(32, p.Sq - sp.q0 - 32 * hf);
             if (warp_live) {
                 half_step(std::true_type{}, brow, ls, dl, sp.q0, jn, sp.k0 + t);
@@ -662,11 +656,11 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
             tc_fence_before();
             mbar_arrive(&p_ready[set]);
             if constexpr (DBIAS == kDbiasTma) {
-                // this warpgroup's 32 fp32 dS rows in one bulk reduce-add (rows past Sq and
-                // keys past Sk clip)
-                named_sync(1 + wg, 128);
-                if (t == 0 && jn > 0) {
-                    tma_reduce_add_3d(&tdb, rbuf, sp.k0, sp.q0 + 32 * hf, sp.h);
+                // this warp's 32 queries x 32 keys of fp32 dS in one bulk reduce-add (rows past
+                // Sq and keys past Sk clip)
+                __syncwarp();
+                if (lane == 0 && jn > 0 && sp.k0 + 32 * (warp & 3) < p.Sk) {
+                    tma_reduce_add_3d(&tdb, rbuf, sp.k0 + 32 * (warp & 3), sp.q0 + 32 * hf, sp.h);
                 }
             }
             // the accumulators of the items before this one: their last MMAs were issued a
@@ -679,7 +673,7 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
             nxt.advance(p, nkt, nqt, NP);
         }
         if constexpr (DBIAS == kDbiasTma) {
-            if (t == 0) {
+            if (lane == 0) {
                 bulk_wait_all();
             }
         }
@@ -700,10 +694,12 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
     }
 }
 
-// delta[row] = sum_c out[row][c] * dout[row][c], one thread per row, 16-byte loads
+// The backward's row statistics, negated: ndelta[row] = -sum_c out[row][c] * dout[row][c] and
+// nlse[row] = -lse[row]; one thread per row, 16-byte loads
 template <typename T>
 __global__ void row_delta_kernel(const T* __restrict__ out, const T* __restrict__ dout,
-                                 float* __restrict__ delta, long long rows, int D) {
+                                 const float* __restrict__ lse, float* __restrict__ ndelta,
+                                 float* __restrict__ nlse, long long rows, int D) {
     using E = Elem<T>;
     const long long r = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= rows) {
@@ -722,7 +718,8 @@ __global__ void row_delta_kernel(const T* __restrict__ out, const T* __restrict_
             s = fmaf(x.y, y.y, s);
         }
     }
-    delta[r] = s;
+    ndelta[r] = -s;
+    nlse[r] = -lse[r];
 }
 
 // bt[h][k][q] = log2e * bias[h][q][k] in fp32, queries padded to Sqp with zeros; 32x32 tiles
@@ -778,16 +775,17 @@ bool aligned16(const void* p) {
     return (reinterpret_cast<uintptr_t>(p) & 15) == 0;
 }
 
-// Workspace: dQ accumulator | row statistic | bias^T (f16, queries padded to a multiple of 8),
+// Workspace: dQ accumulator | -delta | -lse | bias^T (f16, queries padded to a multiple of 8),
 // each 256-byte aligned
 struct Workspace {
-    size_t dq, delta, bt, total;
+    size_t dq, delta, nlse, bt, total;
     static Workspace of(size_t N, size_t H, size_t Sq, size_t Sk, size_t D) {
         Workspace w;
         const size_t rows = N * H * Sq, sqp = (Sq + 7) & ~size_t(7);
         w.dq = 0;
         w.delta = align256(rows * D * sizeof(float));
-        w.bt = w.delta + align256(rows * sizeof(float));
+        w.nlse = w.delta + align256(rows * sizeof(float));
+        w.bt = w.nlse + align256(rows * sizeof(float));
         w.total = w.bt + align256(H * Sk * sqp * sizeof(__half));
         return w;
     }
@@ -831,7 +829,7 @@ cudaError_t launch_dp(cudaStream_t stream, const CUtensorMap* maps, const BwdPar
 template <typename T>
 cudaError_t run_backward(cudaStream_t stream, const CUtensorMap* maps, const BwdParams& p,
                          const void* bias, __half* bt, int Sqp, const void* out, const void* dout,
-                         float* delta, void* dq, int dbias_mode) {
+                         const float* lse, float* ndelta, float* nlse, void* dq, int dbias_mode) {
     const long long rows = (long long)p.N * p.H * p.Sq;
     cudaError_t e;
     if ((e = cudaMemsetAsync(p.dbias, 0, sizeof(float) * (size_t)p.H * p.Sq * p.Sk, stream)) !=
@@ -843,7 +841,7 @@ cudaError_t run_backward(cudaStream_t stream, const CUtensorMap* maps, const Bwd
         return e;
     }
     row_delta_kernel<T><<<(unsigned)((rows + 255) / 256), 256, 0, stream>>>(
-        static_cast<const T*>(out), static_cast<const T*>(dout), delta, rows, p.D);
+        static_cast<const T*>(out), static_cast<const T*>(dout), lse, ndelta, nlse, rows, p.D);
     const dim3 tgrid((Sqp + 31) / 32, (p.Sk + 31) / 32, p.H);
     bias_transpose_kernel<T><<<tgrid, dim3(32, 8), 0, stream>>>(static_cast<const T*>(bias), bt,
                                                                  p.Sq, p.Sk, Sqp);
@@ -919,7 +917,8 @@ extern "C" int cflk_volta_mma_bwd(void* stream_, int dtype, const void* q, const
     const size_t rows = (size_t)N * H * Sq;
     uint8_t* wsb = static_cast<uint8_t*>(workspace);
     float* dq_acc = reinterpret_cast<float*>(wsb + ws.dq);
-    float* delta = reinterpret_cast<float*>(wsb + ws.delta);
+    float* ndelta = reinterpret_cast<float*>(wsb + ws.delta);
+    float* nlse = reinterpret_cast<float*>(wsb + ws.nlse);
     __half* bt = reinterpret_cast<__half*>(wsb + ws.bt);
     const int Sqp = (int)((Sq + 7) & ~int64_t(7));
     if (H == 0 || Sq == 0 || Sk == 0 || N == 0) {
@@ -970,7 +969,7 @@ extern "C" int cflk_volta_mma_bwd(void* stream_, int dtype, const void* q, const
     if (want_dbias && Sk % 4 == 0 && (reinterpret_cast<uintptr_t>(dbias) & 15) == 0) {
         const uint64_t ddb[3] = {(uint64_t)Sk, (uint64_t)Sq, (uint64_t)H};
         const uint64_t sdb[2] = {(uint64_t)Sk, (uint64_t)Sq * (uint64_t)Sk};
-        const uint32_t boxdb[3] = {(uint32_t)kBK, (uint32_t)(kBQ / 2), 1};
+        const uint32_t boxdb[3] = {32, 32, 1};  // one warp's keys x one warpgroup's queries
         if (encode_tiled(&maps[5], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, 3, dbias, ddb, sdb, boxdb,
                          CU_TENSOR_MAP_SWIZZLE_NONE)) {
             dbias_mode = kDbiasTma;
@@ -978,8 +977,8 @@ extern "C" int cflk_volta_mma_bwd(void* stream_, int dtype, const void* q, const
     }
     BwdParams p;
     p.kmask = kmask;
-    p.lse = lse;
-    p.delta = delta;
+    p.nlse = nlse;
+    p.ndelta = ndelta;
     p.dq_acc = dq_acc;
     p.dk = dk;
     p.dv = dv;
@@ -992,9 +991,9 @@ extern "C" int cflk_volta_mma_bwd(void* stream_, int dtype, const void* q, const
     p.scale = scale;
     const cudaError_t e =
         dtype == kBF16 ? run_backward<__nv_bfloat16>(stream, maps, p, bias, bt, Sqp, out, dout,
-                                                     delta, dq, dbias_mode)
-                       : run_backward<__half>(stream, maps, p, bias, bt, Sqp, out, dout, delta,
-                                              dq, dbias_mode);
+                                                     lse, ndelta, nlse, dq, dbias_mode)
+                       : run_backward<__half>(stream, maps, p, bias, bt, Sqp, out, dout, lse,
+                                              ndelta, nlse, dq, dbias_mode);
     if (e != cudaSuccess) {
         return fail(kInternal, std::string("volta_mma_bwd launch: ") + cudaGetErrorString(e));
     }
@@ -1065,7 +1064,7 @@ extern "C" int cflk_volta_mma_bwd_noalloc(void* stream, int dtype, const void* q
                           "volta_mma_bwd_noalloc: needs " + std::to_string(need) +
                               " bytes of scratch, the static scratch holds " +
                               std::to_string(kNoAllocScratchBytes) +
-                              " (cflk_volta_mma_bwd_workspace_size: about 4*N*H*Sq*(D+1) + "
+                              " (cflk_volta_mma_bwd_workspace_size: about 4*N*H*Sq*(D+2) + "
                               "2*H*Sk*Sq bytes); use cflk_volta_mma_bwd with a workspace");
     }
     void* scratch = nullptr;

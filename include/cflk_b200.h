@@ -73,7 +73,8 @@ CFLK_API int cflk_volta_mma_packed(void* stream, int dtype, const void* p, const
                                    int64_t block_q, int64_t block_k, int column);
 
 /* Bytes of device workspace cflk_volta_mma_bwd needs for these sizes: a float32 dQ accumulator,
- * the row statistic and the bias transposed to f16 [H][Sk][Sq rounded up to 8] (the reference
+ * the negated row statistics (-delta, -lse) and the bias transposed to f16
+ * [H][Sk][Sq rounded up to 8] (the reference
  * takes its dQ accumulator and row statistic from XLA's ScratchAllocator,
  * cuda/volta_mma_attn_bwd.cu:346-361). */
 CFLK_API int cflk_volta_mma_bwd_workspace_size(int64_t N, int64_t H, int64_t Sq, int64_t Sk,

@@ -62,8 +62,9 @@ def test_workspace_size():
                                                ctypes.c_int64(32), ctypes.byref(n)) == 0
     rows = 2 * 3 * 10
     align = lambda x: (x + 255) // 256 * 256
-    # dQ accumulator, row statistic, f16 bias^T with the queries padded to a multiple of 8
-    assert n.value == align(rows * 32 * 4) + align(rows * 4) + align(3 * 7 * 16 * 2)
+    # dQ accumulator, the two negated row statistics (-delta, -lse), f16 bias^T with the
+    # queries padded to a multiple of 8
+    assert n.value == (align(rows * 32 * 4) + 2 * align(rows * 4) + align(3 * 7 * 16 * 2))
 
 
 def test_resolver_capabilities():

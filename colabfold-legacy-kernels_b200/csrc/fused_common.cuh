@@ -61,6 +61,42 @@ __device__ __forceinline__ int tile_work(const T* keep, int M, int m0, float oth
     return __any_sync(0xffffffffu, zero) ? kPadding : kSkip;
 }
 
+// The keep values of rows m0 + lane + 32i (i < 4) for tile_work_of, loaded by volatile
+// instructions so that the compiler keeps them where they are written (ahead of the waits that
+// follow), which lets a worker load the next tile's values a whole tile early.
+template <typename T>
+__device__ __forceinline__ void keep_load(const T* keep, int M, int m0, float other,
+                                          float (&v)[BM / 32]) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int i = 0; i < BM / 32; ++i) {
+        const int r = m0 + lane + 32 * i;
+        unsigned short bits = 0;
+        if (keep != nullptr && r < M) {
+            asm volatile("ld.global.nc.u16 %0, [%1];"
+                         : "=h"(bits)
+                         : "l"(reinterpret_cast<const unsigned short*>(keep) + r));
+            v[i] = Elem<T>::to_f(*reinterpret_cast<const T*>(&bits));
+        } else {
+            v[i] = keep == nullptr ? 1.f : other;
+        }
+    }
+}
+
+// tile_work from values keep_load fetched (the same rule)
+__device__ __forceinline__ int tile_work_of(const float (&v)[BM / 32]) {
+    bool live = false, zero = false;
+#pragma unroll
+    for (int i = 0; i < BM / 32; ++i) {
+        live |= v[i] > 0.f;
+        zero |= v[i] == 0.f;
+    }
+    if (__any_sync(0xffffffffu, live)) {
+        return kCompute;
+    }
+    return __any_sync(0xffffffffu, zero) ? kPadding : kSkip;
+}
+
 // Barrier among the 256 workers (id 1).
 __device__ __forceinline__ void workers_sync() {
     named_sync(1, kWorkers);

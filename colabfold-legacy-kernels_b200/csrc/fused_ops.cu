@@ -146,9 +146,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t lane_base = tmem_lane_base(warp);
         typename Op::Regs regs{};
         int c = 0, q = 0;
+        // the keep values of the worker's next tile load a tile ahead (the classification's
+        // global loads would otherwise stall every tile); a worker's own row value is also
+        // handed to the op (ln_gdp's row mask)
+        float kv[BM / 32];
+        keep_load(Op::keep(a), a.M, blockIdx.x * BM, Op::kOther, kv);
         for (int cursor = blockIdx.x; cursor < ntiles; cursor += gridDim.x) {
             const int m0 = cursor * BM;
-            const int work = tile_work(Op::keep(a), a.M, m0, Op::kOther);
+            const int work = tile_work_of(kv);
+            Op::row_keep(regs, kv[warp & 3]);
+            keep_load(Op::keep(a), a.M, m0 + gridDim.x * BM, Op::kOther, kv);
             if (work == kPadding) {
                 Op::padding(a, m0, t, g);
                 continue;
@@ -261,7 +268,9 @@ struct LnGdpOp {
     struct Regs {
         const float* maskv;  // this tile's row mask (shared memory)
         int parity;
+        float row_mask;      // this worker's row of the mask, from the tile classification
     };
+    static __device__ void row_keep(Regs& r, float v) { r.row_mask = v; }
     static __device__ const T* keep(const Args& a) { return a.mask; }
     // scale [K], offset [K], bp [P], bg [P]
     static __device__ void load_params(const Args& a, float* sp, int tid) {
@@ -297,8 +306,7 @@ struct LnGdpOp {
         // two buffers, as the epilogue of the previous tile may still read the other one
         float* mv = red + 4 * BM + regs.parity * BM;
         if (g == 0) {
-            const int m = m0 + t;
-            mv[t] = m < a.M ? fmaxf(E::to_f(a.mask[m]), 0.f) : 0.f;
+            mv[t] = m0 + t < a.M ? fmaxf(regs.row_mask, 0.f) : 0.f;
         }
         regs.maskv = mv;
         regs.parity ^= 1;
@@ -389,6 +397,7 @@ struct ProjOp {
     struct Regs {
         uint4 res[8];  // the residual part of the next block (up to 64 columns)
     };
+    static __device__ void row_keep(Regs&, float) {}
     static __device__ const T* keep(const Args& a) { return a.keep; }
     // scale [K], offset [K], b [n], wb [8][K]
     static __device__ void load_params(const Args& a, float* sp, int tid) {
@@ -559,6 +568,7 @@ struct TrimulOp {
     struct Regs {
         uint4 res[4];  // x of worker half g's 32 channels of the next block (add_input)
     };
+    static __device__ void row_keep(Regs&, float) {}
     static __device__ const T* keep(const Args& a) { return a.keep; }
     // in_scale [CA], in_offset [CA], ln_scale [C], ln_offset [C], bo [O], bg [O]
     static __device__ void load_params(const Args& a, float* sp, int tid) {

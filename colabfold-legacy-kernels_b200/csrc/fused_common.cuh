@@ -132,40 +132,67 @@ __device__ __forceinline__ void ln_rows_half(uint8_t* tile, int t, int g, const 
             v[8 * ch + 2 * e + 1] = f.y;
         }
     }
-    float s = 0.f;
+    // sums in four paired partial accumulators (short dependency chains)
+    uint64_t acc[4];
 #pragma unroll
-    for (int i = 0; i < KH; ++i) {
-        s += v[i];
+    for (int i = 0; i < 4; ++i) {
+        acc[i] = pk2(v[2 * i], v[2 * i + 1]);
     }
-    red[(0 * 2 + g) * BM + t] = s;
+#pragma unroll
+    for (int i = 8; i < KH; i += 2) {
+        acc[(i >> 1) & 3] = add2(acc[(i >> 1) & 3], pk2(v[i], v[i + 1]));
+    }
+    float2 sp2 = upk2(add2(add2(acc[0], acc[1]), add2(acc[2], acc[3])));
+    red[(0 * 2 + g) * BM + t] = sp2.x + sp2.y;
     workers_sync();
     const float mean = (red[0 * BM + t] + red[1 * BM + t]) * (1.f / K);
-    float q = 0.f;
+    const uint64_t nm2 = pk2(-mean, -mean);
 #pragma unroll
-    for (int i = 0; i < KH; ++i) {
-        v[i] -= mean;
-        q += v[i] * v[i];
+    for (int i = 0; i < KH; i += 2) {
+        const float2 d = upk2(add2(pk2(v[i], v[i + 1]), nm2));
+        v[i] = d.x;
+        v[i + 1] = d.y;
     }
-    red[(2 + g) * BM + t] = q;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint64_t d = pk2(v[2 * i], v[2 * i + 1]);
+        acc[i] = mul2(d, d);
+    }
+#pragma unroll
+    for (int i = 8; i < KH; i += 2) {
+        const uint64_t d = pk2(v[i], v[i + 1]);
+        acc[(i >> 1) & 3] = fma2(d, d, acc[(i >> 1) & 3]);
+    }
+    sp2 = upk2(add2(add2(acc[0], acc[1]), add2(acc[2], acc[3])));
+    red[(2 + g) * BM + t] = sp2.x + sp2.y;
     workers_sync();
     const float rstd = rsqrtf((red[2 * BM + t] + red[3 * BM + t]) * (1.f / K) + eps);
+    const uint64_t r2 = pk2(rstd, rstd);
 #pragma unroll
     for (int ch = 0; ch < KH / 8; ++ch) {
+        const int c0 = g * KH + 8 * ch;
+        // this 8-column chunk's scale and offset, 16-byte loads (broadcast across the warp)
+        const float4 s0 = *reinterpret_cast<const float4*>(scale + c0);
+        const float4 s1 = *reinterpret_cast<const float4*>(scale + c0 + 4);
+        const float4 o0 = *reinterpret_cast<const float4*>(offset + c0);
+        const float4 o1 = *reinterpret_cast<const float4*>(offset + c0 + 4);
+        const float sc[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+        const float of[8] = {o0.x, o0.y, o0.z, o0.w, o1.x, o1.y, o1.z, o1.w};
         uint32_t w[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-            const int c = g * KH + 8 * ch + 2 * e;
-            const float y0 = v[8 * ch + 2 * e] * rstd * scale[c] + offset[c];
-            const float y1 = v[8 * ch + 2 * e + 1] * rstd * scale[c + 1] + offset[c + 1];
-            w[e] = E::pack(y0, y1);
+            const int i = 8 * ch + 2 * e;
+            const uint64_t y = fma2(mul2(pk2(v[i], v[i + 1]), r2),
+                                    pk2(sc[2 * e], sc[2 * e + 1]), pk2(of[2 * e], of[2 * e + 1]));
+            const float2 yf = upk2(y);
+            w[e] = E::pack(yf.x, yf.y);
             if (y_out != nullptr) {
                 const float2 r = E::unpack(w[e]);
-                y_out[8 * ch + 2 * e] = r.x;
-                y_out[8 * ch + 2 * e + 1] = r.y;
+                y_out[i] = r.x;
+                y_out[i + 1] = r.y;
             }
         }
-        *reinterpret_cast<uint4*>(tile + sw128(t, g * KH + 8 * ch)) =
-            make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(tile + sw128(t, c0)) = make_uint4(w[0], w[1], w[2], w[3]);
     }
 }
 

@@ -331,20 +331,29 @@ struct LnGdpOp {
             if (m >= a.M) {
                 continue;
             }
+            // two rows an instruction (paired fp32): mask * (p + bp) * sigmoid(g + bg) with
+            // sigmoid(x) = (1 + tanh(x / 2)) / 2
+            const uint64_t bp2 = pk2(bpv, bpv), hbg2 = pk2(0.5f * bgv, 0.5f * bgv);
+            const uint64_t half2 = pk2(0.5f, 0.5f);
             uint32_t w[16];
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
                 const float4 mk = *reinterpret_cast<const float4*>(regs.maskv + r0 + 4 * q);
-                const float mm[4] = {mk.x, mk.y, mk.z, mk.w};
-                float o[4];
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
+                for (int e = 0; e < 4; e += 2) {
                     const int i = 4 * q + e;
-                    o[e] = mm[e] * (__uint_as_float(pr[i]) + bpv) *
-                           sigmoid_fast(__uint_as_float(gr[i]) + bgv);
+                    const uint64_t pv =
+                        add2(pk2(__uint_as_float(pr[i]), __uint_as_float(pr[i + 1])), bp2);
+                    const float2 hg = upk2(fma2(
+                        pk2(__uint_as_float(gr[i]), __uint_as_float(gr[i + 1])), half2, hbg2));
+                    float t0, t1;
+                    asm("tanh.approx.f32 %0, %1;" : "=f"(t0) : "f"(hg.x));
+                    asm("tanh.approx.f32 %0, %1;" : "=f"(t1) : "f"(hg.y));
+                    const uint64_t sg = fma2(pk2(t0, t1), half2, half2);
+                    const uint64_t mm = e == 0 ? pk2(mk.x, mk.y) : pk2(mk.z, mk.w);
+                    const float2 o = upk2(mul2(mul2(mm, pv), sg));
+                    w[2 * q + e / 2] = E::pack(o.x, o.y);
                 }
-                w[2 * q] = E::pack(o[0], o[1]);
-                w[2 * q + 1] = E::pack(o[2], o[3]);
             }
             if (a.vec_store && m + 32 <= a.M) {
                 uint4* dst = reinterpret_cast<uint4*>(out + m);

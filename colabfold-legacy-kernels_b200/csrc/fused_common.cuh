@@ -97,6 +97,14 @@ __device__ __forceinline__ int tile_work_of(const float (&v)[BM / 32]) {
     return __any_sync(0xffffffffu, zero) ? kPadding : kSkip;
 }
 
+// One 32-byte store (sm_100's 256-bit vector store): half the store instructions, and half the
+// separate segments a warp's row-strided stores put through the memory pipeline
+__device__ __forceinline__ void st_global_v8(void* p, const uint4& lo, const uint4& hi) {
+    asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(lo.x),
+                 "r"(lo.y), "r"(lo.z), "r"(lo.w), "r"(hi.x), "r"(hi.y), "r"(hi.z), "r"(hi.w)
+                 : "memory");
+}
+
 // Barrier among the 256 workers (id 1).
 __device__ __forceinline__ void workers_sync() {
     named_sync(1, kWorkers);

@@ -355,7 +355,14 @@ struct LnGdpOp {
                     w[2 * q + e / 2] = E::pack(o.x, o.y);
                 }
             }
-            if (a.vec_store && m + 32 <= a.M) {
+            if (a.vec_store == 2 && m + 32 <= a.M) {
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    st_global_v8(out + m + 16 * q,
+                                 make_uint4(w[8 * q], w[8 * q + 1], w[8 * q + 2], w[8 * q + 3]),
+                                 make_uint4(w[8 * q + 4], w[8 * q + 5], w[8 * q + 6], w[8 * q + 7]));
+                }
+            } else if (a.vec_store == 1 && m + 32 <= a.M) {
                 uint4* dst = reinterpret_cast<uint4*>(out + m);
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
@@ -400,7 +407,7 @@ struct ProjOp {
         const float *scale, *offset;
         T *out, *bias;
         int M, n, ldp, heads;
-        int w_bytes, param_floats;
+        int w_bytes, param_floats, v8;  // v8: 32-byte output stores allowed
         float eps;
     };
     struct Regs {
@@ -526,8 +533,14 @@ struct ProjOp {
                 for (int e = 0; e < 8; ++e) {
                     w[e] = E::pack(v[2 * e], v[2 * e + 1]);
                 }
-                *reinterpret_cast<uint4*>(orow + c0) = make_uint4(w[0], w[1], w[2], w[3]);
-                *reinterpret_cast<uint4*>(orow + c0 + 8) = make_uint4(w[4], w[5], w[6], w[7]);
+                if (a.v8) {
+                    st_global_v8(orow + c0, make_uint4(w[0], w[1], w[2], w[3]),
+                                 make_uint4(w[4], w[5], w[6], w[7]));
+                } else {
+                    *reinterpret_cast<uint4*>(orow + c0) = make_uint4(w[0], w[1], w[2], w[3]);
+                    *reinterpret_cast<uint4*>(orow + c0 + 8) =
+                        make_uint4(w[4], w[5], w[6], w[7]);
+                }
             }
         }
     }
@@ -571,7 +584,7 @@ struct TrimulOp {
         const T *x, *woT, *bo, *wgT, *bg, *keep;
         const float *in_scale, *in_offset, *ln_scale, *ln_offset;
         T* out;
-        int M, w_bytes, param_floats;
+        int M, w_bytes, param_floats, v8;  // v8: 32-byte output stores allowed
         float eps;
     };
     struct Regs {
@@ -708,8 +721,14 @@ struct TrimulOp {
                 for (int e = 0; e < 8; ++e) {
                     w[e] = E::pack(v[2 * e], v[2 * e + 1]);
                 }
-                *reinterpret_cast<uint4*>(orow + c0) = make_uint4(w[0], w[1], w[2], w[3]);
-                *reinterpret_cast<uint4*>(orow + c0 + 8) = make_uint4(w[4], w[5], w[6], w[7]);
+                if (a.v8) {
+                    st_global_v8(orow + c0, make_uint4(w[0], w[1], w[2], w[3]),
+                                 make_uint4(w[4], w[5], w[6], w[7]));
+                } else {
+                    *reinterpret_cast<uint4*>(orow + c0) = make_uint4(w[0], w[1], w[2], w[3]);
+                    *reinterpret_cast<uint4*>(orow + c0 + 8) =
+                        make_uint4(w[4], w[5], w[6], w[7]);
+                }
             }
         };
         // unrolled where the registers allow (C = 128 keeps a wider prologue state)
@@ -1212,8 +1231,9 @@ cudaError_t ln_gdp_typed(cudaStream_t stream, int dtype, const void* x, const fl
     a.M = M;
     a.w_bytes = 2 * Op::P * K * 2;
     a.param_floats = 2 * K + 2 * Op::P;
-    a.vec_store = M % 8 == 0 && (reinterpret_cast<uintptr_t>(left) & 15) == 0 &&
-                  (reinterpret_cast<uintptr_t>(right) & 15) == 0;
+    // 2: 32-byte stores, 1: 16-byte stores, 0: element stores
+    const uintptr_t lr = reinterpret_cast<uintptr_t>(left) | reinterpret_cast<uintptr_t>(right);
+    a.vec_store = M % 16 == 0 && (lr & 31) == 0 ? 2 : M % 8 == 0 && (lr & 15) == 0 ? 1 : 0;
     a.eps = eps;
     return launch_op<Op>(stream, tx, tw0, tw1, a);
 }
@@ -1250,6 +1270,7 @@ cudaError_t proj_typed(cudaStream_t stream, int dtype, const void* x, const floa
     a.n = n;
     a.ldp = ldp;
     a.heads = heads;
+    a.v8 = ldp % 16 == 0 && (reinterpret_cast<uintptr_t>(out) & 31) == 0;
     a.w_bytes = n * K * 2;
     a.param_floats = 2 * K + n + 8 * K;
     a.eps = eps;
@@ -1283,6 +1304,7 @@ cudaError_t trimul_typed(cudaStream_t stream, int dtype, const float* x_cm, cons
     a.ln_offset = ln_offset;
     a.out = static_cast<T*>(out);
     a.M = M;
+    a.v8 = (reinterpret_cast<uintptr_t>(out) & 31) == 0;
     a.w_bytes = (O * C + O * CA) * 2;
     a.param_floats = 2 * CA + 2 * C + 2 * O;
     a.eps = eps;

@@ -204,6 +204,80 @@ __device__ __forceinline__ void ln_rows_half(uint8_t* tile, int t, int g, const 
     }
 }
 
+// LayerNorm of row t in place on a swizzled tile, the whole row by one thread (no exchange, no
+// barrier): three passes over the row in shared memory (sum, centred sum of squares, then the
+// normalised row rounded to T and written back), so the row never sits in registers.
+// use(ch, y[8]) sees the rounded outputs of every 8-column chunk (the per-head bias of
+// ln_projection).
+template <typename T, int K, typename Use>
+__device__ __forceinline__ void ln_row_full(uint8_t* tile, int t, const float* scale,
+                                            const float* offset, float eps, Use&& use) {
+    using E = Elem<T>;
+    uint64_t acc[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        acc[i] = pk2(0.f, 0.f);
+    }
+#pragma unroll 4
+    for (int ch = 0; ch < K / 8; ++ch) {
+        const uint4 w = *reinterpret_cast<const uint4*>(tile + sw128(t, 8 * ch));
+        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float2 f = E::unpack(ww[e]);
+            acc[e] = add2(acc[e], pk2(f.x, f.y));
+        }
+    }
+    float2 r = upk2(add2(add2(acc[0], acc[1]), add2(acc[2], acc[3])));
+    const float mean = (r.x + r.y) * (1.f / K);
+    const uint64_t nm2 = pk2(-mean, -mean);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        acc[i] = pk2(0.f, 0.f);
+    }
+#pragma unroll 4
+    for (int ch = 0; ch < K / 8; ++ch) {
+        const uint4 w = *reinterpret_cast<const uint4*>(tile + sw128(t, 8 * ch));
+        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float2 f = E::unpack(ww[e]);
+            const uint64_t d = add2(pk2(f.x, f.y), nm2);
+            acc[e] = fma2(d, d, acc[e]);
+        }
+    }
+    r = upk2(add2(add2(acc[0], acc[1]), add2(acc[2], acc[3])));
+    const float rstd = rsqrtf((r.x + r.y) * (1.f / K) + eps);
+    const uint64_t r2 = pk2(rstd, rstd);
+#pragma unroll 4
+    for (int ch = 0; ch < K / 8; ++ch) {
+        uint8_t* p = tile + sw128(t, 8 * ch);
+        const uint4 w = *reinterpret_cast<const uint4*>(p);
+        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+        const float4 s0 = *reinterpret_cast<const float4*>(scale + 8 * ch);
+        const float4 s1 = *reinterpret_cast<const float4*>(scale + 8 * ch + 4);
+        const float4 o0 = *reinterpret_cast<const float4*>(offset + 8 * ch);
+        const float4 o1 = *reinterpret_cast<const float4*>(offset + 8 * ch + 4);
+        const float sc[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+        const float of[8] = {o0.x, o0.y, o0.z, o0.w, o1.x, o1.y, o1.z, o1.w};
+        uint32_t o[4];
+        float yr[8];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float2 f = E::unpack(ww[e]);
+            const uint64_t y = fma2(mul2(add2(pk2(f.x, f.y), nm2), r2),
+                                    pk2(sc[2 * e], sc[2 * e + 1]), pk2(of[2 * e], of[2 * e + 1]));
+            const float2 yf = upk2(y);
+            o[e] = E::pack(yf.x, yf.y);
+            const float2 rr = E::unpack(o[e]);
+            yr[2 * e] = rr.x;
+            yr[2 * e + 1] = rr.y;
+        }
+        use(ch, yr);
+        *reinterpret_cast<uint4*>(p) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+}
+
 // sigmoid(g) = (1 + tanh(g/2)) / 2: one MUFU operation (tanh.approx, relative error ~2^-11)
 // instead of an exponential and a reciprocal
 __device__ __forceinline__ float sigmoid_fast(float g) {

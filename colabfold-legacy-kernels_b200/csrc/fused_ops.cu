@@ -27,9 +27,12 @@ using namespace fused;
 // ---------------------------------------------------------------------------------------------
 // The accumulators live in a ring of Op::kSlots blocks of Op::kSlotCols tensor-memory columns: the MMA
 // warp fills block j+1.. while the workers drain block j, so neither side waits for a whole
-// tile. Op supplies: T, Args (M, w_bytes, param_floats, eps), keep(), kOther, X_BYTES,
+// tile. With Op::kPingPong the two worker warpgroups take the tiles in turn (tile c to
+// warpgroup c % 2, which uses x stage c % 2), each doing a tile's whole prologue and epilogue, so
+// one tile's LayerNorm overlaps the other's epilogue; otherwise both split every tile.
+// Op supplies: T, Args (M, w_bytes, param_floats, eps), keep(), kOther, X_BYTES,
 // RED_FLOATS, nblocks(), load_params, load_weights, load_x, issue_block, prologue,
-// epilogue_block, prefetch_block, padding, Regs.
+// epilogue_block, prefetch_block, padding, Regs, kPingPong, kSlots, kSlotCols.
 
 template <class Op>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -43,8 +46,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* ws = smem + 2 * Op::X_BYTES;
     float* sp = reinterpret_cast<float*>(ws + a.w_bytes);
     float* red = sp + a.param_floats;  // [Op::RED_FLOATS]
-    __shared__ uint64_t x_full[2], x_empty[2], a_ready[2], acc_full[kSlots], acc_empty[kSlots],
-        w_full;
+    // accumulator slot barriers per warpgroup that consumes the slot's block (both ping-pong
+    // warpgroups pass blocks through the same slots; one barrier each keeps every barrier's
+    // phases in one consumer's order, so no waiter can be two phases ahead)
+    constexpr int kTeams = Op::kPingPong ? 2 : 1;
+    __shared__ uint64_t x_full[2], x_empty[2], a_ready[2], acc_full[kTeams][kSlots],
+        acc_empty[kTeams][kSlots], w_full;
     __shared__ uint32_t tmem_sh;
     __shared__ int abort_flag;
 
@@ -53,14 +60,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int nb = Op::nblocks(a);
     if (warp == kProducerWarp) {
         if (lane == 0) {
+            // ping-pong ops: one worker warpgroup per tile (the two take the tiles in turn)
+            constexpr int kTeam = Op::kPingPong ? kWorkers / 2 : kWorkers;
             for (int i = 0; i < 2; ++i) {
                 mbar_init(&x_full[i], 1);
                 mbar_init(&x_empty[i], 1);
-                mbar_init(&a_ready[i], kWorkers);
+                mbar_init(&a_ready[i], kTeam);
             }
-            for (int i = 0; i < kSlots; ++i) {
-                mbar_init(&acc_full[i], 1);
-                mbar_init(&acc_empty[i], kWorkers);
+            for (int tm = 0; tm < kTeams; ++tm) {
+                for (int i = 0; i < kSlots; ++i) {
+                    mbar_init(&acc_full[tm][i], 1);
+                    mbar_init(&acc_empty[tm][i], kTeam);
+                }
             }
             mbar_init(&w_full, 1);
             abort_flag = 0;
@@ -89,6 +100,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             return -1;
         };
         int cur = blockIdx.x, pcur = blockIdx.x, c = 0, q = 0;
+        int empty_seen[2 * kSlots] = {};  // acc_empty phases waited for, per (team, slot)
         if (lane == 0) {
             Op::load_weights(a, &tw0, &tw1, ws, &w_full);
         }
@@ -115,16 +127,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 mbar_wait(&a_ready[s], (c >> 1) & 1, &g_status, kStatusSyncWait, &abort_flag);
                 tc_fence_after();
+                const int team = kTeams == 2 ? (c & 1) : 0;
                 for (int j = 0; j < nb; ++j, ++q) {
                     const int slot = q % kSlots;
                     if (q >= kSlots) {
-                        mbar_wait(&acc_empty[slot], ((q - kSlots) / kSlots) & 1, &g_status,
-                                  kStatusSyncWait, &abort_flag);
+                        // the slot's previous block: consumed by its warpgroup (the n-th of that
+                        // warpgroup's blocks in this slot completes the barrier's n-th phase)
+                        const int pt = kTeams == 2 ? (((q - kSlots) / nb) & 1) : 0;
+                        const int n_prev = empty_seen[pt * kSlots + slot]++;
+                        mbar_wait(&acc_empty[pt][slot], n_prev & 1, &g_status, kStatusSyncWait,
+                                  &abort_flag);
                         tc_fence_after();
                     }
                     Op::issue_block(a, smem_u32(xs0 + s * Op::X_BYTES), smem_u32(ws),
                                     tmem + slot * kSlotCols, j);
-                    mma_commit(&acc_full[slot]);
+                    mma_commit(&acc_full[team][slot]);
                 }
                 mma_commit(&x_empty[s]);
             } else {
@@ -146,6 +163,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t lane_base = tmem_lane_base(warp);
         typename Op::Regs regs{};
         int c = 0, q = 0;
+        int full_seen[kSlots] = {};  // acc_full phases this warpgroup waited for, per slot
         // the keep values of the worker's next tile load a tile ahead (the classification's
         // global loads would otherwise stall every tile); a worker's own row value is also
         // handed to the op (ln_gdp's row mask)
@@ -164,21 +182,30 @@ __global__ void __launch_bounds__(kThreads, 1)
                 continue;
             }
             const int s = c & 1;
+            if constexpr (Op::kPingPong) {
+                if (s != g) {  // the other warpgroup's tile
+                    q += nb;
+                    ++c;
+                    continue;
+                }
+            }
             uint8_t* stage = xs0 + s * Op::X_BYTES;
             mbar_wait(&x_full[s], (c >> 1) & 1, &g_status, kStatusTmaWait, &abort_flag);
             Op::prologue(a, stage, sp, red, t, g, m0, regs);
             fence_async_smem();
             mbar_arrive(&a_ready[s]);
+            const int team = kTeams == 2 ? g : 0;
             for (int j = 0; j < nb; ++j, ++q) {
                 const int slot = q % kSlots;
                 // global inputs of the block's epilogue start loading before the MMA wait
                 Op::prefetch_block(a, t, g, m0, j, regs);
-                mbar_wait(&acc_full[slot], (q / kSlots) & 1, &g_status, kStatusMmaWait,
+                const int n_full = full_seen[slot]++;  // this warpgroup's blocks in the slot
+                mbar_wait(&acc_full[team][slot], n_full & 1, &g_status, kStatusMmaWait,
                           &abort_flag);
                 tc_fence_after();
                 Op::epilogue_block(a, tmem + slot * kSlotCols + lane_base, sp, t, g, m0, j, regs);
                 tc_fence_before();
-                mbar_arrive(&acc_empty[slot]);
+                mbar_arrive(&acc_empty[team][slot]);
             }
             ++c;
         }
@@ -252,8 +279,9 @@ struct LnGdpOp {
     static constexpr int P = 2 * CI;
     static constexpr int X_BYTES = K * BM * 2;
     static constexpr float kOther = 0.f;
-    // LN sums, then the tile's row mask max(mask, 0) in two buffers (tile parity)
-    static constexpr int RED_FLOATS = 4 * BM + 2 * BM;
+    // the tile's row mask max(mask, 0): per warpgroup two buffers (its tile parity)
+    static constexpr int RED_FLOATS = 4 * BM;
+    static constexpr bool kPingPong = true;
     // the outputs are channel major, so the product is computed transposed (lanes = channels):
     // a block is 128 channels, the projection in the slot's columns [0, 128) and the gate in
     // [128, 256), one column per row of the tile
@@ -300,29 +328,29 @@ struct LnGdpOp {
         mma_cols(acc, wa, P, 128 * j, xa, K, E::kBf16);
         mma_cols(acc + 128, wa + P * K * 2, P, 128 * j, xa, K, E::kBf16);
     }
+    // warpgroup g's tile: LayerNorm of row t (the whole row), the row mask into shared memory
+    // (two buffers a warpgroup: its previous tile's epilogue may still read the other one),
+    // then a barrier of the warpgroup, whose epilogue threads read every row's mask
     static __device__ void prologue(const Args& a, uint8_t* stage, const float* sp, float* red,
                                     int t, int g, int m0, Regs& regs) {
-        // the row mask of the tile, visible to all workers after the LayerNorm's barriers;
-        // two buffers, as the epilogue of the previous tile may still read the other one
-        float* mv = red + 4 * BM + regs.parity * BM;
-        if (g == 0) {
-            mv[t] = m0 + t < a.M ? fmaxf(regs.row_mask, 0.f) : 0.f;
-        }
+        float* mv = red + (2 * g + regs.parity) * BM;
+        mv[t] = m0 + t < a.M ? fmaxf(regs.row_mask, 0.f) : 0.f;
         regs.maskv = mv;
         regs.parity ^= 1;
-        ln_rows_half<T, K>(stage, t, g, sp, sp + K, a.eps, red, nullptr, nullptr);
+        ln_row_full<T, K>(stage, t, sp, sp + K, a.eps, [](int, const float*) {});
+        named_sync(2 + g, 128);
     }
     static __device__ void prefetch_block(const Args&, int, int, int, int, Regs&) {}
-    // worker (g, t): channel 128j + t (TMEM lane t), the tile's rows [64g, 64g + 64) in two
-    // runs of 32, each stored as 64 contiguous bytes of the channel-major output
+    // worker t of the tile's warpgroup: channel 128j + t (TMEM lane t), the tile's 128 rows in
+    // four runs of 32, each stored as 64 contiguous bytes of the channel-major output
     static __device__ void epilogue_block(const Args& a, uint32_t acc, const float* sp, int t,
                                           int g, int m0, int j, Regs& regs) {
         const int ch = 128 * j + t;
         const float bpv = sp[2 * K + ch], bgv = sp[2 * K + P + ch];
         T* out = ch < CI ? a.left + (long long)ch * a.M : a.right + (long long)(ch - CI) * a.M;
 #pragma unroll 1
-        for (int cc = 0; cc < 2; ++cc) {
-            const int r0 = 64 * g + 32 * cc;
+        for (int cc = 0; cc < 4; ++cc) {
+            const int r0 = 32 * cc;
             uint32_t pr[32], gr[32];
             tmem_ld32(acc + r0, pr);
             tmem_ld32(acc + 128 + r0, gr);
@@ -399,9 +427,10 @@ struct ProjOp {
     using T = T_;
     using E = Elem<T>;
     static constexpr int kSlots = 4, kSlotCols = 128;
+    static constexpr bool kPingPong = true;
     static constexpr int X_BYTES = K * BM * 2;
     static constexpr float kOther = -1.f;
-    static constexpr int RED_FLOATS = 4 * BM + 16 * BM;  // LN sums + per-head halves
+    static constexpr int RED_FLOATS = 4;  // unused: a row's LayerNorm is one thread's
     struct Args {
         const T *x, *wT, *b, *residual, *wbT, *keep;
         const float *scale, *offset;
@@ -446,34 +475,45 @@ struct ProjOp {
         const int n0 = 128 * j, N = a.n - n0 < 128 ? a.n - n0 : 128;
         mma_rows(acc, xa, wa, a.n, K, n0, N, E::kBf16, false);
     }
+    // warpgroup g's tile: LayerNorm of row t (the whole row) and, with heads, the per-head
+    // bias: a row reduction over the rounded LN(x) (wb rows in shared memory, 16-byte reads)
     static __device__ void prologue(const Args& a, uint8_t* stage, const float* sp, float* red,
                                     int t, int g, int m0, Regs&) {
         if constexpr (LN) {
-            float y[K / 2];
-            ln_rows_half<T, K>(stage, t, g, sp, sp + K, a.eps, red, nullptr, y);
-            if (a.heads > 0) {
-                // the per-head bias: a row reduction over the rounded LN(x), halves summed
-                const float* wb = sp + 2 * K + a.n;
-                float* hred = red + 4 * BM;
-                for (int h = 0; h < a.heads; ++h) {
-                    float d = 0.f;
+            const float* wb = sp + 2 * K + a.n;
+            const int heads = a.heads;
+            float hd[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            ln_row_full<T, K>(stage, t, sp, sp + K, a.eps, [&](int ch, const float* y) {
 #pragma unroll
-                    for (int i = 0; i < K / 2; ++i) {
-                        d = fmaf(y[i], wb[h * K + g * (K / 2) + i], d);
+                for (int h = 0; h < 8; ++h) {
+                    if (h < heads) {
+                        const float4 w0 = *reinterpret_cast<const float4*>(wb + h * K + 8 * ch);
+                        const float4 w1 =
+                            *reinterpret_cast<const float4*>(wb + h * K + 8 * ch + 4);
+                        float d = hd[h];
+                        d = fmaf(y[0], w0.x, d);
+                        d = fmaf(y[1], w0.y, d);
+                        d = fmaf(y[2], w0.z, d);
+                        d = fmaf(y[3], w0.w, d);
+                        d = fmaf(y[4], w1.x, d);
+                        d = fmaf(y[5], w1.y, d);
+                        d = fmaf(y[6], w1.z, d);
+                        d = fmaf(y[7], w1.w, d);
+                        hd[h] = d;
                     }
-                    hred[(h * 2 + g) * BM + t] = d;
                 }
-                workers_sync();
-                if (g == 0 && m0 + t < a.M) {
-                    for (int h = 0; h < a.heads; ++h) {
-                        a.bias[(long long)h * a.M + m0 + t] =
-                            E::from_f(hred[(h * 2) * BM + t] + hred[(h * 2 + 1) * BM + t]);
+            });
+            if (m0 + t < a.M) {
+#pragma unroll
+                for (int h = 0; h < 8; ++h) {
+                    if (h < heads) {
+                        a.bias[(long long)h * a.M + m0 + t] = E::from_f(hd[h]);
                     }
                 }
             }
         }
     }
-    // the residual of worker half g's columns of block j, loaded ahead of the MMA wait
+    // the residual of row t's first 64 columns of block j, loaded ahead of the MMA wait
     static __device__ void prefetch_block(const Args& a, int t, int g, int m0, int j,
                                           Regs& regs) {
         const int m = m0 + t;
@@ -481,28 +521,36 @@ struct ProjOp {
             return;
         }
         const int width = a.n - 128 * j < 128 ? a.n - 128 * j : 128;
-        const int half = width / 2;
-        const uint4* rr = reinterpret_cast<const uint4*>(a.residual + (long long)m * a.ldp +
-                                                         128 * j + g * half);
+        const uint4* rr =
+            reinterpret_cast<const uint4*>(a.residual + (long long)m * a.ldp + 128 * j);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            if (8 * i < half) {
+            if (8 * i < width) {
                 regs.res[i] = rr[i];
             }
         }
     }
-    // worker half g: columns 128j + g w/2 + [0, w/2) of the block's width w
+    // worker t of the tile's warpgroup: row t, every column 128j + [0, w) of the block's width w
     static __device__ void epilogue_block(const Args& a, uint32_t acc, const float* sp, int t,
                                           int g, int m0, int j, Regs& regs) {
         const int m = m0 + t;
         const int width = a.n - 128 * j < 128 ? a.n - 128 * j : 128;
-        const int half = width / 2;
         const float* b = sp + 2 * K + 128 * j;
         T* orow = a.out + (long long)m * a.ldp + 128 * j;
+        // the residual of columns [64, 128) loads while the first 64 are done
+        uint4 res2[8];
+        if (a.residual != nullptr && m < a.M && width > 64) {
+            const uint4* rr = reinterpret_cast<const uint4*>(a.residual + (long long)m * a.ldp +
+                                                             128 * j + 64);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int c0 = g * half + 16 * i;
-            if (16 * i >= half) {
+            for (int i = 0; i < 8; ++i) {
+                res2[i] = rr[i];
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int c0 = 16 * i;
+            if (c0 >= width) {
                 break;
             }
             uint32_t r[16];
@@ -519,7 +567,8 @@ struct ProjOp {
                     v[4 * q + 3] = __uint_as_float(r[4 * q + 3]) + bb.w;
                 }
                 if (a.residual != nullptr) {
-                    const uint4 q0 = regs.res[2 * i], q1 = regs.res[2 * i + 1];
+                    const uint4 q0 = i < 4 ? regs.res[2 * i] : res2[2 * i - 8];
+                    const uint4 q1 = i < 4 ? regs.res[2 * i + 1] : res2[2 * i - 7];
                     const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
                     for (int e = 0; e < 8; ++e) {
@@ -574,6 +623,7 @@ template <typename T_, int C, int CA, int O, bool ADD>
 struct TrimulOp {
     using T = T_;
     using E = Elem<T>;
+    static constexpr bool kPingPong = false;
     static constexpr int kSlots = 4, kSlotCols = 128;
     static constexpr int X_BYTES = (C + CA) * BM * 2;
     static constexpr int XOFF = C * BM * 2;  // x's atoms after Y's

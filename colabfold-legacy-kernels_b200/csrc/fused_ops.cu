@@ -839,6 +839,7 @@ struct TransArgs {
     int M, H;
     float eps;
     bool add;
+    int v8;  // 32-byte output stores allowed
 };
 
 template <typename T, int C>
@@ -1053,45 +1054,8 @@ __global__ void __launch_bounds__(TransCfg<C>::THREADS, 1)
             mbar_wait(&x_full, c & 1, &g_status, kStatusTmaWait, &abort_flag);
             uint8_t* tile_s = xs + s * BM * C * 2;
             if constexpr (SUB == 2) {
-                // a full row per worker: plain two-pass LN, no exchange
-                using Ev = Elem<T>;
-                float v[C];
-#pragma unroll
-                for (int ch = 0; ch < C / 8; ++ch) {
-                    const uint4 u = *reinterpret_cast<const uint4*>(tile_s + sw128(t, 8 * ch));
-                    const uint32_t uw[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const float2 f = Ev::unpack(uw[e]);
-                        v[8 * ch + 2 * e] = f.x;
-                        v[8 * ch + 2 * e + 1] = f.y;
-                    }
-                }
-                float sum = 0.f;
-#pragma unroll
-                for (int i = 0; i < C; ++i) {
-                    sum += v[i];
-                }
-                const float mean = sum * (1.f / C);
-                float sq = 0.f;
-#pragma unroll
-                for (int i = 0; i < C; ++i) {
-                    v[i] -= mean;
-                    sq += v[i] * v[i];
-                }
-                const float rstd = rsqrtf(sq * (1.f / C) + a.eps);
-#pragma unroll
-                for (int ch = 0; ch < C / 8; ++ch) {
-                    uint32_t ww[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int cc = 8 * ch + 2 * e;
-                        ww[e] = Ev::pack(v[cc] * rstd * sp[cc] + sp[C + cc],
-                                         v[cc + 1] * rstd * sp[cc + 1] + sp[C + cc + 1]);
-                    }
-                    *reinterpret_cast<uint4*>(tile_s + sw128(t, 8 * ch)) =
-                        make_uint4(ww[0], ww[1], ww[2], ww[3]);
-                }
+                // a full row per worker, no exchange
+                ln_row_full<T, C>(tile_s, t, sp, sp + C, a.eps, [](int, const float*) {});
             } else {
                 ln_rows_half<T, C>(tile_s, t, g, sp, sp + C, a.eps, red, nullptr, nullptr);
             }
@@ -1140,27 +1104,55 @@ __global__ void __launch_bounds__(TransCfg<C>::THREADS, 1)
                 tc_fence_before();
                 mbar_arrive(&hid_ready[b]);
             }
+            // the residual (x as it came in) of this worker's columns, loaded before the wait for
+            // the second GEMM (up to 128 columns, 16 x 16 bytes)
+            constexpr int RC = SUB == 2 ? C : C / 2;   // columns a worker stores
+            constexpr int RPRE = RC <= 128 && C <= 128 ? RC : 0;  // of them prefetched
+            uint4 res[RPRE / 8 > 0 ? RPRE / 8 : 1];
+            if constexpr (RPRE > 0) {
+                const int c0 = SUB == 2 ? 0 : g * (C / 2);
+                if (a.add && m < a.M) {
+                    const uint4* xr = reinterpret_cast<const uint4*>(a.x + (long long)m * C + c0);
+#pragma unroll
+                    for (int i = 0; i < RPRE / 8; ++i) {
+                        res[i] = xr[i];
+                    }
+                }
+            }
             mbar_wait(&acc2_full, c & 1, &g_status, kStatusMmaWait, &abort_flag);
             tc_fence_after();
             {
                 const uint32_t acc = tmem + G::ACC2 + s * C + lane_base;
-                const int c0 = SUB == 2 ? 0 : g * (C / 2), c1 = SUB == 2 ? C : c0 + C / 2;
+                const int c0 = SUB == 2 ? 0 : g * (C / 2);
                 T* orow = a.out + (long long)m * C;
-                const T* xrow = a.x + (long long)m * C;
-#pragma unroll 1
-                for (int cc = c0; cc < c1; cc += 16) {
+#pragma unroll
+                for (int ci = 0; ci < RC / 16; ++ci) {
+                    const int cc = c0 + 16 * ci;
                     uint32_t r[16];
                     tmem_ld16(acc + cc, r);
                     tmem_wait_ld();
                     if (m < a.M) {
                         float v[16];
 #pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            v[i] = __uint_as_float(r[i]) + sp[2 * C + cc + i];
+                        for (int q4 = 0; q4 < 4; ++q4) {
+                            const float4 bb =
+                                *reinterpret_cast<const float4*>(sp + 2 * C + cc + 4 * q4);
+                            v[4 * q4] = __uint_as_float(r[4 * q4]) + bb.x;
+                            v[4 * q4 + 1] = __uint_as_float(r[4 * q4 + 1]) + bb.y;
+                            v[4 * q4 + 2] = __uint_as_float(r[4 * q4 + 2]) + bb.z;
+                            v[4 * q4 + 3] = __uint_as_float(r[4 * q4 + 3]) + bb.w;
                         }
                         if (a.add) {
-                            const uint4 q0 = *reinterpret_cast<const uint4*>(xrow + cc);
-                            const uint4 q1 = *reinterpret_cast<const uint4*>(xrow + cc + 8);
+                            uint4 q0, q1;
+                            if constexpr (RPRE > 0) {
+                                q0 = res[2 * ci];
+                                q1 = res[2 * ci + 1];
+                            } else {
+                                const uint4* xr =
+                                    reinterpret_cast<const uint4*>(a.x + (long long)m * C + cc);
+                                q0 = xr[0];
+                                q1 = xr[1];
+                            }
                             const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w,
                                                     q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
@@ -1175,9 +1167,15 @@ __global__ void __launch_bounds__(TransCfg<C>::THREADS, 1)
                         for (int e = 0; e < 8; ++e) {
                             ww[e] = E::pack(v[2 * e], v[2 * e + 1]);
                         }
-                        *reinterpret_cast<uint4*>(orow + cc) = make_uint4(ww[0], ww[1], ww[2], ww[3]);
-                        *reinterpret_cast<uint4*>(orow + cc + 8) =
-                            make_uint4(ww[4], ww[5], ww[6], ww[7]);
+                        if (a.v8) {
+                            st_global_v8(orow + cc, make_uint4(ww[0], ww[1], ww[2], ww[3]),
+                                         make_uint4(ww[4], ww[5], ww[6], ww[7]));
+                        } else {
+                            *reinterpret_cast<uint4*>(orow + cc) =
+                                make_uint4(ww[0], ww[1], ww[2], ww[3]);
+                            *reinterpret_cast<uint4*>(orow + cc + 8) =
+                                make_uint4(ww[4], ww[5], ww[6], ww[7]);
+                        }
                     }
                 }
             }
@@ -1421,6 +1419,7 @@ cudaError_t transition_typed(cudaStream_t stream, int dtype, const void* x, cons
     a.H = H;
     a.eps = eps;
     a.add = add;
+    a.v8 = (reinterpret_cast<uintptr_t>(out) & 31) == 0;
     auto kern = transition_kernel<T, C>;
     const int smem = G::X_BYTES + G::NSLOT * G::SLOT + (3 * C + H + 4 * BM) * 4 + 1024;
     const cudaError_t e =

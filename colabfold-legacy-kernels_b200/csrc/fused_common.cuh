@@ -105,6 +105,93 @@ __device__ __forceinline__ void st_global_v8(void* p, const uint4& lo, const uin
                  : "memory");
 }
 
+// Output tiles leave through TMA stores (shared memory to L2, no pass through L1): a worker warp
+// writes its 32 rows' chunk into a staging buffer, fences it for the async proxy, and lane 0
+// stores the box and commits it as one bulk group.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int c0,
+                                             int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+            map),
+        "r"(src), "r"(c0), "r"(c1)
+        : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// until at most N of this thread's committed bulk groups still read shared memory
+template <int N>
+__device__ __forceinline__ void bulk_wait_reads() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+// until every bulk group this thread committed has completed (writes included)
+__device__ __forceinline__ void bulk_wait_done() {
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+// 16-byte shared-memory store
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
+                 "r"(d)
+                 : "memory");
+}
+
+// Per-warp staging of 32 rows x 64 bytes (32 columns of 16-bit values) for a TMA box {32, 32}
+// with the 64-byte swizzle, in NB buffers of 2 KB: row r's 16-byte quarter k sits at
+// 64r + 16(k ^ bits 1-2 of r), which keeps a quarter-warp's eight 16-byte stores on distinct
+// banks. With NB = 1 the buffer is reused once the previous store has read it.
+template <int NB>
+struct RowChunkStager {
+    static constexpr int BYTES = NB * 2048;
+    uint32_t base;  // shared address of the warp's NB 2 KB buffers, 1024-byte aligned
+    int n;          // chunks issued so far
+
+    // the next buffer, once the store that last used it has read it (whole warp)
+    __device__ __forceinline__ uint32_t acquire(int lane) {
+        const uint32_t b = base + (NB == 1 ? 0 : (n % NB) * 2048);
+        if (n >= NB) {
+            if (lane == 0) {
+                bulk_wait_reads<NB - 1>();
+            }
+            __syncwarp();
+        }
+        return b;
+    }
+    // lane's row, 16-byte quarter k (columns 8k .. 8k + 7) of buffer b
+    __device__ __forceinline__ void write(uint32_t b, int lane, int k, uint32_t w0, uint32_t w1,
+                                          uint32_t w2, uint32_t w3) {
+        st_shared_v4(b + 64 * lane + 16 * (k ^ ((lane >> 1) & 3)), w0, w1, w2, w3);
+    }
+    // buffer b (every lane's four quarters written) as one box store of rows [row0, row0 + 32),
+    // columns [col0, col0 + 32) of map; TMA clips rows and columns past the map (whole warp)
+    __device__ __forceinline__ void issue(const CUtensorMap* map, uint32_t b, int lane, int col0,
+                                          int row0) {
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+            tma_store_2d(map, b, col0, row0);
+        }
+        ++n;
+    }
+    // lane's row: 16 packed pairs (32 columns) through the next buffer
+    __device__ __forceinline__ void put(const CUtensorMap* map, int lane, const uint32_t (&w)[16],
+                                        int col0, int row0) {
+        const uint32_t b = acquire(lane);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            write(b, lane, k, w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+        }
+        issue(map, b, lane, col0, row0);
+    }
+    __device__ __forceinline__ void finish(int lane) {
+        if (lane == 0) {
+            bulk_wait_done();
+        }
+        __syncwarp();
+    }
+};
+
 // Barrier among the 256 workers (id 1).
 __device__ __forceinline__ void workers_sync() {
     named_sync(1, kWorkers);

@@ -31,13 +31,16 @@ using namespace fused;
 // warpgroup c % 2, which uses x stage c % 2), each doing a tile's whole prologue and epilogue, so
 // one tile's LayerNorm overlaps the other's epilogue; otherwise both split every tile.
 // Op supplies: T, Args (M, w_bytes, param_floats, eps), keep(), kOther, X_BYTES,
-// RED_FLOATS, nblocks(), load_params, load_weights, load_x, issue_block, prologue,
-// epilogue_block, prefetch_block, padding, Regs, kPingPong, kSlots, kSlotCols.
+// RED_FLOATS, STORE_BYTES, nblocks(), load_params, load_weights, load_x, issue_block, prologue,
+// epilogue_block, prefetch_block, padding, Regs, bind, finish, kPingPong, kSlots, kSlotCols.
+// STORE_BYTES of 1024-byte-aligned shared memory after the others are the op's output staging
+// (TMA stores through the map `to`), handed to Op::bind with the map.
 
 template <class Op>
 __global__ void __launch_bounds__(kThreads, 1)
     row_tile_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tw0,
-                    const __grid_constant__ CUtensorMap tw1, const typename Op::Args a) {
+                    const __grid_constant__ CUtensorMap tw1,
+                    const __grid_constant__ CUtensorMap to, const typename Op::Args a) {
     constexpr int kSlots = Op::kSlots, kSlotCols = Op::kSlotCols;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -46,6 +49,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* ws = smem + 2 * Op::X_BYTES;
     float* sp = reinterpret_cast<float*>(ws + a.w_bytes);
     float* red = sp + a.param_floats;  // [Op::RED_FLOATS]
+    uint8_t* stb = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(red + Op::RED_FLOATS) + 1023) & ~uintptr_t(1023));
     // accumulator slot barriers per warpgroup that consumes the slot's block (both ping-pong
     // warpgroups pass blocks through the same slots; one barrier each keeps every barrier's
     // phases in one consumer's order, so no waiter can be two phases ahead)
@@ -81,7 +86,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_alloc(&tmem_sh, kSlots * kSlotCols);
         tmem_relinquish();
     } else {
-        Op::load_params(a, sp, threadIdx.x);
+        Op::load_params(a, sp, ws, threadIdx.x);
+        fence_async_smem();  // weight rows the workers wrote, read by the MMA
     }
     tc_fence_before();
     __syncthreads();
@@ -162,6 +168,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int g = warp >> 2, t = ((warp & 3) << 5) | lane;
         const uint32_t lane_base = tmem_lane_base(warp);
         typename Op::Regs regs{};
+        Op::bind(regs, stb, warp);
         int c = 0, q = 0;
         int full_seen[kSlots] = {};  // acc_full phases this warpgroup waited for, per slot
         // the keep values of the worker's next tile load a tile ahead (the classification's
@@ -203,12 +210,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_wait(&acc_full[team][slot], n_full & 1, &g_status, kStatusMmaWait,
                           &abort_flag);
                 tc_fence_after();
-                Op::epilogue_block(a, tmem + slot * kSlotCols + lane_base, sp, t, g, m0, j, regs);
+                Op::epilogue_block(a, tmem + slot * kSlotCols + lane_base, sp, t, g, m0, j, regs,
+                                   &to);
                 tc_fence_before();
                 mbar_arrive(&acc_empty[team][slot]);
             }
             ++c;
         }
+        Op::finish(regs, lane);
     }
     tc_fence_before();
     __syncthreads();
@@ -298,10 +307,13 @@ struct LnGdpOp {
         int parity;
         float row_mask;      // this worker's row of the mask, from the tile classification
     };
+    static constexpr int STORE_BYTES = 0;
+    static __device__ void bind(Regs&, uint8_t*, int) {}
+    static __device__ void finish(Regs&, int) {}
     static __device__ void row_keep(Regs& r, float v) { r.row_mask = v; }
     static __device__ const T* keep(const Args& a) { return a.mask; }
     // scale [K], offset [K], bp [P], bg [P]
-    static __device__ void load_params(const Args& a, float* sp, int tid) {
+    static __device__ void load_params(const Args& a, float* sp, uint8_t*, int tid) {
         for (int i = tid; i < K; i += kWorkers) {
             sp[i] = a.scale[i];
             sp[K + i] = a.offset[i];
@@ -344,7 +356,8 @@ struct LnGdpOp {
     // worker t of the tile's warpgroup: channel 128j + t (TMEM lane t), the tile's 128 rows in
     // four runs of 32, each stored as 64 contiguous bytes of the channel-major output
     static __device__ void epilogue_block(const Args& a, uint32_t acc, const float* sp, int t,
-                                          int g, int m0, int j, Regs& regs) {
+                                          int g, int m0, int j, Regs& regs,
+                                          const CUtensorMap* to) {
         const int ch = 128 * j + t;
         const float bpv = sp[2 * K + ch], bgv = sp[2 * K + P + ch];
         T* out = ch < CI ? a.left + (long long)ch * a.M : a.right + (long long)(ch - CI) * a.M;
@@ -431,21 +444,34 @@ struct ProjOp {
     static constexpr int X_BYTES = K * BM * 2;
     static constexpr float kOther = -1.f;
     static constexpr int RED_FLOATS = 4;  // unused: a row's LayerNorm is one thread's
+    // output staging: per worker warp one 2 KB box buffer for ln_projection (its weights fill
+    // shared memory), two for output_projection
+    using Stager = RowChunkStager<LN ? 1 : 2>;
+    static constexpr int STORE_BYTES = (kWorkers / 32) * Stager::BYTES;
     struct Args {
         const T *x, *wT, *b, *residual, *wbT, *keep;
         const float *scale, *offset;
         T *out, *bias;
         int M, n, ldp, heads;
-        int w_bytes, param_floats, v8;  // v8: 32-byte output stores allowed
+        int hp;  // weight rows of the head bias after the n projection rows: 16 with heads, else 0
+        int w_bytes, param_floats;
         float eps;
     };
     struct Regs {
         uint4 res[8];  // the residual part of the next block (up to 64 columns)
+        Stager st;
     };
+    static __device__ void bind(Regs& r, uint8_t* stb, int warp) {
+        r.st.base = smem_u32(stb) + warp * Stager::BYTES;
+        r.st.n = 0;
+    }
+    static __device__ void finish(Regs& r, int lane) { r.st.finish(lane); }
     static __device__ void row_keep(Regs&, float) {}
     static __device__ const T* keep(const Args& a) { return a.keep; }
-    // scale [K], offset [K], b [n], wb [8][K]
-    static __device__ void load_params(const Args& a, float* sp, int tid) {
+    // scale [K], offset [K], b [n]; with heads, the head weights wb [heads][K] as weight rows
+    // [n, n + 16) of every 64-column atom (rows past heads zero), so the MMA computes the
+    // per-head bias of the rounded LN(x) as 16 more output columns
+    static __device__ void load_params(const Args& a, float* sp, uint8_t* ws, int tid) {
         for (int i = tid; i < K; i += kWorkers) {
             sp[i] = LN ? a.scale[i] : 0.f;
             sp[K + i] = LN ? a.offset[i] : 0.f;
@@ -453,143 +479,150 @@ struct ProjOp {
         for (int i = tid; i < a.n; i += kWorkers) {
             sp[2 * K + i] = a.b != nullptr ? E::to_f(a.b[i]) : 0.f;
         }
-        for (int i = tid; i < 8 * K; i += kWorkers) {
-            sp[2 * K + a.n + i] = (i / K) < a.heads ? E::to_f(a.wbT[i]) : 0.f;
+        if (a.hp > 0) {
+            const int rows = a.n + a.hp;
+            const uint16_t* wb = reinterpret_cast<const uint16_t*>(a.wbT);
+            for (int i = tid; i < 16 * K; i += kWorkers) {
+                const int r = i / K, c = i % K;
+                *reinterpret_cast<uint16_t*>(ws + sw128_rows(rows, a.n + r, c)) =
+                    r < a.heads ? wb[(long long)r * K + c] : (uint16_t)0;
+            }
         }
     }
     static __device__ void load_weights(const Args& a, const CUtensorMap* tw0,
                                         const CUtensorMap*, uint8_t* ws, uint64_t* bar) {
         mbar_arrive_expect_tx(bar, (uint32_t)(a.n * K * 2));
         if (a.n > 0) {
-            load_weight(tw0, ws, bar, a.n, K);
+            const int rows = a.n + a.hp, box = weight_box(a.n);
+            for (int at = 0; at < K / 64; ++at) {
+                for (int r0 = 0; r0 < a.n; r0 += box) {
+                    tma_load_2d(ws + at * rows * 128 + r0 * 128, tw0, bar, at * 64, r0);
+                }
+            }
         }
     }
     static __device__ void load_x(const Args& a, const CUtensorMap* tx, uint8_t* dst,
                                   uint64_t* bar, int m0) {
         load_rows_tile(tx, dst, bar, K, m0);
     }
-    // block j: output columns [128j, 128j + 128) (the last one 64 wide when n % 128 == 64)
-    static __device__ int nblocks(const Args& a) { return (a.n + 127) / 128; }
+    // block j < nb: output columns [128j, 128j + 128) (the last one 64 wide when n % 128 == 64);
+    // with heads, block nb is the 16 head-bias columns
+    static __device__ int nmain(const Args& a) { return (a.n + 127) / 128; }
+    static __device__ int nblocks(const Args& a) { return nmain(a) + (a.hp > 0 ? 1 : 0); }
     static __device__ void issue_block(const Args& a, uint32_t xa, uint32_t wa, uint32_t acc,
                                        int j) {
+        const int rows = a.n + a.hp;
+        if (j == nmain(a)) {
+            mma_rows(acc, xa, wa, rows, K, a.n, 16, E::kBf16, false);
+            return;
+        }
         const int n0 = 128 * j, N = a.n - n0 < 128 ? a.n - n0 : 128;
-        mma_rows(acc, xa, wa, a.n, K, n0, N, E::kBf16, false);
+        mma_rows(acc, xa, wa, rows, K, n0, N, E::kBf16, false);
     }
-    // warpgroup g's tile: LayerNorm of row t (the whole row) and, with heads, the per-head
-    // bias: a row reduction over the rounded LN(x) (wb rows in shared memory, 16-byte reads)
+    // warpgroup g's tile: LayerNorm of row t (the whole row), written back rounded to T
     static __device__ void prologue(const Args& a, uint8_t* stage, const float* sp, float* red,
                                     int t, int g, int m0, Regs&) {
         if constexpr (LN) {
-            const float* wb = sp + 2 * K + a.n;
-            const int heads = a.heads;
-            float hd[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            ln_row_full<T, K>(stage, t, sp, sp + K, a.eps, [&](int ch, const float* y) {
-#pragma unroll
-                for (int h = 0; h < 8; ++h) {
-                    if (h < heads) {
-                        const float4 w0 = *reinterpret_cast<const float4*>(wb + h * K + 8 * ch);
-                        const float4 w1 =
-                            *reinterpret_cast<const float4*>(wb + h * K + 8 * ch + 4);
-                        float d = hd[h];
-                        d = fmaf(y[0], w0.x, d);
-                        d = fmaf(y[1], w0.y, d);
-                        d = fmaf(y[2], w0.z, d);
-                        d = fmaf(y[3], w0.w, d);
-                        d = fmaf(y[4], w1.x, d);
-                        d = fmaf(y[5], w1.y, d);
-                        d = fmaf(y[6], w1.z, d);
-                        d = fmaf(y[7], w1.w, d);
-                        hd[h] = d;
-                    }
-                }
-            });
-            if (m0 + t < a.M) {
-#pragma unroll
-                for (int h = 0; h < 8; ++h) {
-                    if (h < heads) {
-                        a.bias[(long long)h * a.M + m0 + t] = E::from_f(hd[h]);
-                    }
-                }
-            }
+            ln_row_full<T, K>(stage, t, sp, sp + K, a.eps, [](int, const float*) {});
         }
     }
     // the residual of row t's first 64 columns of block j, loaded ahead of the MMA wait
     static __device__ void prefetch_block(const Args& a, int t, int g, int m0, int j,
                                           Regs& regs) {
-        const int m = m0 + t;
-        if (a.residual == nullptr || m >= a.M) {
-            return;
-        }
-        const int width = a.n - 128 * j < 128 ? a.n - 128 * j : 128;
-        const uint4* rr =
-            reinterpret_cast<const uint4*>(a.residual + (long long)m * a.ldp + 128 * j);
+        if constexpr (!LN) {
+            const int m = m0 + t;
+            if (a.residual == nullptr || m >= a.M || j >= nmain(a)) {
+                return;
+            }
+            const int width = a.n - 128 * j < 128 ? a.n - 128 * j : 128;
+            const uint4* rr =
+                reinterpret_cast<const uint4*>(a.residual + (long long)m * a.ldp + 128 * j);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            if (8 * i < width) {
-                regs.res[i] = rr[i];
+            for (int i = 0; i < 8; ++i) {
+                if (8 * i < width) {
+                    regs.res[i] = rr[i];
+                }
             }
         }
     }
-    // worker t of the tile's warpgroup: row t, every column 128j + [0, w) of the block's width w
+    // worker t of the tile's warpgroup: row t, every column 128j + [0, w) of the block's width
+    // w, 32 columns at a time through the warp's staging buffer and TMA stores
     static __device__ void epilogue_block(const Args& a, uint32_t acc, const float* sp, int t,
-                                          int g, int m0, int j, Regs& regs) {
-        const int m = m0 + t;
+                                          int g, int m0, int j, Regs& regs,
+                                          const CUtensorMap* to) {
+        const int m = m0 + t, lane = t & 31;
+        if (j == nmain(a)) {
+            // the head bias: columns h < heads, bias [heads, M] (a warp's 32 rows contiguous)
+            uint32_t r[16];
+            tmem_ld16(acc, r);
+            tmem_wait_ld();
+            if (m < a.M) {
+#pragma unroll
+                for (int h = 0; h < 8; ++h) {
+                    if (h < a.heads) {
+                        a.bias[(long long)h * a.M + m] = E::from_f(__uint_as_float(r[h]));
+                    }
+                }
+            }
+            return;
+        }
         const int width = a.n - 128 * j < 128 ? a.n - 128 * j : 128;
         const float* b = sp + 2 * K + 128 * j;
-        T* orow = a.out + (long long)m * a.ldp + 128 * j;
+        const int row0 = m0 + (t & ~31);
         // the residual of columns [64, 128) loads while the first 64 are done
         uint4 res2[8];
-        if (a.residual != nullptr && m < a.M && width > 64) {
-            const uint4* rr = reinterpret_cast<const uint4*>(a.residual + (long long)m * a.ldp +
-                                                             128 * j + 64);
+        if constexpr (!LN) {
+            if (a.residual != nullptr && m < a.M && width > 64) {
+                const uint4* rr = reinterpret_cast<const uint4*>(
+                    a.residual + (long long)m * a.ldp + 128 * j + 64);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                res2[i] = rr[i];
+                for (int i = 0; i < 8; ++i) {
+                    res2[i] = rr[i];
+                }
             }
         }
+        // 32 columns a TMEM wait and a store
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const int c0 = 16 * i;
+        for (int gi = 0; gi < 4; ++gi) {
+            const int c0 = 32 * gi;
             if (c0 >= width) {
                 break;
             }
-            uint32_t r[16];
-            tmem_ld16(acc + c0, r);
+            uint32_t r[32];
+            tmem_ld32(acc + c0, r);
             tmem_wait_ld();
-            if (m < a.M) {
-                float v[16];
+            float v[32];
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const float4 bb = *reinterpret_cast<const float4*>(b + c0 + 4 * q);
-                    v[4 * q] = __uint_as_float(r[4 * q]) + bb.x;
-                    v[4 * q + 1] = __uint_as_float(r[4 * q + 1]) + bb.y;
-                    v[4 * q + 2] = __uint_as_float(r[4 * q + 2]) + bb.z;
-                    v[4 * q + 3] = __uint_as_float(r[4 * q + 3]) + bb.w;
-                }
+            for (int q = 0; q < 8; ++q) {
+                const float4 bb = *reinterpret_cast<const float4*>(b + c0 + 4 * q);
+                v[4 * q] = __uint_as_float(r[4 * q]) + bb.x;
+                v[4 * q + 1] = __uint_as_float(r[4 * q + 1]) + bb.y;
+                v[4 * q + 2] = __uint_as_float(r[4 * q + 2]) + bb.z;
+                v[4 * q + 3] = __uint_as_float(r[4 * q + 3]) + bb.w;
+            }
+            if constexpr (!LN) {
                 if (a.residual != nullptr) {
-                    const uint4 q0 = i < 4 ? regs.res[2 * i] : res2[2 * i - 8];
-                    const uint4 q1 = i < 4 ? regs.res[2 * i + 1] : res2[2 * i - 7];
-                    const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        const float2 f = E::unpack(qw[e]);
-                        v[2 * e] += f.x;
-                        v[2 * e + 1] += f.y;
+                    for (int u = 0; u < 4; ++u) {
+                        const uint4 qq = gi < 2 ? regs.res[4 * gi + u] : res2[4 * gi - 8 + u];
+                        const uint32_t qw[4] = {qq.x, qq.y, qq.z, qq.w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const float2 f = E::unpack(qw[e]);
+                            v[8 * u + 2 * e] += f.x;
+                            v[8 * u + 2 * e + 1] += f.y;
+                        }
                     }
                 }
-                uint32_t w[8];
+            }
+            uint32_t w[16];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    w[e] = E::pack(v[2 * e], v[2 * e + 1]);
-                }
-                if (a.v8) {
-                    st_global_v8(orow + c0, make_uint4(w[0], w[1], w[2], w[3]),
-                                 make_uint4(w[4], w[5], w[6], w[7]));
-                } else {
-                    *reinterpret_cast<uint4*>(orow + c0) = make_uint4(w[0], w[1], w[2], w[3]);
-                    *reinterpret_cast<uint4*>(orow + c0 + 8) =
-                        make_uint4(w[4], w[5], w[6], w[7]);
-                }
+            for (int e = 0; e < 16; ++e) {
+                w[e] = E::pack(v[2 * e], v[2 * e + 1]);
+            }
+            // rows past M hold garbage; the store clips them (a warp wholly past M stores nothing)
+            if (row0 < a.M) {
+                regs.st.put(to, lane, w, 128 * j + c0, row0);
             }
         }
     }
@@ -629,21 +662,32 @@ struct TrimulOp {
     static constexpr int XOFF = C * BM * 2;  // x's atoms after Y's
     static constexpr float kOther = -1.f;
     static constexpr int RED_FLOATS = 8 * BM;
+    // C <= 64: the output leaves through per-warp staging (two 2 KB box buffers a worker warp)
+    // and TMA stores; C = 128, whose prologue state fills the registers, stores from registers
+    static constexpr bool kTmaOut = C <= 64;
+    using Stager = RowChunkStager<2>;
+    static constexpr int STORE_BYTES = kTmaOut ? (kWorkers / 32) * Stager::BYTES : 0;
     struct Args {
         const float* x_cm;
         const T *x, *woT, *bo, *wgT, *bg, *keep;
         const float *in_scale, *in_offset, *ln_scale, *ln_offset;
         T* out;
-        int M, w_bytes, param_floats, v8;  // v8: 32-byte output stores allowed
+        int M, w_bytes, param_floats, v8;  // v8: 32-byte output stores allowed (C = 128)
         float eps;
     };
     struct Regs {
         uint4 res[4];  // x of worker half g's 32 channels of the next block (add_input)
+        Stager st;
     };
+    static __device__ void bind(Regs& r, uint8_t* stb, int warp) {
+        r.st.base = smem_u32(stb) + warp * Stager::BYTES;
+        r.st.n = 0;
+    }
+    static __device__ void finish(Regs& r, int lane) { r.st.finish(lane); }
     static __device__ void row_keep(Regs&, float) {}
     static __device__ const T* keep(const Args& a) { return a.keep; }
     // in_scale [CA], in_offset [CA], ln_scale [C], ln_offset [C], bo [O], bg [O]
-    static __device__ void load_params(const Args& a, float* sp, int tid) {
+    static __device__ void load_params(const Args& a, float* sp, uint8_t*, int tid) {
         for (int i = tid; i < CA; i += kWorkers) {
             sp[i] = a.in_scale[i];
             sp[CA + i] = a.in_offset[i];
@@ -738,12 +782,70 @@ struct TrimulOp {
     }
     // worker half g: channels 64j + 32g + [0, 32)
     static __device__ void epilogue_block(const Args& a, uint32_t acc, const float* sp, int t,
-                                          int g, int m0, int j, Regs& regs) {
+                                          int g, int m0, int j, Regs& regs,
+                                          const CUtensorMap* to) {
+        if constexpr (kTmaOut) {
+            epilogue_staged(a, acc, sp, t, g, m0, j, regs, to);
+        } else {
+            epilogue_direct(a, acc, sp, t, g, m0, j, regs);
+        }
+    }
+    static __device__ void epilogue_staged(const Args& a, uint32_t acc, const float* sp, int t,
+                                           int g, int m0, int j, Regs& regs,
+                                           const CUtensorMap* to) {
+        const int lane = t & 31, row0 = m0 + (t & ~31), c0 = 32 * g;
+        const float* bo = sp + 2 * CA + 2 * C + 64 * j + c0;
+        const float* bg = bo + O;
+        // rows past M would compute garbage that the store clips: a warp wholly past M skips
+        if (row0 >= a.M) {
+            return;
+        }
+        const uint32_t sb = regs.st.acquire(lane);
+        // the 32 columns in two halves of 16 (one TMEM wait each), stored as one box
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+            uint32_t ro[16], rg[16];
+            tmem_ld16(acc + c0 + 16 * hh, ro);
+            tmem_ld16(acc + 64 + c0 + 16 * hh, rg);
+            tmem_wait_ld();
+            uint32_t w[8];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float4 b0 = *reinterpret_cast<const float4*>(bo + 16 * hh + 4 * q);
+                const float4 b1 = *reinterpret_cast<const float4*>(bg + 16 * hh + 4 * q);
+                float v[4] = {(__uint_as_float(ro[4 * q]) + b0.x) *
+                                  sigmoid_fast(__uint_as_float(rg[4 * q]) + b1.x),
+                              (__uint_as_float(ro[4 * q + 1]) + b0.y) *
+                                  sigmoid_fast(__uint_as_float(rg[4 * q + 1]) + b1.y),
+                              (__uint_as_float(ro[4 * q + 2]) + b0.z) *
+                                  sigmoid_fast(__uint_as_float(rg[4 * q + 2]) + b1.z),
+                              (__uint_as_float(ro[4 * q + 3]) + b0.w) *
+                                  sigmoid_fast(__uint_as_float(rg[4 * q + 3]) + b1.w)};
+                if constexpr (ADD) {
+                    const uint4 qq = regs.res[2 * hh + (q >> 1)];
+                    const float2 f0 = E::unpack((q & 1) ? qq.z : qq.x);
+                    const float2 f1 = E::unpack((q & 1) ? qq.w : qq.y);
+                    v[0] += f0.x;
+                    v[1] += f0.y;
+                    v[2] += f1.x;
+                    v[3] += f1.y;
+                }
+                w[2 * q] = E::pack(v[0], v[1]);
+                w[2 * q + 1] = E::pack(v[2], v[3]);
+            }
+            regs.st.write(sb, lane, 2 * hh, w[0], w[1], w[2], w[3]);
+            regs.st.write(sb, lane, 2 * hh + 1, w[4], w[5], w[6], w[7]);
+        }
+        regs.st.issue(to, sb, lane, 64 * j + c0, row0);
+    }
+    static __device__ void epilogue_direct(const Args& a, uint32_t acc, const float* sp, int t,
+                                           int g, int m0, int j, Regs& regs) {
         const int m = m0 + t;
         const float* bo = sp + 2 * CA + 2 * C + 64 * j;
         const float* bg = bo + O;
         T* orow = a.out + (long long)m * O + 64 * j;
-        const auto chunk = [&](int c0) {
+#pragma unroll 1
+        for (int c0 = 32 * g; c0 < 32 * g + 32; c0 += 16) {
             uint32_t ro[16], rg[16];
             tmem_ld16(acc + c0, ro);
             tmem_ld16(acc + 64 + c0, rg);
@@ -751,9 +853,9 @@ struct TrimulOp {
             if (m < a.M) {
                 float v[16];
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    v[j] = (__uint_as_float(ro[j]) + bo[c0 + j]) *
-                           sigmoid_fast(__uint_as_float(rg[j]) + bg[c0 + j]);
+                for (int e = 0; e < 16; ++e) {
+                    v[e] = (__uint_as_float(ro[e]) + bo[c0 + e]) *
+                           sigmoid_fast(__uint_as_float(rg[e]) + bg[c0 + e]);
                 }
                 if constexpr (ADD) {
                     const int ri = (c0 - 32 * g) / 8;
@@ -779,18 +881,6 @@ struct TrimulOp {
                     *reinterpret_cast<uint4*>(orow + c0 + 8) =
                         make_uint4(w[4], w[5], w[6], w[7]);
                 }
-            }
-        };
-        // unrolled where the registers allow (C = 128 keeps a wider prologue state)
-        if constexpr (C <= 64) {
-#pragma unroll
-            for (int c0 = 32 * g; c0 < 32 * g + 32; c0 += 16) {
-                chunk(c0);
-            }
-        } else {
-#pragma unroll 1
-            for (int c0 = 32 * g; c0 < 32 * g + 32; c0 += 16) {
-                chunk(c0);
             }
         }
     }
@@ -1232,9 +1322,10 @@ bool map_rows(CUtensorMap* m, int dtype, const void* base, long long rows, long 
 
 template <class Op>
 cudaError_t launch_op(cudaStream_t stream, const CUtensorMap& tx, const CUtensorMap& tw0,
-                      const CUtensorMap& tw1, const typename Op::Args& a) {
+                      const CUtensorMap& tw1, const CUtensorMap& to, const typename Op::Args& a) {
     auto kern = row_tile_kernel<Op>;
-    const int smem = 2 * Op::X_BYTES + a.w_bytes + (a.param_floats + Op::RED_FLOATS) * 4 + 1024;
+    const int smem = 2 * Op::X_BYTES + a.w_bytes + (a.param_floats + Op::RED_FLOATS) * 4 + 1024 +
+                     (Op::STORE_BYTES > 0 ? Op::STORE_BYTES + 1024 : 0);
     const cudaError_t e =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) {
@@ -1242,7 +1333,7 @@ cudaError_t launch_op(cudaStream_t stream, const CUtensorMap& tx, const CUtensor
     }
     const int ntiles = (a.M + BM - 1) / BM;
     const int grid = std::min(ntiles, sm_count());
-    kern<<<grid, kThreads, smem, stream>>>(tx, tw0, tw1, a);
+    kern<<<grid, kThreads, smem, stream>>>(tx, tw0, tw1, to, a);
     return cudaGetLastError();
 }
 
@@ -1283,7 +1374,7 @@ cudaError_t ln_gdp_typed(cudaStream_t stream, int dtype, const void* x, const fl
     const uintptr_t lr = reinterpret_cast<uintptr_t>(left) | reinterpret_cast<uintptr_t>(right);
     a.vec_store = M % 16 == 0 && (lr & 31) == 0 ? 2 : M % 8 == 0 && (lr & 15) == 0 ? 1 : 0;
     a.eps = eps;
-    return launch_op<Op>(stream, tx, tw0, tw1, a);
+    return launch_op<Op>(stream, tx, tw0, tw1, tx, a);
 }
 
 template <typename T, int K, bool LN>
@@ -1292,16 +1383,24 @@ cudaError_t proj_typed(cudaStream_t stream, int dtype, const void* x, const floa
                        const void* wbT, const void* keep, void* out, void* bias, int M, int n,
                        int ldp, int heads, float eps) {
     using Op = ProjOp<T, K, LN>;
-    CUtensorMap tx, tw0;
+    CUtensorMap tx, tw0, to;
     if (!map_rows(&tx, dtype, x, M, K, K, BM)) {
         return cudaErrorInvalidValue;
     }
     if (n > 0) {
-        if (!map_rows(&tw0, dtype, wT, n, K, K, weight_box(n))) {
+        // the output leaves in boxes of 32 columns x 32 rows (64-byte swizzle), one per worker
+        // warp and 32 columns
+        const uint64_t dims[2] = {(uint64_t)n, (uint64_t)M};
+        const uint64_t strides[1] = {(uint64_t)ldp};
+        const uint32_t box[2] = {32, 32};
+        if (!map_rows(&tw0, dtype, wT, n, K, K, weight_box(n)) ||
+            !encode_tiled(&to, tdt(dtype), 2, 2, out, dims, strides, box,
+                          CU_TENSOR_MAP_SWIZZLE_64B)) {
             return cudaErrorInvalidValue;
         }
     } else {
         tw0 = tx;
+        to = tx;
     }
     typename Op::Args a;
     a.x = static_cast<const T*>(x);
@@ -1318,11 +1417,11 @@ cudaError_t proj_typed(cudaStream_t stream, int dtype, const void* x, const floa
     a.n = n;
     a.ldp = ldp;
     a.heads = heads;
-    a.v8 = ldp % 16 == 0 && (reinterpret_cast<uintptr_t>(out) & 31) == 0;
-    a.w_bytes = n * K * 2;
-    a.param_floats = 2 * K + n + 8 * K;
+    a.hp = heads > 0 ? 16 : 0;
+    a.w_bytes = (n + a.hp) * K * 2;
+    a.param_floats = 2 * K + n;
     a.eps = eps;
-    return launch_op<Op>(stream, tx, tw0, tw0, a);
+    return launch_op<Op>(stream, tx, tw0, tw0, to, a);
 }
 
 
@@ -1332,10 +1431,19 @@ cudaError_t trimul_typed(cudaStream_t stream, int dtype, const float* x_cm, cons
                          const float* ln_offset, const void* woT, const void* bo, const void* wgT,
                          const void* bg, const void* keep, void* out, int M, float eps) {
     using Op = TrimulOp<T, C, CA, O, ADD>;
-    CUtensorMap tx, tw0, tw1;
+    CUtensorMap tx, tw0, tw1, to;
+    // the output leaves in boxes of 32 columns x 32 rows (64-byte swizzle)
+    const uint64_t dims[2] = {(uint64_t)O, (uint64_t)M};
+    const uint64_t strides[1] = {(uint64_t)O};
+    const uint32_t box[2] = {32, 32};
     if (!map_rows(&tx, dtype, x, M, CA, CA, BM) ||
         !map_rows(&tw0, dtype, woT, O, C, C, weight_box(O)) ||
         !map_rows(&tw1, dtype, wgT, O, CA, CA, weight_box(O))) {
+        return cudaErrorInvalidValue;
+    }
+    to = tx;
+    if (Op::kTmaOut &&
+        !encode_tiled(&to, tdt(dtype), 2, 2, out, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B)) {
         return cudaErrorInvalidValue;
     }
     typename Op::Args a;
@@ -1356,7 +1464,7 @@ cudaError_t trimul_typed(cudaStream_t stream, int dtype, const float* x_cm, cons
     a.w_bytes = (O * C + O * CA) * 2;
     a.param_floats = 2 * CA + 2 * C + 2 * O;
     a.eps = eps;
-    return launch_op<Op>(stream, tx, tw0, tw1, a);
+    return launch_op<Op>(stream, tx, tw0, tw1, to, a);
 }
 
 template <typename T, int C, int CA>

@@ -291,6 +291,76 @@ __device__ __forceinline__ void ln_rows_half(uint8_t* tile, int t, int g, const 
     }
 }
 
+// LayerNorm of row t in place on a swizzled tile, the whole row by one thread, with the row
+// held in registers (K <= 128: one pass of 16-byte reads, the centred second moment from the
+// registers, then the normalised row rounded to T written back): a third of ln_row_full's
+// shared-memory reads, the same arithmetic.
+template <typename T, int K>
+__device__ __forceinline__ void ln_row_regs(uint8_t* tile, int t, const float* scale,
+                                            const float* offset, float eps) {
+    static_assert(K <= 128, "row in registers");
+    using E = Elem<T>;
+    uint4 w[K / 8];
+#pragma unroll
+    for (int ch = 0; ch < K / 8; ++ch) {
+        w[ch] = *reinterpret_cast<const uint4*>(tile + sw128(t, 8 * ch));
+    }
+    uint64_t acc[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        acc[i] = pk2(0.f, 0.f);
+    }
+#pragma unroll
+    for (int ch = 0; ch < K / 8; ++ch) {
+        const uint32_t ww[4] = {w[ch].x, w[ch].y, w[ch].z, w[ch].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float2 f = E::unpack(ww[e]);
+            acc[e] = add2(acc[e], pk2(f.x, f.y));
+        }
+    }
+    float2 r = upk2(add2(add2(acc[0], acc[1]), add2(acc[2], acc[3])));
+    const float mean = (r.x + r.y) * (1.f / K);
+    const uint64_t nm2 = pk2(-mean, -mean);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        acc[i] = pk2(0.f, 0.f);
+    }
+#pragma unroll
+    for (int ch = 0; ch < K / 8; ++ch) {
+        const uint32_t ww[4] = {w[ch].x, w[ch].y, w[ch].z, w[ch].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float2 f = E::unpack(ww[e]);
+            const uint64_t d = add2(pk2(f.x, f.y), nm2);
+            acc[e] = fma2(d, d, acc[e]);
+        }
+    }
+    r = upk2(add2(add2(acc[0], acc[1]), add2(acc[2], acc[3])));
+    const float rstd = rsqrtf((r.x + r.y) * (1.f / K) + eps);
+    const uint64_t r2 = pk2(rstd, rstd);
+#pragma unroll
+    for (int ch = 0; ch < K / 8; ++ch) {
+        const uint32_t ww[4] = {w[ch].x, w[ch].y, w[ch].z, w[ch].w};
+        const float4 s0 = *reinterpret_cast<const float4*>(scale + 8 * ch);
+        const float4 s1 = *reinterpret_cast<const float4*>(scale + 8 * ch + 4);
+        const float4 o0 = *reinterpret_cast<const float4*>(offset + 8 * ch);
+        const float4 o1 = *reinterpret_cast<const float4*>(offset + 8 * ch + 4);
+        const float sc[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+        const float of[8] = {o0.x, o0.y, o0.z, o0.w, o1.x, o1.y, o1.z, o1.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float2 f = E::unpack(ww[e]);
+            const float2 yf = upk2(fma2(mul2(add2(pk2(f.x, f.y), nm2), r2),
+                                        pk2(sc[2 * e], sc[2 * e + 1]),
+                                        pk2(of[2 * e], of[2 * e + 1])));
+            o[e] = E::pack(yf.x, yf.y);
+        }
+        *reinterpret_cast<uint4*>(tile + sw128(t, 8 * ch)) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+}
+
 // LayerNorm of row t in place on a swizzled tile, the whole row by one thread (no exchange, no
 // barrier): three passes over the row in shared memory (sum, centred sum of squares, then the
 // normalised row rounded to T and written back), so the row never sits in registers.

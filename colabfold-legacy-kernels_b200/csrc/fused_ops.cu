@@ -40,7 +40,8 @@ template <class Op>
 __global__ void __launch_bounds__(kThreads, 1)
     row_tile_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tw0,
                     const __grid_constant__ CUtensorMap tw1,
-                    const __grid_constant__ CUtensorMap to, const typename Op::Args a) {
+                    const __grid_constant__ CUtensorMap to,
+                    const __grid_constant__ CUtensorMap to1, const typename Op::Args a) {
     constexpr int kSlots = Op::kSlots, kSlotCols = Op::kSlotCols;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -211,7 +212,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                           &abort_flag);
                 tc_fence_after();
                 Op::epilogue_block(a, tmem + slot * kSlotCols + lane_base, sp, t, g, m0, j, regs,
-                                   &to);
+                                   &to, &to1);
                 tc_fence_before();
                 mbar_arrive(&acc_empty[team][slot]);
             }
@@ -295,21 +296,29 @@ struct LnGdpOp {
     // a block is 128 channels, the projection in the slot's columns [0, 128) and the gate in
     // [128, 256), one column per row of the tile
     static constexpr int kSlots = 2, kSlotCols = 256;
+    // output staging when M % 8 == 0 (TMA row strides): per worker warp one 2 KB box buffer
+    // for CI = 128 (its weights fill shared memory), two for CI = 64
+    using Stager = RowChunkStager<CI <= 64 ? 2 : 1>;
+    static constexpr int STORE_BYTES = (kWorkers / 32) * Stager::BYTES;
     struct Args {
         const T *x, *wpT, *bp, *wgT, *bg, *mask;
         const float *scale, *offset;
         T *left, *right;
         int M, w_bytes, param_floats, vec_store;
+        int tma_out;  // outputs through the staging buffers and TMA stores (maps to, to1)
         float eps;
     };
     struct Regs {
         const float* maskv;  // this tile's row mask (shared memory)
         int parity;
         float row_mask;      // this worker's row of the mask, from the tile classification
+        Stager st;
     };
-    static constexpr int STORE_BYTES = 0;
-    static __device__ void bind(Regs&, uint8_t*, int) {}
-    static __device__ void finish(Regs&, int) {}
+    static __device__ void bind(Regs& r, uint8_t* stb, int warp) {
+        r.st.base = smem_u32(stb) + warp * Stager::BYTES;
+        r.st.n = 0;
+    }
+    static __device__ void finish(Regs& r, int lane) { r.st.finish(lane); }
     static __device__ void row_keep(Regs& r, float v) { r.row_mask = v; }
     static __device__ const T* keep(const Args& a) { return a.mask; }
     // scale [K], offset [K], bp [P], bg [P]
@@ -349,7 +358,7 @@ struct LnGdpOp {
         mv[t] = m0 + t < a.M ? fmaxf(regs.row_mask, 0.f) : 0.f;
         regs.maskv = mv;
         regs.parity ^= 1;
-        ln_row_full<T, K>(stage, t, sp, sp + K, a.eps, [](int, const float*) {});
+        ln_row_regs<T, K>(stage, t, sp, sp + K, a.eps);
         named_sync(2 + g, 128);
     }
     static __device__ void prefetch_block(const Args&, int, int, int, int, Regs&) {}
@@ -357,7 +366,7 @@ struct LnGdpOp {
     // four runs of 32, each stored as 64 contiguous bytes of the channel-major output
     static __device__ void epilogue_block(const Args& a, uint32_t acc, const float* sp, int t,
                                           int g, int m0, int j, Regs& regs,
-                                          const CUtensorMap* to) {
+                                          const CUtensorMap* to, const CUtensorMap* to1) {
         const int ch = 128 * j + t;
         const float bpv = sp[2 * K + ch], bgv = sp[2 * K + P + ch];
         T* out = ch < CI ? a.left + (long long)ch * a.M : a.right + (long long)(ch - CI) * a.M;
@@ -396,7 +405,11 @@ struct LnGdpOp {
                     w[2 * q + e / 2] = E::pack(o.x, o.y);
                 }
             }
-            if (a.vec_store == 2 && m + 32 <= a.M) {
+            if (a.tma_out) {
+                // the warp's 32 channels x these 32 rows as one box of left or right
+                const int chw = 128 * j + (t & ~31);
+                regs.st.put(chw < CI ? to : to1, t & 31, w, m, chw < CI ? chw : chw - CI);
+            } else if (a.vec_store == 2 && m + 32 <= a.M) {
 #pragma unroll
                 for (int q = 0; q < 2; ++q) {
                     st_global_v8(out + m + 16 * q,
@@ -549,7 +562,7 @@ struct ProjOp {
     // w, 32 columns at a time through the warp's staging buffer and TMA stores
     static __device__ void epilogue_block(const Args& a, uint32_t acc, const float* sp, int t,
                                           int g, int m0, int j, Regs& regs,
-                                          const CUtensorMap* to) {
+                                          const CUtensorMap* to, const CUtensorMap* to1) {
         const int m = m0 + t, lane = t & 31;
         if (j == nmain(a)) {
             // the head bias: columns h < heads, bias [heads, M] (a warp's 32 rows contiguous)
@@ -783,7 +796,7 @@ struct TrimulOp {
     // worker half g: channels 64j + 32g + [0, 32)
     static __device__ void epilogue_block(const Args& a, uint32_t acc, const float* sp, int t,
                                           int g, int m0, int j, Regs& regs,
-                                          const CUtensorMap* to) {
+                                          const CUtensorMap* to, const CUtensorMap* to1) {
         if constexpr (kTmaOut) {
             epilogue_staged(a, acc, sp, t, g, m0, j, regs, to);
         } else {
@@ -1322,7 +1335,8 @@ bool map_rows(CUtensorMap* m, int dtype, const void* base, long long rows, long 
 
 template <class Op>
 cudaError_t launch_op(cudaStream_t stream, const CUtensorMap& tx, const CUtensorMap& tw0,
-                      const CUtensorMap& tw1, const CUtensorMap& to, const typename Op::Args& a) {
+                      const CUtensorMap& tw1, const CUtensorMap& to, const CUtensorMap& to1,
+                      const typename Op::Args& a) {
     auto kern = row_tile_kernel<Op>;
     const int smem = 2 * Op::X_BYTES + a.w_bytes + (a.param_floats + Op::RED_FLOATS) * 4 + 1024 +
                      (Op::STORE_BYTES > 0 ? Op::STORE_BYTES + 1024 : 0);
@@ -1333,7 +1347,7 @@ cudaError_t launch_op(cudaStream_t stream, const CUtensorMap& tx, const CUtensor
     }
     const int ntiles = (a.M + BM - 1) / BM;
     const int grid = std::min(ntiles, sm_count());
-    kern<<<grid, kThreads, smem, stream>>>(tx, tw0, tw1, to, a);
+    kern<<<grid, kThreads, smem, stream>>>(tx, tw0, tw1, to, to1, a);
     return cudaGetLastError();
 }
 
@@ -1374,7 +1388,23 @@ cudaError_t ln_gdp_typed(cudaStream_t stream, int dtype, const void* x, const fl
     const uintptr_t lr = reinterpret_cast<uintptr_t>(left) | reinterpret_cast<uintptr_t>(right);
     a.vec_store = M % 16 == 0 && (lr & 31) == 0 ? 2 : M % 8 == 0 && (lr & 15) == 0 ? 1 : 0;
     a.eps = eps;
-    return launch_op<Op>(stream, tx, tw0, tw1, tx, a);
+    // channel-major outputs leave in boxes of 32 rows x 32 channels (64-byte swizzle) when the
+    // channel stride (M elements) is a multiple of 16 bytes
+    CUtensorMap to0 = tx, to1 = tx;
+    a.tma_out = 0;
+    if (M % 8 == 0 && (lr & 15) == 0) {
+        const uint64_t dims[2] = {(uint64_t)M, (uint64_t)CI};
+        const uint64_t strides[1] = {(uint64_t)M};
+        const uint32_t box[2] = {32, 32};
+        if (!encode_tiled(&to0, tdt(dtype), 2, 2, left, dims, strides, box,
+                          CU_TENSOR_MAP_SWIZZLE_64B) ||
+            !encode_tiled(&to1, tdt(dtype), 2, 2, right, dims, strides, box,
+                          CU_TENSOR_MAP_SWIZZLE_64B)) {
+            return cudaErrorInvalidValue;
+        }
+        a.tma_out = 1;
+    }
+    return launch_op<Op>(stream, tx, tw0, tw1, to0, to1, a);
 }
 
 template <typename T, int K, bool LN>
@@ -1421,7 +1451,7 @@ cudaError_t proj_typed(cudaStream_t stream, int dtype, const void* x, const floa
     a.w_bytes = (n + a.hp) * K * 2;
     a.param_floats = 2 * K + n;
     a.eps = eps;
-    return launch_op<Op>(stream, tx, tw0, tw0, to, a);
+    return launch_op<Op>(stream, tx, tw0, tw0, to, to, a);
 }
 
 
@@ -1464,7 +1494,7 @@ cudaError_t trimul_typed(cudaStream_t stream, int dtype, const float* x_cm, cons
     a.w_bytes = (O * C + O * CA) * 2;
     a.param_floats = 2 * CA + 2 * C + 2 * O;
     a.eps = eps;
-    return launch_op<Op>(stream, tx, tw0, tw1, to, a);
+    return launch_op<Op>(stream, tx, tw0, tw1, to, to, a);
 }
 
 template <typename T, int C, int CA>

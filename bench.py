@@ -327,7 +327,9 @@ def run_ours(args):
                         'bwd_ms': bwd_ms, 'bwd_tflops': bwd_tf, 'bwd_frac': bwd_tf / peak,
                         'sequences_per_gpu': n_local},
             'e2e': e2e,
-            'gpu_launches': 4 * args.steps,
+            # per step: attn_fwd_kernel; row_delta_kernel, bias_transpose_kernel,
+            # attn_bwd_kernel, dq_convert_kernel
+            'gpu_launches': 5 * args.steps,
             'clocks': clk,
         }
         if cpu_line is not None:
@@ -512,27 +514,73 @@ def bench_inference(torch, b200, dev, rank, world, steps, warmup, flush, pk):
     return res
 
 
+E2E_CHUNKS = 8
+
+
 def run_e2e(args, torch, dist, b200, dev, world, q, k, v, bias, kmask, dout, scale):
-    """The same step through the public API from pinned host buffers: inputs copied in and the
-    gradients copied out inside the timed region."""
-    hosts = [t.cpu().pin_memory() for t in (q, k, v, bias, kmask, dout)]
-    devs = [torch.empty_like(t) for t in (q, k, v, bias, kmask, dout)]
+    """The same step through the public API from pinned host buffers, inputs copied in and the
+    gradients copied out inside the timed region. The batch goes through in E2E_CHUNKS chunks of
+    sequences on three streams, so that the copies in, the kernels and the copies out overlap
+    (PCIe carries both directions at once): chunk i's q/k/v/dout/mask copy in while chunk i-1
+    computes and chunk i-2's dq/dk/dv copy out. The bias is copied once a step; the chunks'
+    dBias partial sums add up on the device and dBias is read back after the last chunk."""
+    N = q.shape[0]
+    nch = E2E_CHUNKS if N % E2E_CHUNKS == 0 else 1
+    cn = N // nch
+    per_seq = [t.cpu().pin_memory() for t in (q, k, v, kmask, dout)]
+    bias_h = bias.cpu().pin_memory()
+    devs = [torch.empty_like(t) for t in (q, k, v, kmask, dout)]
+    bias_d = torch.empty_like(bias)
     outs_h = [torch.empty(q.shape, dtype=q.dtype).pin_memory() for _ in range(3)]
     dbias_h = torch.empty(bias.shape, dtype=torch.float32).pin_memory()
-    h2d = sum(t.numel() * t.element_size() for t in hosts)
+    dbias_d = torch.empty(bias.shape, dtype=torch.float32, device=dev)
+    h2d = sum(t.numel() * t.element_size() for t in per_seq) + bias_h.numel() * 2
     d2h = sum(t.numel() * t.element_size() for t in outs_h) + dbias_h.numel() * 4
+    s_in, s_comp, s_out = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
+    main = torch.cuda.current_stream()
 
     def step():
-        for d, h in zip(devs, hosts):
-            d.copy_(h, non_blocking=True)
-        tq, tk, tv, tb, tm, td = devs
-        out, lse = b200.volta_mma(tq, tk, tv, tb, tm, scale=scale)
-        dq, dk, dv, dbias = b200.volta_mma_bwd(tq, tk, tv, tb, tm, out, td, lse, scale=scale)
-        if world > 1:
-            dist.all_reduce(dbias)
-        for h, d in zip(outs_h, (dq, dk, dv)):
-            h.copy_(d, non_blocking=True)
-        dbias_h.copy_(dbias, non_blocking=True)
+        s_in.wait_stream(main)
+        s_comp.wait_stream(main)
+        s_out.wait_stream(main)
+        ev_in, ev_done = [], []
+        with torch.cuda.stream(s_in):
+            bias_d.copy_(bias_h, non_blocking=True)
+            for c in range(nch):
+                for d, h in zip(devs, per_seq):
+                    d[c * cn:(c + 1) * cn].copy_(h[c * cn:(c + 1) * cn], non_blocking=True)
+                e = torch.cuda.Event()
+                e.record(s_in)
+                ev_in.append(e)
+        for c in range(nch):
+            with torch.cuda.stream(s_comp):
+                s_comp.wait_event(ev_in[c])
+                tq, tk, tv, tm, td = (d[c * cn:(c + 1) * cn] for d in devs)
+                out, lse = b200.volta_mma(tq, tk, tv, bias_d, tm, scale=scale)
+                dq, dk, dv, dbias = b200.volta_mma_bwd(tq, tk, tv, bias_d, tm, out, td, lse,
+                                                       scale=scale)
+                if c == 0:
+                    dbias_d.copy_(dbias)
+                else:
+                    dbias_d.add_(dbias)
+                e = torch.cuda.Event()
+                e.record(s_comp)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(e)
+                for h, d in zip(outs_h, (dq, dk, dv)):
+                    h[c * cn:(c + 1) * cn].copy_(d, non_blocking=True)
+                    d.record_stream(s_out)
+        with torch.cuda.stream(s_comp):
+            if world > 1:
+                dist.all_reduce(dbias_d)
+            e = torch.cuda.Event()
+            e.record(s_comp)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(e)
+            dbias_h.copy_(dbias_d, non_blocking=True)
+        main.wait_stream(s_out)
+        main.wait_stream(s_in)
+        main.wait_stream(s_comp)
 
     step()
     torch.cuda.synchronize()
@@ -553,6 +601,7 @@ def run_e2e(args, torch, dist, b200, dev, world, q, k, v, bias, kmask, dout, sca
     ms = float(t.item())
     return {'value': attn_flops(q.shape[0] * world) / (ms * 1e-3) / 1e12, 'unit': 'TFLOP/s',
             'ms_per_step': ms, 'h2d_bytes_per_step': h2d, 'd2h_bytes_per_step': d2h,
+            'chunks': nch, 'streams': 'copy-in / kernels / copy-out',
             'api': 'colabfold_legacy_kernels.b200.volta_mma / volta_mma_bwd (C ABI)'}
 
 

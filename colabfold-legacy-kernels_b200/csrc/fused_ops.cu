@@ -778,10 +778,22 @@ struct TrimulOp {
         // then LN_in(x) in place on the TMA-loaded x atoms
         ln_rows_half<T, CA>(stage + XOFF, t, g, sp, sp + CA, a.eps, red, nullptr, nullptr);
     }
-    // x of worker half g's channels of block j (add_input), loaded ahead of the MMA wait
+    // x of worker half g's channels of block j (add_input), loaded ahead of the MMA wait; with
+    // the first block, the next tile's x_cm lines of this worker's channels are prefetched into
+    // L2, so that the next prologue's loads do not wait for DRAM
     static __device__ void prefetch_block(const Args& a, int t, int g, int m0, int j,
                                           Regs& regs) {
         const int m = m0 + t;
+        if (j == 0) {
+            const int mn = m + (int)gridDim.x * BM;
+            if (mn < a.M) {
+                const float* xc = a.x_cm + (long long)(g * (C / 2)) * a.M + mn;
+#pragma unroll 8
+                for (int i = 0; i < C / 2; ++i) {
+                    asm volatile("prefetch.global.L2 [%0];" ::"l"(xc + (long long)i * a.M));
+                }
+            }
+        }
         if constexpr (ADD) {
             if (m < a.M) {
                 const uint4* xr =

@@ -370,24 +370,14 @@ struct LnGdpOp {
         const int ch = 128 * j + t;
         const float bpv = sp[2 * K + ch], bgv = sp[2 * K + P + ch];
         T* out = ch < CI ? a.left + (long long)ch * a.M : a.right + (long long)(ch - CI) * a.M;
-#pragma unroll 1
-        for (int cc = 0; cc < 4; ++cc) {
-            const int r0 = 32 * cc;
-            uint32_t pr[32], gr[32];
-            tmem_ld32(acc + r0, pr);
-            tmem_ld32(acc + 128 + r0, gr);
-            tmem_wait_ld();
-            const int m = m0 + r0;
-            if (m >= a.M) {
-                continue;
-            }
-            // two rows an instruction (paired fp32): mask * (p + bp) * sigmoid(g + bg) with
-            // sigmoid(x) = (1 + tanh(x / 2)) / 2
-            const uint64_t bp2 = pk2(bpv, bpv), hbg2 = pk2(0.5f * bgv, 0.5f * bgv);
-            const uint64_t half2 = pk2(0.5f, 0.5f);
-            uint32_t w[16];
+        // two rows an instruction (paired fp32): mask * (p + bp) * sigmoid(g + bg) with
+        // sigmoid(x) = (1 + tanh(x / 2)) / 2, for 16 rows from r0
+        const uint64_t bp2 = pk2(bpv, bpv), hbg2 = pk2(0.5f * bgv, 0.5f * bgv);
+        const uint64_t half2 = pk2(0.5f, 0.5f);
+        const auto rows16 = [&](const uint32_t (&pr)[16], const uint32_t (&gr)[16], int r0,
+                                uint32_t* w) {
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
+            for (int q = 0; q < 4; ++q) {
                 const float4 mk = *reinterpret_cast<const float4*>(regs.maskv + r0 + 4 * q);
 #pragma unroll
                 for (int e = 0; e < 4; e += 2) {
@@ -404,6 +394,34 @@ struct LnGdpOp {
                     const float2 o = upk2(mul2(mul2(mm, pv), sg));
                     w[2 * q + e / 2] = E::pack(o.x, o.y);
                 }
+            }
+        };
+        // the tile's rows in four runs of 32, each read as two halves of 16 whose tensor-memory
+        // loads run one half ahead of the arithmetic (a load is issued right after the wait for
+        // the previous one)
+        uint32_t pa[16], ga[16], pb[16], gb[16];
+        tmem_ld16(acc, pa);
+        tmem_ld16(acc + 128, ga);
+        tmem_wait_ld();
+#pragma unroll 1
+        for (int cc = 0; cc < 4; ++cc) {
+            const int r0 = 32 * cc;
+            tmem_ld16(acc + r0 + 16, pb);
+            tmem_ld16(acc + 128 + r0 + 16, gb);
+            uint32_t w[16];
+            rows16(pa, ga, r0, w);
+            tmem_wait_ld();
+            if (cc < 3) {
+                tmem_ld16(acc + r0 + 32, pa);
+                tmem_ld16(acc + 128 + r0 + 32, ga);
+            }
+            rows16(pb, gb, r0 + 16, w + 8);
+            if (cc < 3) {
+                tmem_wait_ld();
+            }
+            const int m = m0 + r0;
+            if (m >= a.M) {
+                continue;
             }
             if (a.tma_out) {
                 // the warp's 32 channels x these 32 rows as one box of left or right

@@ -1194,8 +1194,34 @@ __global__ void __launch_bounds__(TransCfg<C>::THREADS, 1)
             }
             fence_async_smem();
             mbar_arrive(&a_ready);
-            // hidden chunks: bias, ReLU, 16-bit pairs back over the accumulator's columns
-            for (int j = 0; j < NH; ++j) {
+            // the residual (x as it came in) of this worker's columns (up to 128 columns, 16 x 16
+            // bytes), loaded a few 16-byte pieces a hidden chunk so that the loads spread over
+            // the chunks instead of queueing at once before the second GEMM's wait
+            constexpr int RC = SUB == 2 ? C : C / 2;   // columns a worker stores
+            constexpr int RPRE = RC <= 128 && C <= 128 ? RC : 0;  // of them prefetched
+            constexpr int PER = (RPRE / 8 + 7) / 8;  // pieces a chunk (all of them by chunk 8)
+            uint4 res[RPRE / 8 > 0 ? RPRE / 8 : 1];
+            const uint4* xres = reinterpret_cast<const uint4*>(
+                a.x + (long long)m * C + (SUB == 2 ? 0 : g * (C / 2)));
+            // hidden chunks: bias, ReLU, 16-bit pairs back over the accumulator's columns (in
+            // runs of 8, unrolled, so that the first run's residual pieces have fixed indices)
+            for (int jb = 0; jb < NH; jb += 8) {
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) {
+                const int j = jb + jj;
+                if (j >= NH) {
+                    break;
+                }
+                if constexpr (RPRE > 0) {
+                    if (jb == 0 && a.add && m < a.M) {
+#pragma unroll
+                        for (int u = 0; u < PER; ++u) {
+                            if (jj * PER + u < RPRE / 8) {
+                                res[jj * PER + u] = xres[jj * PER + u];
+                            }
+                        }
+                    }
+                }
                 const int hq = q + j, b = hq & 1;
                 mbar_wait(&acc1_full[b], (hq >> 1) & 1, &g_status, kStatusMmaWait, &abort_flag);
                 tc_fence_after();
@@ -1237,18 +1263,15 @@ __global__ void __launch_bounds__(TransCfg<C>::THREADS, 1)
                 tc_fence_before();
                 mbar_arrive(&hid_ready[b]);
             }
-            // the residual (x as it came in) of this worker's columns, loaded before the wait for
-            // the second GEMM (up to 128 columns, 16 x 16 bytes)
-            constexpr int RC = SUB == 2 ? C : C / 2;   // columns a worker stores
-            constexpr int RPRE = RC <= 128 && C <= 128 ? RC : 0;  // of them prefetched
-            uint4 res[RPRE / 8 > 0 ? RPRE / 8 : 1];
+            }
+            // pieces the chunks did not cover (hidden widths below 512)
             if constexpr (RPRE > 0) {
-                const int c0 = SUB == 2 ? 0 : g * (C / 2);
                 if (a.add && m < a.M) {
-                    const uint4* xr = reinterpret_cast<const uint4*>(a.x + (long long)m * C + c0);
 #pragma unroll
-                    for (int i = 0; i < RPRE / 8; ++i) {
-                        res[i] = xr[i];
+                    for (int idx = 0; idx < RPRE / 8; ++idx) {
+                        if (idx >= (NH < 8 ? NH : 8) * PER) {
+                            res[idx] = xres[idx];
+                        }
                     }
                 }
             }

@@ -1143,10 +1143,9 @@ __global__ void __launch_bounds__(TransCfg<C>::THREADS, 1)
                         gemm2(j - 1);
                     }
                 }
-                gemm2(NH - 1);
-                mma_commit(&acc2_full);
                 if (ntile >= 0) {
-                    // the next tile's x, once this tile's GEMM1s no longer read the stage
+                    // the next tile's x, once this tile's GEMM1s no longer read the stage (the
+                    // workers normalise it before they store this tile)
                     mbar_wait(&x_empty, c & 1, &g_status, kStatusMmaWait, &abort_flag);
                     mbar_arrive_expect_tx(&x_full, G::X_BYTES);
                     for (int s = 0; s < SUB; ++s) {
@@ -1156,6 +1155,8 @@ __global__ void __launch_bounds__(TransCfg<C>::THREADS, 1)
                         }
                     }
                 }
+                gemm2(NH - 1);
+                mma_commit(&acc2_full);
             }
             __syncwarp();
             q += NH;
@@ -1163,28 +1164,34 @@ __global__ void __launch_bounds__(TransCfg<C>::THREADS, 1)
             tile = ntile;
         }
     } else {
-        // workers: (g, t) = sub-tile g, row t (SUB = 2), or column half g of row t (SUB = 1)
+        // workers: (g, t) = sub-tile g, row t (SUB = 2), or column half g of row t (SUB = 1).
+        // A tile's order: hidden chunks; then the next computed tile's LayerNorm (its x arrives
+        // while the last chunks run), so that the MMA warp starts the next tile's first GEMMs
+        // while this tile's output is stored; then the output.
         const int g = warp >> 2, t = ((warp & 3) << 5) | lane;
         const uint32_t lane_base = tmem_lane_base(warp);
-        int q = 0, c = 0;
-        for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-            const int w = work_of(tile);
-            const int s = SUB == 2 ? g : 0;
-            const int m = tile * ROWS + s * BM + t;
-            if (w == kPadding) {
-                if (!a.add && m < a.M) {
-                    T* orow = a.out + (long long)m * C;
+        const int s = SUB == 2 ? g : 0;
+        // the next computed tile from `from` on, writing the padding tiles passed over
+        const auto advance = [&](int from) -> int {
+            for (int tl = from; tl < ntiles; tl += gridDim.x) {
+                const int w = work_of(tl);
+                if (w == kCompute) {
+                    return tl;
+                }
+                const int mp = tl * ROWS + s * BM + t;
+                if (w == kPadding && !a.add && mp < a.M) {
+                    T* orow = a.out + (long long)mp * C;
                     const int c0 = SUB == 2 ? 0 : g * (C / 2), c1 = SUB == 2 ? C : c0 + C / 2;
                     for (int cc = c0; cc < c1; cc += 8) {
                         *reinterpret_cast<uint4*>(orow + cc) = make_uint4(0, 0, 0, 0);
                     }
                 }
-                continue;
             }
-            if (w == kSkip) {
-                continue;
-            }
-            mbar_wait(&x_full, c & 1, &g_status, kStatusTmaWait, &abort_flag);
+            return -1;
+        };
+        // LayerNorm of the stage (tile number c of this CTA's computed tiles)
+        const auto normalise = [&](int cn) {
+            mbar_wait(&x_full, cn & 1, &g_status, kStatusTmaWait, &abort_flag);
             uint8_t* tile_s = xs + s * BM * C * 2;
             if constexpr (SUB == 2) {
                 // a full row per worker, no exchange
@@ -1194,6 +1201,14 @@ __global__ void __launch_bounds__(TransCfg<C>::THREADS, 1)
             }
             fence_async_smem();
             mbar_arrive(&a_ready);
+        };
+        int q = 0, c = 0;
+        int tile = advance(blockIdx.x);
+        if (tile >= 0) {
+            normalise(0);
+        }
+        while (tile >= 0) {
+            const int m = tile * ROWS + s * BM + t;
             // the residual (x as it came in) of this worker's columns (up to 128 columns, 16 x 16
             // bytes), loaded a few 16-byte pieces a hidden chunk so that the loads spread over
             // the chunks instead of queueing at once before the second GEMM's wait
@@ -1275,6 +1290,10 @@ __global__ void __launch_bounds__(TransCfg<C>::THREADS, 1)
                     }
                 }
             }
+            const int ntile = advance(tile + gridDim.x);
+            if (ntile >= 0) {
+                normalise(c + 1);
+            }
             mbar_wait(&acc2_full, c & 1, &g_status, kStatusMmaWait, &abort_flag);
             tc_fence_after();
             {
@@ -1339,6 +1358,7 @@ __global__ void __launch_bounds__(TransCfg<C>::THREADS, 1)
             mbar_arrive(&acc2_empty);
             q += NH;
             ++c;
+            tile = ntile;
         }
     }
     tc_fence_before();

@@ -955,11 +955,16 @@ struct TransCfg {
     static constexpr int SUB = C <= 128 ? 2 : 1;
     static constexpr int ROWS = SUB * BM;
     static constexpr int X_BYTES = ROWS * C * 2;           // one stage
-    static constexpr int SLOT = 2 * C * 128;               // w1 chunk + w2 chunk
-    static constexpr int NSLOT = C == 64 ? 6 : C == 128 ? 4 : 2;
+    // hidden chunk width: 128 for the two-sub-tile case (one accumulator buffer a sub-tile, the
+    // two sub-tiles' chains interleaved on the tensor pipe; fewer, wider GEMM1 MMAs), 64 with
+    // two buffers for C = 256
+    static constexpr int HC = SUB == 2 ? 128 : 64;
+    static constexpr int SLOT = 4 * C * HC;                // w1 chunk [HC][C] + w2 chunk [C][HC]
+    static constexpr int NSLOT = C == 64 ? 5 : 2;
     static constexpr int ACC2 = 0;                         // acc2[s] at s * C
-    static constexpr int ACC1 = SUB * C;                   // acc1[s][b] at ACC1 + (b*SUB + s)*64
-    static constexpr int COLS = ACC1 + 2 * SUB * 64;
+    // SUB = 2: acc1[s] at ACC1 + s * HC; SUB = 1: acc1[b] at ACC1 + b * 64
+    static constexpr int ACC1 = SUB * C;
+    static constexpr int COLS = ACC1 + 2 * 64 * (SUB == 2 ? 2 : 1);
     static constexpr int ALLOC = COLS <= 256 ? 256 : 512;
     static constexpr int THREADS = kWorkers + 64;          // + MMA warp + loader warp
 };
@@ -986,7 +991,7 @@ __global__ void __launch_bounds__(TransCfg<C>::THREADS, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* xs = smem;                       // [SUB][C/64 atoms][128 rows][128 B]
-    uint8_t* ring = smem + G::X_BYTES;        // NSLOT x (w1 chunk [C/64][64][128B], w2 chunk)
+    uint8_t* ring = smem + G::X_BYTES;        // NSLOT x (w1 chunk [C/64][HC][128B], w2 chunk)
     float* sp = reinterpret_cast<float*>(ring + NSLOT * G::SLOT);  // scale, offset, b2, b1
     float* red = sp + 3 * C + a.H;            // [4][BM]
     __shared__ uint64_t x_full, x_empty, a_ready, acc1_full[2], hid_ready[2], g2_done[2],
@@ -995,7 +1000,8 @@ __global__ void __launch_bounds__(TransCfg<C>::THREADS, 1)
     __shared__ int abort_flag;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int NH = a.H / 64;
+    constexpr int HC = G::HC;
+    const int NH = a.H / HC;
     const int ntiles = (a.M + ROWS - 1) / ROWS;
     if (warp == kProducerWarp) {
         if (lane == 0) {
@@ -1004,7 +1010,8 @@ __global__ void __launch_bounds__(TransCfg<C>::THREADS, 1)
             mbar_init(&a_ready, kWorkers);
             for (int i = 0; i < 2; ++i) {
                 mbar_init(&acc1_full[i], 1);
-                mbar_init(&hid_ready[i], kWorkers);
+                // SUB = 2: one barrier a sub-tile, its warpgroup's 128 workers
+                mbar_init(&hid_ready[i], SUB == 2 ? kWorkers / 2 : kWorkers);
                 mbar_init(&g2_done[i], 1);
             }
             mbar_init(&acc2_full, 1);
@@ -1058,13 +1065,17 @@ __global__ void __launch_bounds__(TransCfg<C>::THREADS, 1)
                     }
                     uint8_t* dst = ring + slot * G::SLOT;
                     mbar_arrive_expect_tx(&w_full[slot], G::SLOT);
+                    // w1 rows [HC j, HC j + HC) as C/64 atoms of HC rows
                     for (int at = 0; at < C / 64; ++at) {
-                        tma_load_2d(dst + at * 64 * 128, &tw1, &w_full[slot], at * 64, j * 64);
+                        tma_load_2d(dst + at * HC * 128, &tw1, &w_full[slot], at * 64, j * HC);
                     }
-                    // w2T chunk j: [C][64] rows j*C .. j*C + C of the [H/64 * C][64] view
-                    for (int r0 = 0; r0 < C; r0 += 128) {
-                        tma_load_2d(dst + C * 128 + r0 * 128, &tw2, &w_full[slot], 0,
-                                    j * C + r0);
+                    // w2T's 64-wide chunks HC/64 j + u: [C][64] rows (HC/64 j + u) C .. + C of
+                    // the [H/64 * C][64] view, one K atom each
+                    for (int u = 0; u < HC / 64; ++u) {
+                        for (int r0 = 0; r0 < C; r0 += 128) {
+                            tma_load_2d(dst + C * HC * 2 + u * C * 128 + r0 * 128, &tw2,
+                                        &w_full[slot], 0, ((HC / 64) * j + u) * C + r0);
+                        }
                     }
                 }
                 __syncwarp();
@@ -1096,8 +1107,85 @@ __global__ void __launch_bounds__(TransCfg<C>::THREADS, 1)
         }
         const uint32_t id1 = idesc_f16(E::kBf16, 128, 64, false, false);
         const uint32_t id2 = idesc_f16(E::kBf16, 128, C, false, false);
+        // the next tile's x, once this tile's GEMM1s no longer read the stage (the workers
+        // normalise it before they store this tile)
+        const auto load_next_x = [&](int ntile) {
+            mbar_wait(&x_empty, c & 1, &g_status, kStatusMmaWait, &abort_flag);
+            mbar_arrive_expect_tx(&x_full, G::X_BYTES);
+            for (int s = 0; s < SUB; ++s) {
+                for (int at = 0; at < C / 64; ++at) {
+                    tma_load_2d(xs + s * BM * C * 2 + at * ATOM, &tx, &x_full, at * 64,
+                                ntile * ROWS + s * BM);
+                }
+            }
+        };
         while (tile >= 0) {
             const int ntile = next();
+            if constexpr (SUB == 2) {
+                // two chains, one a sub-tile s: GEMM1(s, j) -> acc1[s] -> the warpgroup's
+                // bias + ReLU -> GEMM2(s, j) -> GEMM1(s, j + 1) once GEMM2(s, j) has read acc1[s];
+                // the chains interleave on the tensor pipe
+                if (lane == 0) {
+                    mbar_wait(&a_ready, c & 1, &g_status, kStatusSyncWait, &abort_flag);
+                    tc_fence_after();
+                    const auto gemm1 = [&](int sb, int j) {
+                        const int hq = q + j, slot = hq % NSLOT;
+                        if (sb == 0) {
+                            mbar_wait(&w_full[slot], (hq / NSLOT) & 1, &g_status,
+                                      kStatusTmaWait, &abort_flag);
+                        }
+                        if (hq >= 1) {
+                            // GEMM2(sb, hq - 1) has read acc1[sb]
+                            mbar_wait(&g2_done[sb], (hq - 1) & 1, &g_status, kStatusMmaWait,
+                                      &abort_flag);
+                        }
+                        tc_fence_after();
+                        mma_rows(tmem + G::ACC1 + sb * HC, smem_u32(xs + sb * BM * C * 2),
+                                 smem_u32(ring + slot * G::SLOT), HC, C, 0, HC, E::kBf16, false);
+                        mma_commit(&acc1_full[sb]);
+                        if (sb == SUB - 1 && j == NH - 1) {
+                            mma_commit(&x_empty);
+                        }
+                    };
+                    gemm1(0, 0);
+                    gemm1(1, 0);
+                    for (int j = 0; j < NH; ++j) {
+                        const int hq = q + j, slot = hq % NSLOT;
+                        if (j == NH - 1 && ntile >= 0) {
+                            load_next_x(ntile);
+                        }
+                        const uint32_t w2 = smem_u32(ring + slot * G::SLOT + C * HC * 2);
+                        for (int sb = 0; sb < SUB; ++sb) {
+                            mbar_wait(&hid_ready[sb], hq & 1, &g_status, kStatusSyncWait,
+                                      &abort_flag);
+                            if (j == 0 && sb == 0 && c > 0) {
+                                mbar_wait(&acc2_empty, (c - 1) & 1, &g_status, kStatusSyncWait,
+                                          &abort_flag);
+                            }
+                            tc_fence_after();
+                            for (int k = 0; k < HC / 16; ++k) {
+                                mma_ts(tmem + G::ACC2 + sb * C,
+                                       tmem + G::ACC1 + sb * HC + 64 * (k >> 2) + (k & 3) * 8,
+                                       desc_k128(w2 + (k >> 2) * C * 128 + (k & 3) * 32), id2,
+                                       (j > 0 || k > 0) ? 1u : 0u);
+                            }
+                            mma_commit(&g2_done[sb]);
+                            if (sb == SUB - 1) {
+                                mma_commit(&w_empty[slot]);
+                            }
+                            if (j + 1 < NH) {
+                                gemm1(sb, j + 1);
+                            }
+                        }
+                    }
+                    mma_commit(&acc2_full);
+                }
+                __syncwarp();
+                q += NH;
+                ++c;
+                tile = ntile;
+                continue;
+            }
             if (lane == 0) {
                 mbar_wait(&a_ready, c & 1, &g_status, kStatusSyncWait, &abort_flag);
                 tc_fence_after();
@@ -1144,16 +1232,7 @@ __global__ void __launch_bounds__(TransCfg<C>::THREADS, 1)
                     }
                 }
                 if (ntile >= 0) {
-                    // the next tile's x, once this tile's GEMM1s no longer read the stage (the
-                    // workers normalise it before they store this tile)
-                    mbar_wait(&x_empty, c & 1, &g_status, kStatusMmaWait, &abort_flag);
-                    mbar_arrive_expect_tx(&x_full, G::X_BYTES);
-                    for (int s = 0; s < SUB; ++s) {
-                        for (int at = 0; at < C / 64; ++at) {
-                            tma_load_2d(xs + s * BM * C * 2 + at * ATOM, &tx, &x_full, at * 64,
-                                        ntile * ROWS + s * BM);
-                        }
-                    }
+                    load_next_x(ntile);
                 }
                 gemm2(NH - 1);
                 mma_commit(&acc2_full);
@@ -1214,7 +1293,8 @@ __global__ void __launch_bounds__(TransCfg<C>::THREADS, 1)
             // the chunks instead of queueing at once before the second GEMM's wait
             constexpr int RC = SUB == 2 ? C : C / 2;   // columns a worker stores
             constexpr int RPRE = RC <= 128 && C <= 128 ? RC : 0;  // of them prefetched
-            constexpr int PER = (RPRE / 8 + 7) / 8;  // pieces a chunk (all of them by chunk 8)
+            // pieces a chunk: all of them by chunk 4 (128-wide chunks) or 8 (64-wide)
+            constexpr int PER = (RPRE / 8 + 512 / HC / 2 - 1) / (512 / HC / 2);
             uint4 res[RPRE / 8 > 0 ? RPRE / 8 : 1];
             const uint4* xres = reinterpret_cast<const uint4*>(
                 a.x + (long long)m * C + (SUB == 2 ? 0 : g * (C / 2)));
@@ -1238,27 +1318,42 @@ __global__ void __launch_bounds__(TransCfg<C>::THREADS, 1)
                     }
                 }
                 const int hq = q + j, b = hq & 1;
+                if constexpr (SUB == 2) {
+                    // sub-tile s's chunk j: acc1[s] (HC columns) in halves of 64, each written
+                    // back as 32 columns of 16-bit pairs over its own first columns
+                    mbar_wait(&acc1_full[s], hq & 1, &g_status, kStatusMmaWait, &abort_flag);
+                    tc_fence_after();
+#pragma unroll 1
+                    for (int h = 0; h < HC / 64; ++h) {
+                        const uint32_t base = tmem + G::ACC1 + s * HC + 64 * h + lane_base;
+                        const float* b1 = sp + 3 * C + j * HC + 64 * h;
+                        uint32_t r0[32], r1[32];
+                        tmem_ld32(base, r0);
+                        tmem_ld32(base + 32, r1);
+                        tmem_wait_ld();
+                        uint32_t pk[32];
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            pk[i] = E::pack(
+                                fmaxf(__uint_as_float(r0[2 * i]) + b1[2 * i], 0.f),
+                                fmaxf(__uint_as_float(r0[2 * i + 1]) + b1[2 * i + 1], 0.f));
+                            pk[16 + i] = E::pack(
+                                fmaxf(__uint_as_float(r1[2 * i]) + b1[32 + 2 * i], 0.f),
+                                fmaxf(__uint_as_float(r1[2 * i + 1]) + b1[33 + 2 * i], 0.f));
+                        }
+                        tmem_st16(base, *reinterpret_cast<uint32_t(*)[16]>(pk));
+                        tmem_st16(base + 16, *reinterpret_cast<uint32_t(*)[16]>(pk + 16));
+                    }
+                    tmem_wait_st();
+                    tc_fence_before();
+                    mbar_arrive(&hid_ready[s]);
+                    continue;
+                }
                 mbar_wait(&acc1_full[b], (hq >> 1) & 1, &g_status, kStatusMmaWait, &abort_flag);
                 tc_fence_after();
                 const uint32_t base = tmem + G::ACC1 + (b * SUB + s) * 64 + lane_base;
                 const float* b1 = sp + 3 * C + j * 64;
-                if constexpr (SUB == 2) {
-                    uint32_t r0[32], r1[32];
-                    tmem_ld32(base, r0);
-                    tmem_ld32(base + 32, r1);
-                    tmem_wait_ld();
-                    uint32_t pk[32];
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        pk[i] = E::pack(fmaxf(__uint_as_float(r0[2 * i]) + b1[2 * i], 0.f),
-                                        fmaxf(__uint_as_float(r0[2 * i + 1]) + b1[2 * i + 1], 0.f));
-                        pk[16 + i] =
-                            E::pack(fmaxf(__uint_as_float(r1[2 * i]) + b1[32 + 2 * i], 0.f),
-                                    fmaxf(__uint_as_float(r1[2 * i + 1]) + b1[33 + 2 * i], 0.f));
-                    }
-                    tmem_st16(base, *reinterpret_cast<uint32_t(*)[16]>(pk));
-                    tmem_st16(base + 16, *reinterpret_cast<uint32_t(*)[16]>(pk + 16));
-                } else {
+                {
                     // column half g: hidden columns [32g, 32g+32) -> packed columns [16g, 16g+16)
                     uint32_t r0[32];
                     tmem_ld32(base + 32 * g, r0);
@@ -1612,7 +1707,7 @@ cudaError_t transition_typed(cudaStream_t stream, int dtype, const void* x, cons
     using G = TransCfg<C>;
     CUtensorMap tx, tw1, tw2;
     // w2T [H/64][C][64] viewed as [H/64 * C] rows of 64
-    if (!map_rows(&tx, dtype, x, M, C, C, BM) || !map_rows(&tw1, dtype, w1T, H, C, C, 64) ||
+    if (!map_rows(&tx, dtype, x, M, C, C, BM) || !map_rows(&tw1, dtype, w1T, H, C, C, G::HC) ||
         !map_rows(&tw2, dtype, w2T, (long long)(H / 64) * C, 64, 64, std::min(C, 128))) {
         return cudaErrorInvalidValue;
     }

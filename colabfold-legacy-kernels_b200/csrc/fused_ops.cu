@@ -117,7 +117,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
             }
             if (lane == 0) {
-                Op::load_x(a, &tx, xs0 + k * Op::X_BYTES, &x_full[k], m);
+                Op::load_x(a, &tx, &to1, xs0 + k * Op::X_BYTES, &x_full[k], m);
             }
         }
         bool weights_ready = false;
@@ -159,7 +159,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (m2 >= 0) {
                 if (lane == 0) {
                     mbar_wait(&x_empty[s], (c >> 1) & 1, &g_status, kStatusMmaWait, &abort_flag);
-                    Op::load_x(a, &tx, xs0 + s * Op::X_BYTES, &x_full[s], m2);
+                    Op::load_x(a, &tx, &to1, xs0 + s * Op::X_BYTES, &x_full[s], m2);
                 }
             }
             __syncwarp();
@@ -338,8 +338,8 @@ struct LnGdpOp {
         load_weight(tw0, ws, bar, P, K);
         load_weight(tw1, ws + P * K * 2, bar, P, K);
     }
-    static __device__ void load_x(const Args& a, const CUtensorMap* tx, uint8_t* dst,
-                                  uint64_t* bar, int m0) {
+    static __device__ void load_x(const Args& a, const CUtensorMap* tx, const CUtensorMap*,
+                                  uint8_t* dst, uint64_t* bar, int m0) {
         load_rows_tile(tx, dst, bar, K, m0);
     }
     // block j: output channels [128j, 128j + 128) of the P
@@ -532,8 +532,8 @@ struct ProjOp {
             }
         }
     }
-    static __device__ void load_x(const Args& a, const CUtensorMap* tx, uint8_t* dst,
-                                  uint64_t* bar, int m0) {
+    static __device__ void load_x(const Args& a, const CUtensorMap* tx, const CUtensorMap*,
+                                  uint8_t* dst, uint64_t* bar, int m0) {
         load_rows_tile(tx, dst, bar, K, m0);
     }
     // block j < nb: output columns [128j, 128j + 128) (the last one 64 wide when n % 128 == 64);
@@ -689,8 +689,11 @@ struct TrimulOp {
     using E = Elem<T>;
     static constexpr bool kPingPong = false;
     static constexpr int kSlots = 4, kSlotCols = 128;
-    static constexpr int X_BYTES = (C + CA) * BM * 2;
-    static constexpr int XOFF = C * BM * 2;  // x's atoms after Y's
+    // C <= 64: a stage starts with the tile's float32 x_cm columns ([C][128], by TMA with x when
+    // M % 4 == 0), over whose first half the workers write Y; then x's atoms
+    static constexpr bool kXcmStage = C <= 64;
+    static constexpr int X_BYTES = kXcmStage ? (C * 4 + CA * 2) * BM : (C + CA) * BM * 2;
+    static constexpr int XOFF = kXcmStage ? C * BM * 4 : C * BM * 2;  // x's atoms after Y's
     static constexpr float kOther = -1.f;
     static constexpr int RED_FLOATS = 8 * BM;
     // C <= 64: the output leaves through per-warp staging (two 2 KB box buffers a worker warp)
@@ -704,6 +707,7 @@ struct TrimulOp {
         const float *in_scale, *in_offset, *ln_scale, *ln_offset;
         T* out;
         int M, w_bytes, param_floats, v8;  // v8: 32-byte output stores allowed (C = 128)
+        int xcm_tma;  // x_cm arrives in the stage (map tm1)
         float eps;
     };
     struct Regs {
@@ -738,9 +742,18 @@ struct TrimulOp {
         load_weight(tw0, ws, bar, O, C);
         load_weight(tw1, ws + O * C * 2, bar, O, CA);
     }
-    static __device__ void load_x(const Args& a, const CUtensorMap* tx, uint8_t* dst,
-                                  uint64_t* bar, int m0) {
-        load_rows_tile(tx, dst + XOFF, bar, CA, m0);
+    static __device__ void load_x(const Args& a, const CUtensorMap* tx, const CUtensorMap* txc,
+                                  uint8_t* dst, uint64_t* bar, int m0) {
+        if (kXcmStage && a.xcm_tma) {
+            mbar_arrive_expect_tx(bar, (uint32_t)((CA * 2 + C * 4) * BM));
+            for (int at = 0; at < CA / 64; ++at) {
+                tma_load_2d(dst + XOFF + at * ATOM, tx, bar, at * 64, m0);
+            }
+            // x_cm [C][M] float32: rows [m0, m0 + 128) of every channel, [C][128] in the stage
+            tma_load_2d(dst, txc, bar, m0, 0);
+        } else {
+            load_rows_tile(tx, dst + XOFF, bar, CA, m0);
+        }
     }
     // block j: output channels [64j, 64j+64); LN(x_cm^T) wo in the slot's columns [0, 64),
     // LN_in(x) wg in [64, 128)
@@ -757,9 +770,18 @@ struct TrimulOp {
         const int m = m0 + t;
         const bool in = m < a.M;
         float v[CH];
+        if (kXcmStage && a.xcm_tma) {
+            // from the stage (zeros past M); Y overwrites it only after the second barrier
+            const float* xc = reinterpret_cast<const float*>(stage) + g * CH * BM + t;
 #pragma unroll
-        for (int i = 0; i < CH; ++i) {
-            v[i] = in ? a.x_cm[(long long)(g * CH + i) * a.M + m] : 0.f;
+            for (int i = 0; i < CH; ++i) {
+                v[i] = xc[i * BM];
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < CH; ++i) {
+                v[i] = in ? a.x_cm[(long long)(g * CH + i) * a.M + m] : 0.f;
+            }
         }
         float s = 0.f;
 #pragma unroll
@@ -802,7 +824,7 @@ struct TrimulOp {
     static __device__ void prefetch_block(const Args& a, int t, int g, int m0, int j,
                                           Regs& regs) {
         const int m = m0 + t;
-        if (j == 0) {
+        if (j == 0 && !(kXcmStage && a.xcm_tma)) {
             const int mn = m + (int)gridDim.x * BM;
             if (mn < a.M) {
                 const float* xc = a.x_cm + (long long)(g * (C / 2)) * a.M + mn;
@@ -1644,6 +1666,19 @@ cudaError_t trimul_typed(cudaStream_t stream, int dtype, const float* x_cm, cons
         !encode_tiled(&to, tdt(dtype), 2, 2, out, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B)) {
         return cudaErrorInvalidValue;
     }
+    // x_cm [C][M] float32 into the stage with x (row stride M * 4 bytes a multiple of 16)
+    CUtensorMap txc = tx;
+    const bool xcm_tma =
+        Op::kXcmStage && M % 4 == 0 && (reinterpret_cast<uintptr_t>(x_cm) & 15) == 0;
+    if (xcm_tma) {
+        const uint64_t cdims[2] = {(uint64_t)M, (uint64_t)C};
+        const uint64_t cstrides[1] = {(uint64_t)M};
+        const uint32_t cbox[2] = {(uint32_t)BM, (uint32_t)C};
+        if (!encode_tiled(&txc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, 2, x_cm, cdims, cstrides,
+                          cbox, CU_TENSOR_MAP_SWIZZLE_NONE)) {
+            return cudaErrorInvalidValue;
+        }
+    }
     typename Op::Args a;
     a.x_cm = x_cm;
     a.x = static_cast<const T*>(x);
@@ -1659,10 +1694,11 @@ cudaError_t trimul_typed(cudaStream_t stream, int dtype, const float* x_cm, cons
     a.out = static_cast<T*>(out);
     a.M = M;
     a.v8 = (reinterpret_cast<uintptr_t>(out) & 31) == 0;
+    a.xcm_tma = xcm_tma ? 1 : 0;
     a.w_bytes = (O * C + O * CA) * 2;
     a.param_floats = 2 * CA + 2 * C + 2 * O;
     a.eps = eps;
-    return launch_op<Op>(stream, tx, tw0, tw1, to, to, a);
+    return launch_op<Op>(stream, tx, tw0, tw1, to, txc, a);
 }
 
 template <typename T, int C, int CA>

@@ -1314,7 +1314,9 @@ __global__ void __launch_bounds__(TransCfg<C>::THREADS, 1)
             // bytes), loaded a few 16-byte pieces a hidden chunk so that the loads spread over
             // the chunks instead of queueing at once before the second GEMM's wait
             constexpr int RC = SUB == 2 ? C : C / 2;   // columns a worker stores
-            constexpr int RPRE = RC <= 128 && C <= 128 ? RC : 0;  // of them prefetched
+            // of them: the first 64 prefetched during the hidden chunks (all of them held across
+            // the chunks would not leave the chunks' registers), the rest loaded where used
+            constexpr int RPRE = RC <= 128 && C <= 128 ? (RC < 64 ? RC : 64) : 0;
             // pieces a chunk: all of them by chunk 4 (128-wide chunks) or 8 (64-wide)
             constexpr int PER = (RPRE / 8 + 512 / HC / 2 - 1) / (512 / HC / 2);
             uint4 res[RPRE / 8 > 0 ? RPRE / 8 : 1];
@@ -1436,7 +1438,7 @@ __global__ void __launch_bounds__(TransCfg<C>::THREADS, 1)
                         }
                         if (a.add) {
                             uint4 q0, q1;
-                            if constexpr (RPRE > 0) {
+                            if (16 * ci < RPRE) {
                                 q0 = res[2 * ci];
                                 q1 = res[2 * ci + 1];
                             } else {

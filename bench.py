@@ -228,6 +228,18 @@ def run_ours(args):
                                 device_id=dev)
     pk, pk_kind = peaks()
 
+    if args.only_fusion:
+        # one pair-fusion line alone (profiling runs): its warm-up and timed launches only
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+        res = bench_fusions(torch, b200, dev, rank, world, args.steps, args.warmup, flush, pk,
+                            only=args.only_fusion)
+        if rank == 0:
+            print(json.dumps({'fusions': res}), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+
     cpu_line = None
     if rank == 0 and world == 1 and not args.no_cpu:
         # before any CUDA work: the pool is spawned, never forked
@@ -348,7 +360,7 @@ PAIR = 768            # pair [768, 768, 128]
 C_Z = 128
 
 
-def bench_fusions(torch, b200, dev, rank, world, steps, warmup, flush, pk):
+def bench_fusions(torch, b200, dev, rank, world, steps, warmup, flush, pk, only=None):
     """Pair-stack fusions on BASELINE configs[3] (pair [768, 768, 128] ~ N(0,1), M = 589,824
     rows, W ~ N(0, 1/sqrt(128)), bf16), rows sharded across ranks. Algorithmic bytes: every
     input read once and every output written once (bf16; float32 for x_cm and the LN
@@ -406,6 +418,8 @@ def bench_fusions(torch, b200, dev, rank, world, steps, warmup, flush, pk):
                 M * C_Z * 2 * 2, 2.0 * M * C_Z * 512 * 2))
     res_out = {}
     for name, fn, nbytes, flops in ops:
+        if only is not None and not name.startswith(only):
+            continue
         for _ in range(warmup):
             fn()
         torch.cuda.synchronize()
@@ -616,6 +630,9 @@ def main():
     ap.add_argument('--no-e2e', action='store_true', help='skip the host-buffer end-to-end leg')
     ap.add_argument('--no-inference', action='store_true',
                     help='skip the large-protein inference leg (BASELINE configs[4])')
+    ap.add_argument('--only-fusion', default=None, metavar='NAME',
+                    help='run only the pair-fusion lines whose name starts with NAME (e.g. '
+                         'ln_projection, trimul_epilogue, transition) and print them')
     ap.add_argument('--n-seq', type=int, default=N_SEQ,
                     help='sequences of the attention workload (smaller for profiling runs)')
     args = ap.parse_args()

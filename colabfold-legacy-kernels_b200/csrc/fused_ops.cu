@@ -107,7 +107,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             return -1;
         };
         int cur = blockIdx.x, pcur = blockIdx.x, c = 0, q = 0;
-        int empty_seen[2 * kSlots] = {};  // acc_empty phases waited for, per (team, slot)
+        // parity of the acc_empty phases waited for, one bit per (team, slot): a register, not
+        // a dynamically indexed array (which would live in local memory)
+        uint32_t empty_par = 0;
         if (lane == 0) {
             Op::load_weights(a, &tw0, &tw1, ws, &w_full);
         }
@@ -141,9 +143,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                         // the slot's previous block: consumed by its warpgroup (the n-th of that
                         // warpgroup's blocks in this slot completes the barrier's n-th phase)
                         const int pt = kTeams == 2 ? (((q - kSlots) / nb) & 1) : 0;
-                        const int n_prev = empty_seen[pt * kSlots + slot]++;
-                        mbar_wait(&acc_empty[pt][slot], n_prev & 1, &g_status, kStatusSyncWait,
-                                  &abort_flag);
+                        const int bit = pt * kSlots + slot;
+                        mbar_wait(&acc_empty[pt][slot], (empty_par >> bit) & 1, &g_status,
+                                  kStatusSyncWait, &abort_flag);
+                        empty_par ^= 1u << bit;
                         tc_fence_after();
                     }
                     Op::issue_block(a, smem_u32(xs0 + s * Op::X_BYTES), smem_u32(ws),
@@ -171,7 +174,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         typename Op::Regs regs{};
         Op::bind(regs, stb, warp);
         int c = 0, q = 0;
-        int full_seen[kSlots] = {};  // acc_full phases this warpgroup waited for, per slot
+        uint32_t full_par = 0;  // parity of the acc_full phases this warpgroup waited for, per slot
         // the keep values of the worker's next tile load a tile ahead (the classification's
         // global loads would otherwise stall every tile); a worker's own row value is also
         // handed to the op (ln_gdp's row mask)
@@ -207,9 +210,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int slot = q % kSlots;
                 // global inputs of the block's epilogue start loading before the MMA wait
                 Op::prefetch_block(a, t, g, m0, j, regs);
-                const int n_full = full_seen[slot]++;  // this warpgroup's blocks in the slot
-                mbar_wait(&acc_full[team][slot], n_full & 1, &g_status, kStatusMmaWait,
+                // this warpgroup's blocks in the slot so far, modulo 2
+                mbar_wait(&acc_full[team][slot], (full_par >> slot) & 1, &g_status, kStatusMmaWait,
                           &abort_flag);
+                full_par ^= 1u << slot;
                 tc_fence_after();
                 Op::epilogue_block(a, tmem + slot * kSlotCols + lane_base, sp, t, g, m0, j, regs,
                                    &to, &to1);

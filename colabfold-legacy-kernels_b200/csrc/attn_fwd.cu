@@ -122,6 +122,9 @@ __device__ __forceinline__ uint4 bias_chunk(const uint8_t* stage, int r, int i) 
 struct FwdItem {
     int q0, h, n0, nt_max;
     int ntiles[2];  // key tiles per sequence; 0: no output (past N) or zeros (trim)
+    // sequence w's key tiles, chosen without indexing by a run-time w (which would put the
+    // item in local memory)
+    __device__ __forceinline__ int nt(int w) const { return w == 0 ? ntiles[0] : ntiles[1]; }
 };
 
 template <int NSEQ>
@@ -197,13 +200,13 @@ struct SlotTiles {
         if (u < nitems) {
             it = fwd_item<NSEQ>(p, nqt, u);
         }
-        while (u < nitems && j >= it.ntiles[w]) {
+        while (u < nitems && j >= it.nt(w)) {
             next_item(p, nqt, nitems);
         }
     }
     __device__ __forceinline__ void advance(const FwdParams& p, int nqt, int nitems, int w) {
         ++j;
-        while (u < nitems && j >= it.ntiles[w]) {
+        while (u < nitems && j >= it.nt(w)) {
             next_item(p, nqt, nitems);
         }
     }
@@ -338,7 +341,7 @@ __device__ __forceinline__ void fwd_mma(const FwdParams& p, uint8_t* smem, uint3
             mma_ss(t_s, ad, bd, idesc_s, ks > 0);
         }
         mma_commit(&bar.s_full[w]);
-        if (c.j == c.it.ntiles[w] - 1) {
+        if (c.j == c.it.nt(w) - 1) {
             // the item's Q tiles are free once every sequence's last S is done
             for (int r = arrivals_for<NSEQ>(c.it, w, 0); r > 0; --r) {
                 mma_commit(&bar.q_empty[qb]);
@@ -456,7 +459,7 @@ __global__ void __launch_bounds__(Geometry<DP>::THREADS, 1)
         int g = 0, c = 0;  // key tiles, this slot's tiles
         for (int u = blockIdx.x; u < nitems; u += gridDim.x) {
             const FwdItem it = fwd_item<NSEQ>(p, nqt, u);
-            const int n = it.n0 + w, row = it.q0 + t, h = it.h, nt = it.ntiles[w];
+            const int n = it.n0 + w, row = it.q0 + t, h = it.h, nt = it.nt(w);
             const int g0 = g;
             g += it.nt_max;
             if (n >= p.N) {

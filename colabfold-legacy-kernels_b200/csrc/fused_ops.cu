@@ -43,11 +43,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const __grid_constant__ CUtensorMap to,
                     const __grid_constant__ CUtensorMap to1, const typename Op::Args a) {
     constexpr int kSlots = Op::kSlots, kSlotCols = Op::kSlotCols;
+    // x stages: two (tile c in stage c % 2), or one where a stage is too large for two
+    constexpr int kStages = Op::kStages;
+    static_assert(kStages == 2 || (kStages == 1 && !Op::kPingPong), "stages");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* xs0 = smem;
-    uint8_t* ws = smem + 2 * Op::X_BYTES;
+    uint8_t* ws = smem + kStages * Op::X_BYTES;
     float* sp = reinterpret_cast<float*>(ws + a.w_bytes);
     float* red = sp + a.param_floats;  // [Op::RED_FLOATS]
     uint8_t* stb = reinterpret_cast<uint8_t*>(
@@ -113,7 +116,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             Op::load_weights(a, &tw0, &tw1, ws, &w_full);
         }
-        for (int k = 0; k < 2; ++k) {
+        for (int k = 0; k < kStages; ++k) {
             const int m = next(pcur);
             if (m < 0) {
                 break;
@@ -128,13 +131,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (m < 0) {
                 break;
             }
-            const int s = c & 1;
+            const int s = c % kStages, sph = (c / kStages) & 1;
             if (lane == 0) {
                 if (!weights_ready) {
                     mbar_wait(&w_full, 0, &g_status, kStatusTmaWait, &abort_flag);
                     weights_ready = true;
                 }
-                mbar_wait(&a_ready[s], (c >> 1) & 1, &g_status, kStatusSyncWait, &abort_flag);
+                mbar_wait(&a_ready[s], sph, &g_status, kStatusSyncWait, &abort_flag);
                 tc_fence_after();
                 const int team = kTeams == 2 ? (c & 1) : 0;
                 for (int j = 0; j < nb; ++j, ++q) {
@@ -161,7 +164,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int m2 = next(pcur);
             if (m2 >= 0) {
                 if (lane == 0) {
-                    mbar_wait(&x_empty[s], (c >> 1) & 1, &g_status, kStatusMmaWait, &abort_flag);
+                    mbar_wait(&x_empty[s], sph, &g_status, kStatusMmaWait, &abort_flag);
                     Op::load_x(a, &tx, &to1, xs0 + s * Op::X_BYTES, &x_full[s], m2);
                 }
             }
@@ -192,16 +195,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (work == kSkip) {
                 continue;
             }
-            const int s = c & 1;
+            const int s = c % kStages, sph = (c / kStages) & 1;
             if constexpr (Op::kPingPong) {
-                if (s != g) {  // the other warpgroup's tile
+                if ((c & 1) != g) {  // the other warpgroup's tile
                     q += nb;
                     ++c;
                     continue;
                 }
             }
             uint8_t* stage = xs0 + s * Op::X_BYTES;
-            mbar_wait(&x_full[s], (c >> 1) & 1, &g_status, kStatusTmaWait, &abort_flag);
+            mbar_wait(&x_full[s], sph, &g_status, kStatusTmaWait, &abort_flag);
             Op::prologue(a, stage, sp, red, t, g, m0, regs);
             fence_async_smem();
             mbar_arrive(&a_ready[s]);
@@ -291,6 +294,7 @@ struct LnGdpOp {
     using T = T_;
     using E = Elem<T>;
     static constexpr int P = 2 * CI;
+    static constexpr int kStages = 2;
     static constexpr int X_BYTES = K * BM * 2;
     static constexpr float kOther = 0.f;
     // the tile's row mask max(mask, 0): per warpgroup two buffers (its tile parity)
@@ -476,6 +480,7 @@ struct ProjOp {
     using E = Elem<T>;
     static constexpr int kSlots = 4, kSlotCols = 128;
     static constexpr bool kPingPong = true;
+    static constexpr int kStages = 2;
     static constexpr int X_BYTES = K * BM * 2;
     static constexpr float kOther = -1.f;
     static constexpr int RED_FLOATS = 4;  // unused: a row's LayerNorm is one thread's
@@ -693,9 +698,11 @@ struct TrimulOp {
     using E = Elem<T>;
     static constexpr bool kPingPong = false;
     static constexpr int kSlots = 4, kSlotCols = 128;
-    // C <= 64: a stage starts with the tile's float32 x_cm columns ([C][128], by TMA with x when
-    // M % 4 == 0), over whose first half the workers write Y; then x's atoms
-    static constexpr bool kXcmStage = C <= 64;
+    // A stage starts with the tile's float32 x_cm columns ([C][128], by TMA with x when
+    // M % 4 == 0), over whose first half the workers write Y; then x's atoms. At C = 128 such a
+    // stage (96 KB) leaves room for one only.
+    static constexpr bool kXcmStage = true;
+    static constexpr int kStages = C <= 64 ? 2 : 1;
     static constexpr int X_BYTES = kXcmStage ? (C * 4 + CA * 2) * BM : (C + CA) * BM * 2;
     static constexpr int XOFF = kXcmStage ? C * BM * 4 : C * BM * 2;  // x's atoms after Y's
     static constexpr float kOther = -1.f;
@@ -1534,7 +1541,8 @@ cudaError_t launch_op(cudaStream_t stream, const CUtensorMap& tx, const CUtensor
                       const CUtensorMap& tw1, const CUtensorMap& to, const CUtensorMap& to1,
                       const typename Op::Args& a) {
     auto kern = row_tile_kernel<Op>;
-    const int smem = 2 * Op::X_BYTES + a.w_bytes + (a.param_floats + Op::RED_FLOATS) * 4 + 1024 +
+    const int smem = Op::kStages * Op::X_BYTES + a.w_bytes +
+                     (a.param_floats + Op::RED_FLOATS) * 4 + 1024 +
                      (Op::STORE_BYTES > 0 ? Op::STORE_BYTES + 1024 : 0);
     const cudaError_t e =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);

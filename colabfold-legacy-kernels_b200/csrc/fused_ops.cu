@@ -707,17 +707,16 @@ struct TrimulOp {
     static constexpr int XOFF = kXcmStage ? C * BM * 4 : C * BM * 2;  // x's atoms after Y's
     static constexpr float kOther = -1.f;
     static constexpr int RED_FLOATS = 8 * BM;
-    // C <= 64: the output leaves through per-warp staging (two 2 KB box buffers a worker warp)
-    // and TMA stores; C = 128, whose prologue state fills the registers, stores from registers
-    static constexpr bool kTmaOut = C <= 64;
+    // the output leaves through per-warp staging (two 2 KB box buffers a worker warp) and TMA
+    // stores
     using Stager = RowChunkStager<2>;
-    static constexpr int STORE_BYTES = kTmaOut ? (kWorkers / 32) * Stager::BYTES : 0;
+    static constexpr int STORE_BYTES = (kWorkers / 32) * Stager::BYTES;
     struct Args {
         const float* x_cm;
         const T *x, *woT, *bo, *wgT, *bg, *keep;
         const float *in_scale, *in_offset, *ln_scale, *ln_offset;
         T* out;
-        int M, w_bytes, param_floats, v8;  // v8: 32-byte output stores allowed (C = 128)
+        int M, w_bytes, param_floats;
         int xcm_tma;  // x_cm arrives in the stage (map tm1)
         float eps;
     };
@@ -860,11 +859,7 @@ struct TrimulOp {
     static __device__ void epilogue_block(const Args& a, uint32_t acc, const float* sp, int t,
                                           int g, int m0, int j, Regs& regs,
                                           const CUtensorMap* to, const CUtensorMap* to1) {
-        if constexpr (kTmaOut) {
-            epilogue_staged(a, acc, sp, t, g, m0, j, regs, to);
-        } else {
-            epilogue_direct(a, acc, sp, t, g, m0, j, regs);
-        }
+        epilogue_staged(a, acc, sp, t, g, m0, j, regs, to);
     }
     static __device__ void epilogue_staged(const Args& a, uint32_t acc, const float* sp, int t,
                                            int g, int m0, int j, Regs& regs,
@@ -913,52 +908,6 @@ struct TrimulOp {
             regs.st.write(sb, lane, 2 * hh + 1, w[4], w[5], w[6], w[7]);
         }
         regs.st.issue(to, sb, lane, 64 * j + c0, row0);
-    }
-    static __device__ void epilogue_direct(const Args& a, uint32_t acc, const float* sp, int t,
-                                           int g, int m0, int j, Regs& regs) {
-        const int m = m0 + t;
-        const float* bo = sp + 2 * CA + 2 * C + 64 * j;
-        const float* bg = bo + O;
-        T* orow = a.out + (long long)m * O + 64 * j;
-#pragma unroll 1
-        for (int c0 = 32 * g; c0 < 32 * g + 32; c0 += 16) {
-            uint32_t ro[16], rg[16];
-            tmem_ld16(acc + c0, ro);
-            tmem_ld16(acc + 64 + c0, rg);
-            tmem_wait_ld();
-            if (m < a.M) {
-                float v[16];
-#pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    v[e] = (__uint_as_float(ro[e]) + bo[c0 + e]) *
-                           sigmoid_fast(__uint_as_float(rg[e]) + bg[c0 + e]);
-                }
-                if constexpr (ADD) {
-                    const int ri = (c0 - 32 * g) / 8;
-                    const uint4 q0 = regs.res[ri], q1 = regs.res[ri + 1];
-                    const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        const float2 f = E::unpack(qw[e]);
-                        v[2 * e] += f.x;
-                        v[2 * e + 1] += f.y;
-                    }
-                }
-                uint32_t w[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    w[e] = E::pack(v[2 * e], v[2 * e + 1]);
-                }
-                if (a.v8) {
-                    st_global_v8(orow + c0, make_uint4(w[0], w[1], w[2], w[3]),
-                                 make_uint4(w[4], w[5], w[6], w[7]));
-                } else {
-                    *reinterpret_cast<uint4*>(orow + c0) = make_uint4(w[0], w[1], w[2], w[3]);
-                    *reinterpret_cast<uint4*>(orow + c0 + 8) =
-                        make_uint4(w[4], w[5], w[6], w[7]);
-                }
-            }
-        }
     }
     static __device__ void padding(const Args& a, int m0, int t, int g) {
         const int m = m0 + t;
@@ -1675,9 +1624,7 @@ cudaError_t trimul_typed(cudaStream_t stream, int dtype, const float* x_cm, cons
         !map_rows(&tw1, dtype, wgT, O, CA, CA, weight_box(O))) {
         return cudaErrorInvalidValue;
     }
-    to = tx;
-    if (Op::kTmaOut &&
-        !encode_tiled(&to, tdt(dtype), 2, 2, out, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B)) {
+    if (!encode_tiled(&to, tdt(dtype), 2, 2, out, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B)) {
         return cudaErrorInvalidValue;
     }
     // x_cm [C][M] float32 into the stage with x (row stride M * 4 bytes a multiple of 16)
@@ -1707,7 +1654,6 @@ cudaError_t trimul_typed(cudaStream_t stream, int dtype, const float* x_cm, cons
     a.ln_offset = ln_offset;
     a.out = static_cast<T*>(out);
     a.M = M;
-    a.v8 = (reinterpret_cast<uintptr_t>(out) & 31) == 0;
     a.xcm_tma = xcm_tma ? 1 : 0;
     a.w_bytes = (O * C + O * CA) * 2;
     a.param_floats = 2 * CA + 2 * C + 2 * O;

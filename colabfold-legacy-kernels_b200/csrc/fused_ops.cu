@@ -1303,31 +1303,39 @@ __global__ void __launch_bounds__(TransCfg<C>::THREADS, 1)
                 }
                 const int hq = q + j, b = hq & 1;
                 if constexpr (SUB == 2) {
-                    // sub-tile s's chunk j: acc1[s] (HC columns) in halves of 64, each written
-                    // back as 32 columns of 16-bit pairs over its own first columns
+                    // sub-tile s's chunk j: acc1[s] (HC columns) in quarters of 32, quarter q
+                    // written back as 16 columns of 16-bit pairs at 64 (q / 2) + 16 (q % 2) (the
+                    // A layout of GEMM2's K steps), over columns already read; each quarter's
+                    // tensor-memory load is issued before the previous quarter's arithmetic
                     mbar_wait(&acc1_full[s], hq & 1, &g_status, kStatusMmaWait, &abort_flag);
                     tc_fence_after();
-#pragma unroll 1
-                    for (int h = 0; h < HC / 64; ++h) {
-                        const uint32_t base = tmem + G::ACC1 + s * HC + 64 * h + lane_base;
-                        const float* b1 = sp + 3 * C + j * HC + 64 * h;
-                        uint32_t r0[32], r1[32];
-                        tmem_ld32(base, r0);
-                        tmem_ld32(base + 32, r1);
-                        tmem_wait_ld();
-                        uint32_t pk[32];
+                    const uint32_t base = tmem + G::ACC1 + s * HC + lane_base;
+                    const float* b1 = sp + 3 * C + j * HC;
+                    const auto relu_pack = [&](const uint32_t (&r)[32], int qq) {
+                        uint32_t pk[16];
 #pragma unroll
                         for (int i = 0; i < 16; ++i) {
                             pk[i] = E::pack(
-                                fmaxf(__uint_as_float(r0[2 * i]) + b1[2 * i], 0.f),
-                                fmaxf(__uint_as_float(r0[2 * i + 1]) + b1[2 * i + 1], 0.f));
-                            pk[16 + i] = E::pack(
-                                fmaxf(__uint_as_float(r1[2 * i]) + b1[32 + 2 * i], 0.f),
-                                fmaxf(__uint_as_float(r1[2 * i + 1]) + b1[33 + 2 * i], 0.f));
+                                fmaxf(__uint_as_float(r[2 * i]) + b1[32 * qq + 2 * i], 0.f),
+                                fmaxf(__uint_as_float(r[2 * i + 1]) + b1[32 * qq + 2 * i + 1],
+                                      0.f));
                         }
-                        tmem_st16(base, *reinterpret_cast<uint32_t(*)[16]>(pk));
-                        tmem_st16(base + 16, *reinterpret_cast<uint32_t(*)[16]>(pk + 16));
-                    }
+                        tmem_st16(base + 64 * (qq >> 1) + 16 * (qq & 1), pk);
+                    };
+                    static_assert(HC == 128, "four quarters");
+                    uint32_t ra[32], rb[32];
+                    tmem_ld32(base, ra);
+                    tmem_wait_ld();
+                    tmem_ld32(base + 32, rb);
+                    relu_pack(ra, 0);
+                    tmem_wait_ld();
+                    tmem_ld32(base + 64, ra);
+                    relu_pack(rb, 1);
+                    tmem_wait_ld();
+                    tmem_ld32(base + 96, rb);
+                    relu_pack(ra, 2);
+                    tmem_wait_ld();
+                    relu_pack(rb, 3);
                     tmem_wait_st();
                     tc_fence_before();
                     mbar_arrive(&hid_ready[s]);

@@ -2,10 +2,12 @@
 //
 // A CTA walks 128-row tiles of the input (tile = blockIdx.x, + gridDim.x, ...). Warp 8 is the
 // producer: lane 0 loads the op's weights once (TMA, resident in shared memory for the whole
-// CTA), streams x tiles two stages deep, and issues the tcgen05 MMAs of each tile into tensor
-// memory. Warps 0-7 are two warpgroups of workers; worker (g, t) owns row t of the tile (TMEM
-// lane t) and half g of its columns: it runs the op's prologue (LayerNorm in place on the
-// swizzled tile) and epilogue (accumulators from TMEM, bias, gating, residual, stores).
+// CTA), streams x tiles two stages deep (one where a stage is large), and issues the tcgen05
+// MMAs of each tile into tensor memory. Warps 0-7 are two warpgroups of workers; worker (g, t)
+// owns row t of the tile (TMEM lane t) and either half g of its columns or, for ops that run
+// the warpgroups ping-pong, the whole row of every other tile: it runs the op's prologue
+// (LayerNorm in place on the swizzled tile) and epilogue (accumulators from TMEM, bias,
+// gating, residual, stores).
 //
 // Row tiles follow the reference's keep rule (tile_work, colabfold-legacy-kernels
 // cuda/volta_gdp.h:114-136): a tile is computed when a row's keep is above zero, written as
@@ -364,11 +366,9 @@ __device__ __forceinline__ void ln_row_regs(uint8_t* tile, int t, const float* s
 // LayerNorm of row t in place on a swizzled tile, the whole row by one thread (no exchange, no
 // barrier): three passes over the row in shared memory (sum, centred sum of squares, then the
 // normalised row rounded to T and written back), so the row never sits in registers.
-// use(ch, y[8]) sees the rounded outputs of every 8-column chunk (the per-head bias of
-// ln_projection).
-template <typename T, int K, typename Use>
+template <typename T, int K>
 __device__ __forceinline__ void ln_row_full(uint8_t* tile, int t, const float* scale,
-                                            const float* offset, float eps, Use&& use) {
+                                            const float* offset, float eps) {
     using E = Elem<T>;
     uint64_t acc[4];
 #pragma unroll
@@ -418,7 +418,6 @@ __device__ __forceinline__ void ln_row_full(uint8_t* tile, int t, const float* s
         const float sc[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
         const float of[8] = {o0.x, o0.y, o0.z, o0.w, o1.x, o1.y, o1.z, o1.w};
         uint32_t o[4];
-        float yr[8];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             const float2 f = E::unpack(ww[e]);
@@ -426,11 +425,7 @@ __device__ __forceinline__ void ln_row_full(uint8_t* tile, int t, const float* s
                                     pk2(sc[2 * e], sc[2 * e + 1]), pk2(of[2 * e], of[2 * e + 1]));
             const float2 yf = upk2(y);
             o[e] = E::pack(yf.x, yf.y);
-            const float2 rr = E::unpack(o[e]);
-            yr[2 * e] = rr.x;
-            yr[2 * e + 1] = rr.y;
         }
-        use(ch, yr);
         *reinterpret_cast<uint4*>(p) = make_uint4(o[0], o[1], o[2], o[3]);
     }
 }

@@ -563,7 +563,7 @@ struct ProjOp {
     static __device__ void prologue(const Args& a, uint8_t* stage, const float* sp, float* red,
                                     int t, int g, int m0, Regs&) {
         if constexpr (LN) {
-            ln_row_full<T, K>(stage, t, sp, sp + K, a.eps, [](int, const float*) {});
+            ln_row_full<T, K>(stage, t, sp, sp + K, a.eps);
         }
     }
     // the residual of row t's first 64 columns of block j, loaded ahead of the MMA wait
@@ -701,10 +701,9 @@ struct TrimulOp {
     // A stage starts with the tile's float32 x_cm columns ([C][128], by TMA with x when
     // M % 4 == 0), over whose first half the workers write Y; then x's atoms. At C = 128 such a
     // stage (96 KB) leaves room for one only.
-    static constexpr bool kXcmStage = true;
     static constexpr int kStages = C <= 64 ? 2 : 1;
-    static constexpr int X_BYTES = kXcmStage ? (C * 4 + CA * 2) * BM : (C + CA) * BM * 2;
-    static constexpr int XOFF = kXcmStage ? C * BM * 4 : C * BM * 2;  // x's atoms after Y's
+    static constexpr int X_BYTES = (C * 4 + CA * 2) * BM;
+    static constexpr int XOFF = C * BM * 4;  // x's atoms after the x_cm / Y region
     static constexpr float kOther = -1.f;
     static constexpr int RED_FLOATS = 8 * BM;
     // the output leaves through per-warp staging (two 2 KB box buffers a worker warp) and TMA
@@ -754,7 +753,7 @@ struct TrimulOp {
     }
     static __device__ void load_x(const Args& a, const CUtensorMap* tx, const CUtensorMap* txc,
                                   uint8_t* dst, uint64_t* bar, int m0) {
-        if (kXcmStage && a.xcm_tma) {
+        if (a.xcm_tma) {
             mbar_arrive_expect_tx(bar, (uint32_t)((CA * 2 + C * 4) * BM));
             for (int at = 0; at < CA / 64; ++at) {
                 tma_load_2d(dst + XOFF + at * ATOM, tx, bar, at * 64, m0);
@@ -780,7 +779,7 @@ struct TrimulOp {
         const int m = m0 + t;
         const bool in = m < a.M;
         float v[CH];
-        if (kXcmStage && a.xcm_tma) {
+        if (a.xcm_tma) {
             // from the stage (zeros past M); Y overwrites it only after the second barrier
             const float* xc = reinterpret_cast<const float*>(stage) + g * CH * BM + t;
 #pragma unroll
@@ -834,7 +833,7 @@ struct TrimulOp {
     static __device__ void prefetch_block(const Args& a, int t, int g, int m0, int j,
                                           Regs& regs) {
         const int m = m0 + t;
-        if (j == 0 && !(kXcmStage && a.xcm_tma)) {
+        if (j == 0 && !a.xcm_tma) {
             const int mn = m + (int)gridDim.x * BM;
             if (mn < a.M) {
                 const float* xc = a.x_cm + (long long)(g * (C / 2)) * a.M + mn;
@@ -1256,7 +1255,7 @@ __global__ void __launch_bounds__(TransCfg<C>::THREADS, 1)
             uint8_t* tile_s = xs + s * BM * C * 2;
             if constexpr (SUB == 2) {
                 // a full row per worker, no exchange
-                ln_row_full<T, C>(tile_s, t, sp, sp + C, a.eps, [](int, const float*) {});
+                ln_row_full<T, C>(tile_s, t, sp, sp + C, a.eps);
             } else {
                 ln_rows_half<T, C>(tile_s, t, g, sp, sp + C, a.eps, red, nullptr, nullptr);
             }
@@ -1638,7 +1637,7 @@ cudaError_t trimul_typed(cudaStream_t stream, int dtype, const float* x_cm, cons
     // x_cm [C][M] float32 into the stage with x (row stride M * 4 bytes a multiple of 16)
     CUtensorMap txc = tx;
     const bool xcm_tma =
-        Op::kXcmStage && M % 4 == 0 && (reinterpret_cast<uintptr_t>(x_cm) & 15) == 0;
+        M % 4 == 0 && (reinterpret_cast<uintptr_t>(x_cm) & 15) == 0;
     if (xcm_tma) {
         const uint64_t cdims[2] = {(uint64_t)M, (uint64_t)C};
         const uint64_t cstrides[1] = {(uint64_t)M};

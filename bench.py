@@ -16,6 +16,12 @@ dBias partials are summed by an NCCL all-reduce. value = algorithmic FLOPs of th
 
 --impl reference times the reference's CPU arithmetic for the same path (the float32 port of
 its closed-form oracle, oracle/attention.py) on this host's cores, one bounded sample per step.
+
+The line also carries the e2e leg (the same step from pinned host buffers through the public
+API, in 8 chunks of sequences on copy-in / kernel / copy-out streams), the pair fusions on
+BASELINE configs[3] and the large-protein inference leg; --no-e2e, --no-fusions,
+--no-inference and --no-cpu skip legs, and --only-fusion NAME runs one fusion line alone (the
+form the ncu captures use).
 """
 import argparse
 import json

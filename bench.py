@@ -416,6 +416,10 @@ def bench_fusions(torch, b200, dev, rank, world, steps, warmup, flush, pk, only=
                 lambda: b200.volta_out_proj(o, woT, bo, res, keep1, has_residual=True,
                                             has_keep=False),
                 M * C_Z * 2 * 3, 2.0 * M * C_Z * C_Z))
+    ln_out = torch.empty_like(x)
+    ops.append(('layer_norm C=128',
+                lambda: b200.volta_layer_norm(x, ones, zeros, eps=1e-5, out=ln_out),
+                M * C_Z * 2 * 2, 0.0))
     w1T, b1 = rn(512, C_Z, s=w), rn(512, s=0.1)
     w2T, b2 = rn(512 * C_Z, s=512 ** -0.5), rn(C_Z, s=0.1)
     ops.append(('transition 128->512->128 add_input',

@@ -1456,6 +1456,115 @@ __global__ void __launch_bounds__(TransCfg<C>::THREADS, 1)
 }
 
 // ---------------------------------------------------------------------------------------------
+// VoltaLayerNorm: out [M, C] = (x - mean) rstd scale + offset over the last axis, with the
+// reference's one-pass statistics: fp32 sum and sum of squares, var = max(E[x^2] - mean^2, 0),
+// rstd = rsqrt(var + eps), the result rounded to the 16-bit type (cuda/volta_ops.cu:27-60).
+// No tensor-core work: a bandwidth kernel, every row read once and written once.
+// ---------------------------------------------------------------------------------------------
+constexpr int kLnRows = 4;  // rows a thread group has in flight
+
+// C = 8G, G a power of two <= 32: G consecutive lanes take a row, 8 columns (one 16-byte load
+// and store) each; a warp takes 32/G rows per pass, kLnRows passes at once (all loads issued
+// before any arithmetic). Warp-uniform loop bounds keep every lane in the shuffles.
+template <typename T, int G>
+__global__ void __launch_bounds__(256) layer_norm_vec_kernel(const T* __restrict__ x,
+                                                             const float* __restrict__ scale,
+                                                             const float* __restrict__ offset,
+                                                             T* __restrict__ out, long long M,
+                                                             float eps) {
+    using E = Elem<T>;
+    constexpr int C = 8 * G, RPW = 32 / G;  // columns, rows a warp-pass
+    const int lane = threadIdx.x & 31, sub = lane & (G - 1);
+    const long long warp = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
+    float sc[8], of[8];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const float4 s4 = *reinterpret_cast<const float4*>(scale + 8 * sub + 4 * h);
+        const float4 o4 = *reinterpret_cast<const float4*>(offset + 8 * sub + 4 * h);
+        sc[4 * h] = s4.x, sc[4 * h + 1] = s4.y, sc[4 * h + 2] = s4.z, sc[4 * h + 3] = s4.w;
+        of[4 * h] = o4.x, of[4 * h + 1] = o4.y, of[4 * h + 2] = o4.z, of[4 * h + 3] = o4.w;
+    }
+    const float inv = 1.0f / (float)C;
+    for (long long r0 = warp * RPW * kLnRows; r0 < M; r0 += nwarps * RPW * kLnRows) {
+        uint4 v[kLnRows];
+#pragma unroll
+        for (int i = 0; i < kLnRows; ++i) {
+            const long long row = r0 + i * RPW + lane / G;
+            v[i] = row < M ? *reinterpret_cast<const uint4*>(x + row * C + 8 * sub)
+                           : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int i = 0; i < kLnRows; ++i) {
+            const long long row = r0 + i * RPW + lane / G;
+            const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+            float f[8];
+            float sum = 0.f, sq = 0.f;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float2 p = E::unpack(w[e]);
+                f[2 * e] = p.x;
+                f[2 * e + 1] = p.y;
+                sum += p.x + p.y;
+                sq = fmaf(p.x, p.x, fmaf(p.y, p.y, sq));
+            }
+#pragma unroll
+            for (int o = G / 2; o > 0; o >>= 1) {
+                sum += __shfl_xor_sync(0xffffffffu, sum, o);
+                sq += __shfl_xor_sync(0xffffffffu, sq, o);
+            }
+            const float mean = sum * inv;
+            const float var = fmaxf(sq * inv - mean * mean, 0.f);
+            const float rstd = rsqrtf(var + eps);
+            uint32_t o4[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                o4[e] = E::pack(fmaf((f[2 * e] - mean) * rstd, sc[2 * e], of[2 * e]),
+                                fmaf((f[2 * e + 1] - mean) * rstd, sc[2 * e + 1], of[2 * e + 1]));
+            }
+            if (row < M) {
+                *reinterpret_cast<uint4*>(out + row * C + 8 * sub) =
+                    make_uint4(o4[0], o4[1], o4[2], o4[3]);
+            }
+        }
+    }
+}
+
+// Any C (and unaligned buffers): a warp a row, lane-strided elements, as the reference does.
+template <typename T>
+__global__ void __launch_bounds__(256) layer_norm_row_kernel(const T* __restrict__ x,
+                                                             const float* __restrict__ scale,
+                                                             const float* __restrict__ offset,
+                                                             T* __restrict__ out, long long M,
+                                                             int C, float eps) {
+    using E = Elem<T>;
+    const int lane = threadIdx.x & 31;
+    const long long warp = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
+    const float inv = 1.0f / (float)C;
+    for (long long row = warp; row < M; row += nwarps) {
+        const T* xr = x + row * C;
+        float sum = 0.f, sq = 0.f;
+        for (int c = lane; c < C; c += 32) {
+            const float v = E::to_f(xr[c]);
+            sum += v;
+            sq = fmaf(v, v, sq);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            sq += __shfl_xor_sync(0xffffffffu, sq, o);
+        }
+        const float mean = sum * inv;
+        const float rstd = rsqrtf(fmaxf(sq * inv - mean * mean, 0.f) + eps);
+        T* orow = out + row * C;
+        for (int c = lane; c < C; c += 32) {
+            orow[c] = E::from_f(fmaf((E::to_f(xr[c]) - mean) * rstd, scale[c], offset[c]));
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
 // host
 // ---------------------------------------------------------------------------------------------
 int sm_count() {
@@ -1741,6 +1850,34 @@ cudaError_t transition_typed(cudaStream_t stream, int dtype, const void* x, cons
     return cudaGetLastError();
 }
 
+template <typename T>
+cudaError_t layer_norm_typed(cudaStream_t stream, const void* x, const float* scale,
+                             const float* offset, void* out, long long M, int C, float eps) {
+    const T* xp = static_cast<const T*>(x);
+    T* op = static_cast<T*>(out);
+    const bool vec = C % 8 == 0 && C / 8 <= 32 && ((C / 8) & (C / 8 - 1)) == 0 &&
+                     ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out) |
+                       reinterpret_cast<uintptr_t>(scale) | reinterpret_cast<uintptr_t>(offset)) &
+                      15) == 0;
+    // persistent grid: 8 blocks of 256 threads an SM at most
+    const long long cap = (long long)sm_count() * 8;
+    if (vec) {
+        const int G = C / 8;
+        const long long rows_per_block = 8LL * (32 / G) * kLnRows;  // 8 warps a block
+        const long long blocks = std::min(cap, (M + rows_per_block - 1) / rows_per_block);
+        switch (G) {
+#define CFLK_LN(GG)                                                                                case GG:                                                                                           layer_norm_vec_kernel<T, GG><<<(unsigned)blocks, 256, 0, stream>>>(xp, scale, offset,                                                                              op, M, eps);               break;
+            CFLK_LN(1) CFLK_LN(2) CFLK_LN(4) CFLK_LN(8) CFLK_LN(16) CFLK_LN(32)
+#undef CFLK_LN
+        }
+    } else {
+        const long long blocks = std::min(cap, (M + 7) / 8);
+        layer_norm_row_kernel<T><<<(unsigned)blocks, 256, 0, stream>>>(xp, scale, offset, op, M,
+                                                                        C, eps);
+    }
+    return cudaGetLastError();
+}
+
 }  // namespace
 
 unsigned read_and_clear_status_fused() {
@@ -1941,4 +2078,28 @@ extern "C" int cflk_volta_transition(void* stream, int dtype, const void* x, con
     e = dtype == kBF16 ? CFLK_TR(__nv_bfloat16) : CFLK_TR(__half);
 #undef CFLK_TR
     return launch_status(e, "transition");
+}
+
+extern "C" int cflk_volta_layer_norm(void* stream, int dtype, const void* x, const float* scale,
+                                     const float* offset, void* out, int64_t M, int64_t C,
+                                     float eps) {
+    clear_error();
+    if (dtype != kF16 && dtype != kBF16) {
+        return fail(kInvalidArgument, "layer_norm: dtype must be f16 or bf16");
+    }
+    if (M < 0 || C < 1 || C > (1 << 20)) {
+        return fail(kInvalidArgument, "x must be [M,C]");
+    }
+    if (M == 0) {
+        return kOk;
+    }
+    if (x == nullptr || scale == nullptr || offset == nullptr || out == nullptr) {
+        return fail(kInvalidArgument, "layer_norm: null buffer");
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const cudaError_t e =
+        dtype == kBF16
+            ? layer_norm_typed<__nv_bfloat16>(s, x, scale, offset, out, M, (int)C, eps)
+            : layer_norm_typed<__half>(s, x, scale, offset, out, M, (int)C, eps);
+    return launch_status(e, "layer_norm");
 }

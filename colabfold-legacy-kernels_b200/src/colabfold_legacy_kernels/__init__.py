@@ -47,6 +47,7 @@ _TABLE = {
         (70, "libvolta_wmma_bwd.so", "VoltaWmmaBwd"),
     ),
     "layer_norm": (
+        (100, _SM100_LIB, "VoltaLayerNorm"),
         (70, "libvolta_ops.so", "VoltaLayerNorm"),
     ),
     "gated_dual_proj": (
@@ -97,6 +98,7 @@ _C_SYMBOLS = {
     "VoltaLnProj": "cflk_volta_ln_proj",
     "VoltaOutProj": "cflk_volta_out_proj",
     "VoltaTransition": "cflk_volta_transition",
+    "VoltaLayerNorm": "cflk_volta_layer_norm",
 }
 
 KERNELS = tuple(_TABLE)

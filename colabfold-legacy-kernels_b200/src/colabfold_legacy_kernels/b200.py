@@ -38,6 +38,7 @@ _SIGS = {
     'cflk_volta_out_proj': [_p, _int, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64],
     'cflk_volta_transition': [_p, _int, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64,
                               _f32, _int],
+    'cflk_volta_layer_norm': [_p, _int, _p, _p, _p, _p, _i64, _i64, _f32],
 }
 
 _lib = None
@@ -185,6 +186,29 @@ def volta_mma_bwd(q, k, v, bias, kmask, out, dout, lse, *, scale, want_dbias=Tru
 
 
 # ---- fused pair-stack ops -------------------------------------------------------------------
+
+def volta_layer_norm(x, scale, offset, *, eps, out=None):
+    """VoltaLayerNorm: out [M,C] (one-pass float32 statistics). `out` may be given (and may be
+    x)."""
+    who = 'layer_norm'
+    if x.dim() != 2:
+        raise ValueError('x must be [M,C]')
+    M, C = x.shape
+    if scale.numel() != C or offset.numel() != C:
+        raise ValueError('layer_norm: scale and offset must be [C]')
+    dt = _dtype_code(x)
+    if out is None:
+        out = torch.empty_like(x)
+    if out.shape != x.shape or out.dtype != x.dtype:
+        raise ValueError('layer_norm: out must match x')
+    if M == 0:
+        return out
+    rc = lib().cflk_volta_layer_norm(_stream(), dt, _ptr(x), _f32_ptr(scale, 'scale', who),
+                                     _f32_ptr(offset, 'offset', who), _ptr(out), M, C,
+                                     float(eps))
+    _check(rc, who)
+    return out
+
 
 def _keep(keep, has_keep, M, who):
     if not has_keep:

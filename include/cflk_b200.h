@@ -162,6 +162,15 @@ CFLK_API int cflk_volta_transition(void* stream, int dtype, const void* x, const
                                    const void* w2T, const void* b2, const void* keep, void* out,
                                    int64_t M, int64_t C, int64_t H, float eps, int add_input);
 
+/* VoltaLayerNorm: out [M,C] = (x - mean) * rsqrt(var + eps) * scale + offset over the last
+ * axis, the statistics in float32 in one pass (var = max(E[x^2] - mean^2, 0)). x, out [M,C]
+ * (out may alias x); scale, offset [C] float32; any C >= 1 (vector path when C / 8 is a power of
+ * two up to 32 and the buffers are 16-byte aligned). Replaces VoltaLayerNorm,
+ * cuda/volta_ops.cu:27-91. */
+CFLK_API int cflk_volta_layer_norm(void* stream, int dtype, const void* x, const float* scale,
+                                   const float* offset, void* out, int64_t M, int64_t C,
+                                   float eps);
+
 #ifdef __cplusplus
 }
 #endif

@@ -10,6 +10,8 @@ packed_attn.ref_output_projection, transition.ref_transition; tests/test_fused.p
 is not vendored, has no pinned version and is absent here. This module restates the math from
 the reference's handler contracts and kernels instead:
 
+  * VoltaLayerNorm (the standalone op): one-pass float32 sum and sum of squares, the variance
+    clamped at zero (cuda/volta_ops.cu:27-60).
   * LayerNorm: two-pass float32 statistics, eps inside the rsqrt, result rounded to the 16-bit
     compute type before the GEMM (ln_rows, cuda/volta_gdp.h:208-240; ln_columns over the
     channel-major float32 x_cm, :244-286).
@@ -47,6 +49,20 @@ def layer_norm(x, scale, offset, eps):
     rstd = np.float32(1.0) / np.sqrt(var + np.float32(eps))
     y = d * rstd * np.asarray(scale, np.float32) + np.asarray(offset, np.float32)
     return y.astype(np.float64)
+
+
+def layer_norm_one_pass(x, scale, offset, eps, dtype):
+    """VoltaLayerNorm (cuda/volta_ops.cu:27-60): float32 sum and sum of squares over the last
+    axis, mean = sum / C, var = max(sqsum / C - mean^2, 0), rstd = 1 / sqrt(var + eps),
+    out = (x - mean) * rstd * scale + offset rounded to `dtype`; float64 out."""
+    v = np.asarray(x, np.float32)
+    inv = np.float32(1.0 / v.shape[-1])
+    mean = v.sum(-1, keepdims=True, dtype=np.float32) * inv
+    sq = (v * v).sum(-1, keepdims=True, dtype=np.float32) * inv
+    var = np.maximum(sq - mean * mean, np.float32(0))
+    rstd = np.float32(1.0) / np.sqrt(var + np.float32(eps))
+    y = (v - mean) * rstd * np.asarray(scale, np.float32) + np.asarray(offset, np.float32)
+    return round_to(y.astype(np.float64), dtype)
 
 
 def sigmoid(g):

@@ -57,6 +57,41 @@ def close(name, got, want, tol=0.02):
     assert r < tol and e < 1e-2, '%s: rel_max %.3e rel_l2 %.3e' % (name, r, e)
 
 
+# ---- layer_norm (VoltaLayerNorm) --------------------------------------------------------------
+
+@pytest.mark.parametrize('dt', ['bf16', 'f16'])
+@pytest.mark.parametrize('M', ROWS)
+@pytest.mark.parametrize('C', [128, 64, 256, 8, 96, 100])
+def test_layer_norm(C, M, dt, cuda_device):
+    """Vector path (C / 8 a power of two up to 32) and the row path (96, 100), against the
+    one-pass oracle; rows with a large common offset check the statistics' accumulation."""
+    g = Gen(7, dt)
+    x = g.h(M, C, s=2., mean=0.5)
+    sc, off = g.f(C, s=.1, mean=1.), g.f(C, s=.1)
+    want = of.layer_norm_one_pass(x, sc, off, 1e-5, dt)
+    got = b200().volta_layer_norm(dev16(x, dt, cuda_device), dev32(sc, cuda_device),
+                                  dev32(off, cuda_device), eps=1e-5)
+    close('layer_norm', host(got), want)
+
+
+def test_layer_norm_in_place_and_empty(cuda_device):
+    g = Gen(8, 'bf16')
+    x = g.h(1000, 128, s=3.)
+    sc, off = g.f(128, s=.1, mean=1.), g.f(128, s=.1)
+    want = of.layer_norm_one_pass(x, sc, off, 1e-5, 'bf16')
+    t = dev16(x, 'bf16', cuda_device)
+    out = b200().volta_layer_norm(t, dev32(sc, cuda_device), dev32(off, cuda_device), eps=1e-5,
+                                  out=t)
+    assert out.data_ptr() == t.data_ptr()
+    close('layer_norm in place', host(t), want)
+    e = torch.empty(0, 128, dtype=torch.bfloat16, device=cuda_device)
+    assert b200().volta_layer_norm(e, dev32(sc, cuda_device), dev32(off, cuda_device),
+                                   eps=1e-5).shape == (0, 128)
+    with pytest.raises(ValueError, match=r'x must be \[M,C\]'):
+        b200().volta_layer_norm(t.view(10, 100, 128), dev32(sc, cuda_device),
+                                dev32(off, cuda_device), eps=1e-5)
+
+
 # ---- ln_gated_dual_proj ---------------------------------------------------------------------
 
 def ln_gdp_case(K, CI, M, dt, d, mask=None, seed=0):

@@ -85,6 +85,21 @@ def test_layer_norm_two_pass():
     np.testing.assert_allclose(y.std(-1), 1, atol=1e-3)
 
 
+def test_layer_norm_one_pass():
+    """VoltaLayerNorm's one-pass statistics: close to a float64 LayerNorm for centred rows, the
+    variance clamped at zero (a constant row gives offset, not NaN)."""
+    rng = np.random.default_rng(3)
+    x = round_to(rng.standard_normal((9, 96)) * 2, 'f16')
+    sc, off = rng.standard_normal(96) * 0.1 + 1, rng.standard_normal(96) * 0.1
+    y = of.layer_norm_one_pass(x, sc, off, 1e-5, 'f32')
+    m, v = x.mean(-1, keepdims=True), x.var(-1, keepdims=True)
+    want = (x - m) / np.sqrt(v + 1e-5) * sc + off
+    np.testing.assert_allclose(y, want, atol=1e-4)
+    const = np.full((2, 32), 3.0)
+    y = of.layer_norm_one_pass(const, np.ones(32), np.full(32, 0.25), 1e-5, 'f16')
+    np.testing.assert_array_equal(y, np.full((2, 32), 0.25))
+
+
 def test_tile_work():
     keep = np.array([1, 0, -1, -1, 0, 0, -1, -1, -1, -1], np.float32)
     assert of.tile_work(keep, 10, 2, -1.0) == ['compute', 'skip', 'padding', 'skip', 'skip']

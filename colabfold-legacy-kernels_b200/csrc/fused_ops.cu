@@ -1850,6 +1850,27 @@ cudaError_t transition_typed(cudaStream_t stream, int dtype, const void* x, cons
     return cudaGetLastError();
 }
 
+// blocks of 256 threads the GPU holds at once (a persistent grid of one wave)
+long long one_wave(const void* kern) {
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, 0) != cudaSuccess ||
+        per_sm < 1) {
+        per_sm = 1;
+    }
+    return (long long)sm_count() * per_sm;
+}
+
+template <typename T, int G>
+cudaError_t layer_norm_vec_launch(cudaStream_t stream, const T* x, const float* scale,
+                                  const float* offset, T* out, long long M, float eps) {
+    auto kern = layer_norm_vec_kernel<T, G>;
+    const long long rows_per_block = 8LL * (32 / G) * kLnRows;  // 8 warps a block
+    const long long blocks =
+        std::min(one_wave((const void*)kern), (M + rows_per_block - 1) / rows_per_block);
+    kern<<<(unsigned)blocks, 256, 0, stream>>>(x, scale, offset, out, M, eps);
+    return cudaGetLastError();
+}
+
 template <typename T>
 cudaError_t layer_norm_typed(cudaStream_t stream, const void* x, const float* scale,
                              const float* offset, void* out, long long M, int C, float eps) {
@@ -1859,22 +1880,19 @@ cudaError_t layer_norm_typed(cudaStream_t stream, const void* x, const float* sc
                      ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out) |
                        reinterpret_cast<uintptr_t>(scale) | reinterpret_cast<uintptr_t>(offset)) &
                       15) == 0;
-    // persistent grid: 8 blocks of 256 threads an SM at most
-    const long long cap = (long long)sm_count() * 8;
     if (vec) {
-        const int G = C / 8;
-        const long long rows_per_block = 8LL * (32 / G) * kLnRows;  // 8 warps a block
-        const long long blocks = std::min(cap, (M + rows_per_block - 1) / rows_per_block);
-        switch (G) {
-#define CFLK_LN(GG)                                                                                case GG:                                                                                           layer_norm_vec_kernel<T, GG><<<(unsigned)blocks, 256, 0, stream>>>(xp, scale, offset,                                                                              op, M, eps);               break;
-            CFLK_LN(1) CFLK_LN(2) CFLK_LN(4) CFLK_LN(8) CFLK_LN(16) CFLK_LN(32)
-#undef CFLK_LN
+        switch (C / 8) {
+        case 1: return layer_norm_vec_launch<T, 1>(stream, xp, scale, offset, op, M, eps);
+        case 2: return layer_norm_vec_launch<T, 2>(stream, xp, scale, offset, op, M, eps);
+        case 4: return layer_norm_vec_launch<T, 4>(stream, xp, scale, offset, op, M, eps);
+        case 8: return layer_norm_vec_launch<T, 8>(stream, xp, scale, offset, op, M, eps);
+        case 16: return layer_norm_vec_launch<T, 16>(stream, xp, scale, offset, op, M, eps);
+        default: return layer_norm_vec_launch<T, 32>(stream, xp, scale, offset, op, M, eps);
         }
-    } else {
-        const long long blocks = std::min(cap, (M + 7) / 8);
-        layer_norm_row_kernel<T><<<(unsigned)blocks, 256, 0, stream>>>(xp, scale, offset, op, M,
-                                                                        C, eps);
     }
+    auto kern = layer_norm_row_kernel<T>;
+    const long long blocks = std::min(one_wave((const void*)kern), (M + 7) / 8);
+    kern<<<(unsigned)blocks, 256, 0, stream>>>(xp, scale, offset, op, M, C, eps);
     return cudaGetLastError();
 }
 

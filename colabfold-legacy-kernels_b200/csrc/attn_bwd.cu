@@ -516,7 +516,8 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
         // over the chunk's own S^T/dP^T columns), dS (shared), dBias
         const auto half_step = [&](auto fast, const uint8_t* brow, const float* lsh,
                                    const float* dlh, int q0, int jn, int key) {
-            float* drow = dbias_col + (long long)(q0 + 32 * hf) * p.Sk;
+            // this half's first dBias row (the per-element reduction mode only)
+            [[maybe_unused]] float* drow = dbias_col + (long long)(q0 + 32 * hf) * p.Sk;
 #pragma unroll
             for (int cc = 0; cc < 2; ++cc) {
                 uint32_t sr[16], dr[16];

@@ -30,6 +30,31 @@ def test_library_exports_every_declared_symbol():
     assert not missing
 
 
+def test_every_cc100_target_has_a_declared_entry_point_and_binding():
+    """Each cc=100 FFI target maps to a C entry point that include/*.h declares, and the torch
+    binding carries its prototype."""
+    from colabfold_legacy_kernels import b200
+    names = set(ge.declared_symbols())
+    for k in clk.KERNELS:
+        if not clk.available(100, k):
+            continue
+        sym = clk.c_symbol(k, 100)
+        assert sym in names, (k, sym)
+        assert sym in b200._SIGS, (k, sym)
+
+
+def test_layer_norm_refuses_bad_shapes_without_gpu():
+    l = lib()
+    l.cflk_last_error.restype = ctypes.c_char_p
+    f = l.cflk_volta_layer_norm
+    f.argtypes = [ctypes.c_void_p, ctypes.c_int] + [ctypes.c_void_p] * 4 + [
+        ctypes.c_int64, ctypes.c_int64, ctypes.c_float]
+    assert f(None, 0, None, None, None, None, -1, 128, 1e-5) == 1
+    assert b'[M,C]' in l.cflk_last_error()
+    assert f(None, 5, None, None, None, None, 4, 128, 1e-5) == 1
+    assert f(None, 0, None, None, None, None, 0, 128, 1e-5) == 0  # M = 0: nothing to do
+
+
 def test_version_and_error_reporting_without_gpu():
     l = lib()
     l.cflk_last_error.restype = ctypes.c_char_p

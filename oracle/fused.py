@@ -12,6 +12,8 @@ the reference's handler contracts and kernels instead:
 
   * VoltaLayerNorm (the standalone op): one-pass float32 sum and sum of squares, the variance
     clamped at zero (cuda/volta_ops.cu:27-60).
+  * VoltaGdp (no cc=100 kernel yet): mask * (x wp + bp) * sigmoid or swish (x wg + bg), the
+    row mask unclamped (cuda/volta_ops.cu:108-205, cuda/volta_gdp.h:10-19).
   * LayerNorm: two-pass float32 statistics, eps inside the rsqrt, result rounded to the 16-bit
     compute type before the GEMM (ln_rows, cuda/volta_gdp.h:208-240; ln_columns over the
     channel-major float32 x_cm, :244-286).
@@ -67,6 +69,23 @@ def layer_norm_one_pass(x, scale, offset, eps, dtype):
 
 def sigmoid(g):
     return 1.0 / (1.0 + np.exp(-g))
+
+
+def gdp(x, wp, bp, wg, bg, mask, activation, dtype):
+    """VoltaGdp, the unfused gated dual projection (cuda/volta_ops.cu:108-205, its activation
+    cuda/volta_gdp.h:10-19): out [M, N] = mask[m] * (x wp + bp) * act(x wg + bg), wp and wg
+    [K, N] row-major, the row mask as given (not clamped), act = sigmoid (activation 0) or
+    swish g * sigmoid(g) (activation 1); products accumulated in float32, the result rounded to
+    `dtype`; float64 out. No cc=100 kernel yet: the oracle for the next row."""
+    if activation not in (0, 1):
+        raise ValueError('gdp: activation is 0 (sigmoid) or 1 (swish), got %r' % (activation,))
+    x32 = np.asarray(x, np.float32)
+    p = x32 @ np.asarray(wp, np.float32) + np.asarray(bp, np.float32)
+    g = x32 @ np.asarray(wg, np.float32) + np.asarray(bg, np.float32)
+    s = sigmoid(g.astype(np.float64))
+    act = s if activation == 0 else g * s
+    out = np.asarray(mask, np.float64)[:, None] * p * act
+    return round_to(out, dtype)
 
 
 def tile_work(keep, M, tile, other):

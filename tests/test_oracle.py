@@ -100,6 +100,23 @@ def test_layer_norm_one_pass():
     np.testing.assert_array_equal(y, np.full((2, 32), 0.25))
 
 
+def test_gdp_activations():
+    """VoltaGdp's restatement: sigmoid and swish gates, the row mask applied unclamped."""
+    rng = np.random.default_rng(4)
+    M, K, N = 5, 16, 8
+    x = round_to(rng.standard_normal((M, K)), 'f16')
+    wp, wg = rng.standard_normal((K, N)) * 0.3, rng.standard_normal((K, N)) * 0.3
+    bp, bg = rng.standard_normal(N) * 0.1, rng.standard_normal(N) * 0.1
+    mask = np.array([1.0, 0.0, -1.0, 0.5, 2.0])
+    p, g = x @ wp + bp, x @ wg + bg
+    s = 1 / (1 + np.exp(-g))
+    for act, gate in ((0, s), (1, g * s)):
+        got = of.gdp(x, wp, bp, wg, bg, mask, act, 'f32')
+        np.testing.assert_allclose(got, mask[:, None] * p * gate, rtol=1e-5, atol=1e-6)
+    with pytest.raises(ValueError, match='activation'):
+        of.gdp(x, wp, bp, wg, bg, mask, 2, 'f16')
+
+
 def test_tile_work():
     keep = np.array([1, 0, -1, -1, 0, 0, -1, -1, -1, -1], np.float32)
     assert of.tile_work(keep, 10, 2, -1.0) == ['compute', 'skip', 'padding', 'skip', 'skip']

@@ -470,6 +470,117 @@ struct LnGdpOp {
 };
 
 // ---------------------------------------------------------------------------------------------
+// VoltaGdp: out [M, N] = mask * (x wp + bp) * act(x wg + bg), act = sigmoid or swish
+// g sigmoid(g), the row mask as given (cuda/volta_ops.cu:108-205; cuda/volta_gdp.h:10-19). wp and
+// wg are [K, N] row-major, so they are the MMA's B operand N-major: each 64-column atom holds K
+// rows of 128 bytes. Warpgroups ping-pong over tiles; a block is the whole N of both products.
+// ---------------------------------------------------------------------------------------------
+template <typename T_, int K>
+struct GdpOp {
+    using T = T_;
+    using E = Elem<T>;
+    static constexpr int kSlots = 2, kSlotCols = 256;
+    static constexpr bool kPingPong = true;
+    static constexpr int kStages = 2;
+    static constexpr int X_BYTES = K * BM * 2;
+    static constexpr float kOther = 0.f;
+    static constexpr int RED_FLOATS = 4;  // unused
+    using Stager = RowChunkStager<2>;
+    static constexpr int STORE_BYTES = (kWorkers / 32) * Stager::BYTES;
+    struct Args {
+        const T *x, *wp, *bp, *wg, *bg, *mask;
+        T* out;
+        int M, N, act;  // act: 0 sigmoid, 1 swish
+        int w_bytes, param_floats;
+        float eps;  // unused
+    };
+    struct Regs {
+        float mv;  // this worker's row of the mask
+        Stager st;
+    };
+    static __device__ void bind(Regs& r, uint8_t* stb, int warp) {
+        r.st.base = smem_u32(stb) + warp * Stager::BYTES;
+        r.st.n = 0;
+    }
+    static __device__ void finish(Regs& r, int lane) { r.st.finish(lane); }
+    static __device__ void row_keep(Regs&, float) {}
+    static __device__ const T* keep(const Args&) { return nullptr; }
+    // bp [N], bg [N]
+    static __device__ void load_params(const Args& a, float* sp, uint8_t*, int tid) {
+        for (int i = tid; i < a.N; i += kWorkers) {
+            sp[i] = E::to_f(a.bp[i]);
+            sp[a.N + i] = E::to_f(a.bg[i]);
+        }
+    }
+    // wp then wg, each N/64 atoms of [K rows][64 columns] (box {64, K})
+    static __device__ void load_weights(const Args& a, const CUtensorMap* tw0,
+                                        const CUtensorMap* tw1, uint8_t* ws, uint64_t* bar) {
+        mbar_arrive_expect_tx(bar, (uint32_t)(2 * K * a.N * 2));
+        for (int at = 0; at < a.N / 64; ++at) {
+            tma_load_2d(ws + at * K * 128, tw0, bar, at * 64, 0);
+            tma_load_2d(ws + K * a.N * 2 + at * K * 128, tw1, bar, at * 64, 0);
+        }
+    }
+    static __device__ void load_x(const Args& a, const CUtensorMap* tx, const CUtensorMap*,
+                                  uint8_t* dst, uint64_t* bar, int m0) {
+        load_rows_tile(tx, dst, bar, K, m0);
+    }
+    static __device__ int nblocks(const Args&) { return 1; }
+    // x wp into the slot's columns [0, N), x wg into [N, 2N)
+    static __device__ void issue_block(const Args& a, uint32_t xa, uint32_t wa, uint32_t acc,
+                                       int) {
+        const uint32_t id = idesc_f16(E::kBf16, 128, a.N, false, true);
+        const uint32_t wg = wa + K * a.N * 2;
+        for (int k = 0; k < K / 16; ++k) {
+            const uint64_t ad = desc_k128(xa + (k >> 2) * ATOM + (k & 3) * 32);
+            // N-major B: K steps 16 rows (2 KB) apart, 8-row groups 1024 bytes apart, the next
+            // 64 columns one atom (K rows of 128 bytes) on
+            mma_ss(acc, ad, smem_desc(wa + k * 16 * 128, K * 128, 1024, kSwizzle128B), id,
+                   k > 0 ? 1u : 0u);
+            mma_ss(acc + a.N, ad, smem_desc(wg + k * 16 * 128, K * 128, 1024, kSwizzle128B), id,
+                   k > 0 ? 1u : 0u);
+        }
+    }
+    static __device__ void prologue(const Args& a, uint8_t*, const float*, float*, int t, int,
+                                    int m0, Regs& regs) {
+        const int m = m0 + t;
+        regs.mv = m < a.M ? E::to_f(a.mask[m]) : 0.f;
+    }
+    static __device__ void prefetch_block(const Args&, int, int, int, int, Regs&) {}
+    // worker t: row t, 32 columns a TMEM wait and a store
+    static __device__ void epilogue_block(const Args& a, uint32_t acc, const float* sp, int t,
+                                          int, int m0, int, Regs& regs, const CUtensorMap* to,
+                                          const CUtensorMap*) {
+        const int lane = t & 31, row0 = m0 + (t & ~31);
+        for (int c0 = 0; c0 < a.N; c0 += 32) {
+            uint32_t rp[32], rg[32];
+            tmem_ld32(acc + c0, rp);
+            tmem_ld32(acc + a.N + c0, rg);
+            tmem_wait_ld();
+            if (row0 >= a.M) {
+                continue;
+            }
+            uint32_t w[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+                float o[2];
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int c = c0 + 2 * e + h;
+                    const float pv = __uint_as_float(rp[2 * e + h]) + sp[c];
+                    const float gv = __uint_as_float(rg[2 * e + h]) + sp[a.N + c];
+                    const float sg = sigmoid_fast(gv);
+                    o[h] = regs.mv * pv * (a.act ? gv * sg : sg);
+                }
+                w[e] = E::pack(o[0], o[1]);
+            }
+            regs.st.put(to, lane, w, c0, row0);
+        }
+    }
+    static __device__ void padding(const Args&, int, int, int) {}
+};
+
+// ---------------------------------------------------------------------------------------------
 // VoltaLnProj (LN = true): p [M, n] = LN(x) w, bias [heads, M] = (LN(x) wb)^T
 // VoltaOutProj (LN = false): out [M, n] = o w + b (+ residual)
 // One launch covers output columns [0, n) of a pass, n <= 512, p's row stride ldp.
@@ -1676,6 +1787,46 @@ cudaError_t ln_gdp_typed(cudaStream_t stream, int dtype, const void* x, const fl
     return launch_op<Op>(stream, tx, tw0, tw1, to0, to1, a);
 }
 
+template <typename T, int K>
+cudaError_t gdp_typed(cudaStream_t stream, int dtype, const void* x, const void* wp,
+                      const void* bp, const void* wg, const void* bg, const void* mask,
+                      void* out, int M, int N, int act) {
+    using Op = GdpOp<T, K>;
+    CUtensorMap tx, twp, twg, to;
+    // weights [K, N] row-major: boxes of 64 columns x K rows (128-byte swizzle)
+    const uint64_t wdims[2] = {(uint64_t)N, (uint64_t)K};
+    const uint64_t wstrides[1] = {(uint64_t)N};
+    const uint32_t wbox[2] = {64, (uint32_t)K};
+    // the output in boxes of 32 columns x 32 rows (64-byte swizzle)
+    const uint64_t odims[2] = {(uint64_t)N, (uint64_t)M};
+    const uint64_t ostrides[1] = {(uint64_t)N};
+    const uint32_t obox[2] = {32, 32};
+    if (!map_rows(&tx, dtype, x, M, K, K, BM) ||
+        !encode_tiled(&twp, tdt(dtype), 2, 2, wp, wdims, wstrides, wbox,
+                      CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_tiled(&twg, tdt(dtype), 2, 2, wg, wdims, wstrides, wbox,
+                      CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_tiled(&to, tdt(dtype), 2, 2, out, odims, ostrides, obox,
+                      CU_TENSOR_MAP_SWIZZLE_64B)) {
+        return cudaErrorInvalidValue;
+    }
+    typename Op::Args a;
+    a.x = static_cast<const T*>(x);
+    a.wp = static_cast<const T*>(wp);
+    a.bp = static_cast<const T*>(bp);
+    a.wg = static_cast<const T*>(wg);
+    a.bg = static_cast<const T*>(bg);
+    a.mask = static_cast<const T*>(mask);
+    a.out = static_cast<T*>(out);
+    a.M = M;
+    a.N = N;
+    a.act = act;
+    a.w_bytes = 2 * K * N * 2;
+    a.param_floats = 2 * N;
+    a.eps = 0.f;
+    return launch_op<Op>(stream, tx, twp, twg, to, to, a);
+}
+
 template <typename T, int K, bool LN>
 cudaError_t proj_typed(cudaStream_t stream, int dtype, const void* x, const float* scale,
                        const float* offset, const void* wT, const void* b, const void* residual,
@@ -2120,4 +2271,47 @@ extern "C" int cflk_volta_layer_norm(void* stream, int dtype, const void* x, con
             ? layer_norm_typed<__nv_bfloat16>(s, x, scale, offset, out, M, (int)C, eps)
             : layer_norm_typed<__half>(s, x, scale, offset, out, M, (int)C, eps);
     return launch_status(e, "layer_norm");
+}
+
+extern "C" int cflk_volta_gdp(void* stream, int dtype, const void* x, const void* wp,
+                              const void* bp, const void* wg, const void* bg, const void* mask,
+                              void* out, int64_t M, int64_t K, int64_t N, int64_t activation) {
+    clear_error();
+    if (dtype != kF16 && dtype != kBF16) {
+        return fail(kInvalidArgument, "gdp: dtype must be f16 or bf16");
+    }
+    if (activation != 0 && activation != 1) {
+        return fail(kInvalidArgument, "gdp: activation is 0 (sigmoid) or 1 (swish), got " +
+                                          std::to_string(activation));
+    }
+    if (M < 0 || K < 1 || N < 1) {
+        return fail(kInvalidArgument, "x must be [M,K]");
+    }
+    if (N % 8) {
+        return fail(kInvalidArgument, "gdp: N must be a multiple of 8");
+    }
+    if ((K != 64 && K != 128) || (N != 64 && N != 128)) {
+        return fail(kInvalidArgument, "gdp: this library takes K and N of 64 or 128");
+    }
+    if (M == 0) {
+        return kOk;
+    }
+    if (!aligned16(x) || !aligned16(wp) || !aligned16(wg) || !aligned16(out) || bp == nullptr ||
+        bg == nullptr || mask == nullptr) {
+        return fail(kInvalidArgument, "gdp: buffers must be 16-byte aligned");
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e;
+    if (dtype == kBF16) {
+        e = K == 64 ? gdp_typed<__nv_bfloat16, 64>(s, dtype, x, wp, bp, wg, bg, mask, out, (int)M,
+                                                   (int)N, (int)activation)
+                    : gdp_typed<__nv_bfloat16, 128>(s, dtype, x, wp, bp, wg, bg, mask, out,
+                                                    (int)M, (int)N, (int)activation);
+    } else {
+        e = K == 64 ? gdp_typed<__half, 64>(s, dtype, x, wp, bp, wg, bg, mask, out, (int)M,
+                                            (int)N, (int)activation)
+                    : gdp_typed<__half, 128>(s, dtype, x, wp, bp, wg, bg, mask, out, (int)M,
+                                             (int)N, (int)activation);
+    }
+    return launch_status(e, "gdp");
 }

@@ -51,6 +51,7 @@ _TABLE = {
         (70, "libvolta_ops.so", "VoltaLayerNorm"),
     ),
     "gated_dual_proj": (
+        (100, _SM100_LIB, "VoltaGdp"),
         (75, "libvolta_ops.so", "VoltaGdp"),
         (70, "libvolta_gdp_wmma.so", "VoltaGdpWmma"),
     ),
@@ -99,6 +100,7 @@ _C_SYMBOLS = {
     "VoltaOutProj": "cflk_volta_out_proj",
     "VoltaTransition": "cflk_volta_transition",
     "VoltaLayerNorm": "cflk_volta_layer_norm",
+    "VoltaGdp": "cflk_volta_gdp",
 }
 
 KERNELS = tuple(_TABLE)

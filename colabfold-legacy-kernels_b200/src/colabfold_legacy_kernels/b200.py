@@ -39,6 +39,7 @@ _SIGS = {
     'cflk_volta_transition': [_p, _int, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64,
                               _f32, _int],
     'cflk_volta_layer_norm': [_p, _int, _p, _p, _p, _p, _i64, _i64, _f32],
+    'cflk_volta_gdp': [_p, _int, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64],
 }
 
 _lib = None
@@ -186,6 +187,29 @@ def volta_mma_bwd(q, k, v, bias, kmask, out, dout, lse, *, scale, want_dbias=Tru
 
 
 # ---- fused pair-stack ops -------------------------------------------------------------------
+
+def volta_gdp(x, wp, bp, wg, bg, mask, *, activation=0, out=None):
+    """VoltaGdp: out [M,N] = mask * (x wp + bp) * act(x wg + bg); wp, wg [K,N]; activation 0
+    (sigmoid) or 1 (swish)."""
+    who = 'gdp'
+    if x.dim() != 2:
+        raise ValueError('x must be [M,K]')
+    M, K = x.shape
+    if wp.dim() != 2 or wp.shape[0] != K or wg.shape != wp.shape:
+        raise ValueError('gdp: wp and wg must be [K,N]')
+    N = wp.shape[1]
+    if bp.numel() != N or bg.numel() != N or mask.numel() != M:
+        raise ValueError('gdp: shapes do not match')
+    dt = _dtype_code(x, wp, bp, wg, bg, mask)
+    if out is None:
+        out = torch.empty((M, N), dtype=x.dtype, device=x.device)
+    if M == 0:
+        return out
+    rc = lib().cflk_volta_gdp(_stream(), dt, _ptr(x), _ptr(wp), _ptr(bp), _ptr(wg), _ptr(bg),
+                              _ptr(mask), _ptr(out), M, K, N, int(activation))
+    _check(rc, who)
+    return out
+
 
 def volta_layer_norm(x, scale, offset, *, eps, out=None):
     """VoltaLayerNorm: out [M,C] (one-pass float32 statistics). `out` may be given (and may be

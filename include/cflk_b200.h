@@ -171,6 +171,14 @@ CFLK_API int cflk_volta_layer_norm(void* stream, int dtype, const void* x, const
                                    const float* offset, void* out, int64_t M, int64_t C,
                                    float eps);
 
+/* VoltaGdp: out [M,N] = mask * (x wp + bp) * act(x wg + bg), act = sigmoid (activation 0) or
+ * swish g * sigmoid(g) (1), the row mask unclamped. x [M,K]; wp, wg [K,N] row-major; bp, bg
+ * [N]; mask [M]. This library takes K and N of 64 or 128 (the reference: any K, N % 8 == 0).
+ * Replaces VoltaGdp, cuda/volta_ops.cu:108-205,212-265. */
+CFLK_API int cflk_volta_gdp(void* stream, int dtype, const void* x, const void* wp,
+                            const void* bp, const void* wg, const void* bg, const void* mask,
+                            void* out, int64_t M, int64_t K, int64_t N, int64_t activation);
+
 #ifdef __cplusplus
 }
 #endif

@@ -95,7 +95,8 @@ def test_workspace_size():
 def test_resolver_capabilities():
     assert clk.supported_capabilities() == (70, 75, 100)
     for k in ('attention', 'attention_bwd', 'ln_gated_dual_proj', 'trimul_epilogue',
-              'ln_projection', 'output_projection', 'transition', 'layer_norm'):
+              'ln_projection', 'output_projection', 'transition', 'layer_norm',
+              'gated_dual_proj'):
         assert clk.available(100, k)
         assert clk.library_path(k, 100).endswith('sm100/libcflk_sm100.so')
     assert clk.symbol('attention', 100) == 'VoltaMma'
@@ -112,8 +113,9 @@ def test_resolver_capabilities():
     assert not clk.available(80)
     assert clk.symbol('layer_norm', 100) == 'VoltaLayerNorm'
     assert clk.c_symbol('layer_norm', 100) == 'cflk_volta_layer_norm'
+    assert clk.symbol('gated_dual_proj', 100) == 'VoltaGdp'
     with pytest.raises(FileNotFoundError):
-        clk.symbol('gated_dual_proj', 100)
+        clk.symbol('opm_update', 100)
     with pytest.raises(KeyError):
         clk.library_path('nonexistent', 100)
     assert clk.kernel_dir(100).endswith('sm100')

@@ -92,6 +92,42 @@ def test_layer_norm_in_place_and_empty(cuda_device):
                                 dev32(off, cuda_device), eps=1e-5)
 
 
+# ---- gated_dual_proj (VoltaGdp) ---------------------------------------------------------------
+
+@pytest.mark.parametrize('act', [0, 1])
+@pytest.mark.parametrize('dt', ['bf16', 'f16'])
+@pytest.mark.parametrize('M', ROWS)
+@pytest.mark.parametrize('K,N', [(128, 128), (64, 64), (128, 64), (64, 128)])
+def test_gdp(K, N, M, dt, act, cuda_device):
+    """The unfused gated dual projection against its oracle, sigmoid and swish gates, a row
+    mask with zeros, negatives and fractions (applied unclamped)."""
+    g = Gen(11, dt)
+    x = g.h(M, K, s=1.)
+    wp, wg = g.h(K, N, s=.1), g.h(K, N, s=.1)
+    bp, bg = g.h(N, s=.1), g.h(N, s=.1)
+    mask = round_to(np.resize(np.array([1.0, 0.0, -1.0, 0.5, 2.0]), M), dt)
+    want = of.gdp(x, wp, bp, wg, bg, mask, act, dt)
+    d = cuda_device
+    got = b200().volta_gdp(dev16(x, dt, d), dev16(wp, dt, d), dev16(bp, dt, d), dev16(wg, dt, d),
+                           dev16(bg, dt, d), dev16(mask, dt, d), activation=act)
+    assert b200().device_status() == 0
+    close('gdp', host(got), want)
+
+
+def test_gdp_refusals(cuda_device):
+    d = cuda_device
+    x = torch.zeros(10, 128, dtype=torch.bfloat16, device=d)
+    w = torch.zeros(128, 128, dtype=torch.bfloat16, device=d)
+    b = torch.zeros(128, dtype=torch.bfloat16, device=d)
+    m = torch.ones(10, dtype=torch.bfloat16, device=d)
+    with pytest.raises(ValueError, match='activation is 0'):
+        b200().volta_gdp(x, w, b, w, b, m, activation=2)
+    w3 = torch.zeros(128, 96, dtype=torch.bfloat16, device=d)
+    b3 = torch.zeros(96, dtype=torch.bfloat16, device=d)
+    with pytest.raises(ValueError, match='K and N of 64 or 128'):
+        b200().volta_gdp(x, w3, b3, w3, b3, m)
+
+
 # ---- ln_gated_dual_proj ---------------------------------------------------------------------
 
 def ln_gdp_case(K, CI, M, dt, d, mask=None, seed=0):

@@ -416,6 +416,12 @@ def bench_fusions(torch, b200, dev, rank, world, steps, warmup, flush, pk, only=
                 lambda: b200.volta_out_proj(o, woT, bo, res, keep1, has_residual=True,
                                             has_keep=False),
                 M * C_Z * 2 * 3, 2.0 * M * C_Z * C_Z))
+    gwp, gwg = rn(C_Z, C_Z, s=w), rn(C_Z, C_Z, s=w)
+    gbp, gbg = rn(C_Z, s=0.1), rn(C_Z, s=0.1)
+    g_out = torch.empty_like(x)
+    ops.append(('gated_dual_proj K=N=128 sigmoid',
+                lambda: b200.volta_gdp(x, gwp, gbp, gwg, gbg, mask, activation=0, out=g_out),
+                M * (C_Z * 2 + C_Z * 2 + 2) + 2 * C_Z * C_Z * 2, 2.0 * M * C_Z * C_Z * 2))
     ln_out = torch.empty_like(x)
     ops.append(('layer_norm C=128',
                 lambda: b200.volta_layer_norm(x, ones, zeros, eps=1e-5, out=ln_out),

@@ -12,8 +12,11 @@ the reference's handler contracts and kernels instead:
 
   * VoltaLayerNorm (the standalone op): one-pass float32 sum and sum of squares, the variance
     clamped at zero (cuda/volta_ops.cu:27-60).
-  * VoltaGdp (no cc=100 kernel yet): mask * (x wp + bp) * sigmoid or swish (x wg + bg), the
-    row mask unclamped (cuda/volta_ops.cu:108-205, cuda/volta_gdp.h:10-19).
+  * VoltaGdp: mask * (x wp + bp) * sigmoid or swish (x wg + bg), the row mask unclamped
+    (cuda/volta_ops.cu:108-205, cuda/volta_gdp.h:10-19).
+  * VoltaOpmUpdate / VoltaOpmOuter (no cc=100 kernels yet): the outer-product-mean update and
+    the 16-row outer product with its inner product rounded to 16 bits
+    (cuda/volta_fused_ffi.h:261-335, cuda/volta_ops.cu:647-787).
   * LayerNorm: two-pass float32 statistics, eps inside the rsqrt, result rounded to the 16-bit
     compute type before the GEMM (ln_rows, cuda/volta_gdp.h:208-240; ln_columns over the
     channel-major float32 x_cm, :244-286).
@@ -71,12 +74,43 @@ def sigmoid(g):
     return 1.0 / (1.0 + np.exp(-g))
 
 
+def opm_update(lhs, t, bias, norm, residual, eps, dtype):
+    """VoltaOpmUpdate (cuda/volta_fused_ffi.h:261-298, kernel cuda/volta_ops.cu:647-699):
+    out [B, D, F] = (lhs @ t[:, d, :] + bias) / (eps + norm[b, d]) (+ residual), lhs [B, K],
+    t [K, D, F], bias [F] and norm [B, D] float32; products in float32, the result rounded to
+    `dtype`; float64 out. No cc=100 kernel yet: the oracle for the next row."""
+    l32 = np.asarray(lhs, np.float32)
+    t32 = np.asarray(t, np.float32)
+    prod = np.einsum('bk,kdf->bdf', l32, t32).astype(np.float32)
+    den = np.float32(eps) + np.asarray(norm, np.float32)[:, :, None]
+    out = (prod + np.asarray(bias, np.float32)) / den
+    if residual is not None:
+        out = out + np.asarray(residual, np.float32)
+    return round_to(out.astype(np.float64), dtype)
+
+
+def opm_outer(left, right, wT, dtype):
+    """VoltaOpmOuter (cuda/volta_fused_ffi.h:300-335, kernel cuda/volta_ops.cu:710-787): on 16
+    MSA rows a, out [B, D, F] = sum over c, e of h(sum_a left[a, b, c] right[a, d, e]) w[c E + e, f]
+    with h the rounding of the float32 inner product to the 16-bit type (the kernel rounds it in
+    registers before the second product), left [16, B, C], right [16, D, E], wT [F, C E];
+    accumulated in float32, the result rounded to `dtype`; float64 out."""
+    l32 = np.asarray(left, np.float32)
+    r32 = np.asarray(right, np.float32)
+    g = np.einsum('abc,ade->bdce', l32, r32).astype(np.float32)
+    g = round_to(g, dtype).astype(np.float32)
+    B, D, C, E = g.shape
+    w = np.asarray(wT, np.float32).T  # [C E, F]
+    out = g.reshape(B, D, C * E) @ w
+    return round_to(out.astype(np.float64), dtype)
+
+
 def gdp(x, wp, bp, wg, bg, mask, activation, dtype):
     """VoltaGdp, the unfused gated dual projection (cuda/volta_ops.cu:108-205, its activation
     cuda/volta_gdp.h:10-19): out [M, N] = mask[m] * (x wp + bp) * act(x wg + bg), wp and wg
     [K, N] row-major, the row mask as given (not clamped), act = sigmoid (activation 0) or
     swish g * sigmoid(g) (activation 1); products accumulated in float32, the result rounded to
-    `dtype`; float64 out. No cc=100 kernel yet: the oracle for the next row."""
+    `dtype`; float64 out."""
     if activation not in (0, 1):
         raise ValueError('gdp: activation is 0 (sigmoid) or 1 (swish), got %r' % (activation,))
     x32 = np.asarray(x, np.float32)

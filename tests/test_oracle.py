@@ -117,6 +117,33 @@ def test_gdp_activations():
         of.gdp(x, wp, bp, wg, bg, mask, 2, 'f16')
 
 
+def test_opm_update_and_outer():
+    """The outer-product-mean restatements against plain float64 loops on small shapes."""
+    rng = np.random.default_rng(5)
+    B, K, D, F = 3, 32, 2, 16
+    lhs = round_to(rng.standard_normal((B, K)), 'f16')
+    t = round_to(rng.standard_normal((K, D, F)) * 0.2, 'f16')
+    bias, norm = rng.standard_normal(F), np.abs(rng.standard_normal((B, D))) + 1
+    res = round_to(rng.standard_normal((B, D, F)), 'f16')
+    want = np.zeros((B, D, F))
+    for b in range(B):
+        for d in range(D):
+            want[b, d] = (lhs[b] @ t[:, d, :] + bias) / (1e-3 + norm[b, d]) + res[b, d]
+    got = of.opm_update(lhs, t, bias, norm, res, 1e-3, 'f32')
+    np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-4)
+    C, E = 2, 32
+    left = round_to(rng.standard_normal((16, B, C)), 'f16')
+    right = round_to(rng.standard_normal((16, D, E)), 'f16')
+    wT = round_to(rng.standard_normal((F, C * E)) * 0.1, 'f16')
+    want = np.zeros((B, D, F))
+    for b in range(B):
+        for d in range(D):
+            g = np.einsum('ac,ae->ce', left[:, b, :], right[:, d, :]).reshape(C * E)
+            want[b, d] = g @ wT.T
+    got = of.opm_outer(left, right, wT, 'f32')
+    np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-3)
+
+
 def test_tile_work():
     keep = np.array([1, 0, -1, -1, 0, 0, -1, -1, -1, -1], np.float32)
     assert of.tile_work(keep, 10, 2, -1.0) == ['compute', 'skip', 'padding', 'skip', 'skip']

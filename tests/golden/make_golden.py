@@ -1,8 +1,8 @@
 """Generate the golden attention fixtures by running the reference's own oracle code.
 
-  python tests/golden/make_golden.py [REFERENCE_ROOT]
+  python tests/golden/make_golden.py REFERENCE_ROOT
 
-REFERENCE_ROOT is a checkout of colabfold-legacy-kernels (default /root/reference). Its test
+REFERENCE_ROOT is a checkout of colabfold-legacy-kernels (or set CFLK_REFERENCE_ROOT). Its test
 files import jax, which this environment does not have, so the script does not import them:
 it parses each file, takes the functions named below out of its syntax tree and executes them
 against numpy, with a small numpy stand-in for the few jax.numpy / jax.nn calls they make.
@@ -135,4 +135,7 @@ def main(ref_root):
 
 
 if __name__ == '__main__':
-    main(sys.argv[1] if len(sys.argv) > 1 else '/root/reference')
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get('CFLK_REFERENCE_ROOT')
+    if not root:
+        sys.exit('usage: make_golden.py REFERENCE_ROOT (a colabfold-legacy-kernels checkout)')
+    main(root)

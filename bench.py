@@ -57,19 +57,95 @@ def attn_flops(n, h=HEADS, s=N_RES, d=HEAD_DIM):
 
 
 # ------------------------------------------------------------------------------------------
-# CPU: the reference's arithmetic (float32 port of its closed form), all host cores
+# CPU: the reference's arithmetic (float32 port of its closed form, and the fusion oracle), on
+# all host cores: a spawn pool of one single-threaded process per core, each given a share of a
+# bounded sample of batch rows (rows are independent, so the sample scales by rows)
 # ------------------------------------------------------------------------------------------
+TRI_RES, TRI_H, TRI_MASKED = 384, 4, 38
+CPU_SAMPLE = {'msa': 32, 'triangle': 48, 'inference': 16}   # batch rows per CPU step
+CPU_FUSION_ROWS = 1 << 16                   # rows of the pair per CPU fusion sample
+
+
+def _attn_shape(kind):
+    if kind == 'msa':
+        return HEADS, N_RES, 0
+    if kind == 'triangle':
+        return TRI_H, TRI_RES, TRI_MASKED
+    return BIG_H, BIG_RES, BIG_RES - int(BIG_RES * 0.95)
+
+
 def _cpu_worker(args):
+    """Seconds for n batch rows of one attention workload (inputs made before the clock)."""
     import numpy as np
     from oracle import attention as oa
-    seed, n = args
+    kind, seed, n = args
+    h, s, masked = _attn_shape(kind)
     rng = np.random.default_rng(seed)
-    q, k, v, dout = (rng.standard_normal((n, HEADS, N_RES, HEAD_DIM), dtype=np.float32)
+    q, k, v, dout = (rng.standard_normal((n, h, s, HEAD_DIM), dtype=np.float32)
                      for _ in range(4))
-    bias = rng.standard_normal((HEADS, N_RES, N_RES), dtype=np.float32)
-    km = np.ones((n, N_RES), np.uint8)
+    bias = rng.standard_normal((h, s, s), dtype=np.float32)
+    km = np.ones((n, s), np.uint8)
+    if masked:
+        km[:, s - masked:] = 0
     t0 = time.perf_counter()
-    oa.attention_grads_f32(q, k, v, bias, km, dout, HEAD_DIM ** -0.5)
+    if kind == 'inference':
+        oa.attention_forward_f32(q, k, v, bias, km, HEAD_DIM ** -0.5)
+    else:
+        oa.attention_grads_f32(q, k, v, bias, km, dout, HEAD_DIM ** -0.5)
+    return time.perf_counter() - t0
+
+
+def _fusion_cpu_inputs(name, rows, rng):
+    """Inputs of one pair fusion for `rows` rows (BASELINE configs[3] distributions) and the
+    oracle call that computes it."""
+    import numpy as np
+    from oracle import fused as of
+    f = np.float32
+    x = rng.standard_normal((rows, C_Z), dtype=f)
+    ones, zeros = np.ones(C_Z, f), np.zeros(C_Z, f)
+    w = C_Z ** -0.5
+    if name.startswith('ln_gated_dual_proj'):
+        ci = int(name.split('=')[1])
+        wpT, wgT = (rng.standard_normal((2 * ci, C_Z), dtype=f) * w for _ in range(2))
+        bp, bg, mask = np.zeros(2 * ci, f), np.ones(2 * ci, f), np.ones(rows, f)
+        return lambda: of.ln_gdp(x, ones, zeros, wpT, bp, wgT, bg, mask, 1e-5, 'bf16', 128)
+    if name.startswith('trimul_epilogue'):
+        c = int(name.split('=')[1].split()[0])
+        x_cm = rng.standard_normal((c, rows), dtype=f)
+        woT = rng.standard_normal((C_Z, c), dtype=f) * c ** -0.5
+        wgT = rng.standard_normal((C_Z, C_Z), dtype=f) * w
+        bo, bg = np.zeros(C_Z, f), np.zeros(C_Z, f)
+        return lambda: of.trimul_epilogue(x_cm, x, ones, zeros, np.ones(c, f), np.zeros(c, f),
+                                          woT, bo, wgT, bg, None, 1e-5, True, 'bf16', 128)
+    if name.startswith('ln_projection'):
+        wT, wbT = rng.standard_normal((512, C_Z), dtype=f) * w, \
+            rng.standard_normal((4, C_Z), dtype=f) * w
+        return lambda: of.ln_projection(x, ones, zeros, wT, wbT, None, 1e-5, 'bf16', 128)
+    if name.startswith('output_projection'):
+        woT, bo = rng.standard_normal((C_Z, C_Z), dtype=f) * w, np.zeros(C_Z, f)
+        res = rng.standard_normal((rows, C_Z), dtype=f)
+        return lambda: of.output_projection(x, woT, bo, res, None, 'bf16', 128)
+    if name.startswith('gated_dual_proj'):
+        wp, wg = (rng.standard_normal((C_Z, C_Z), dtype=f) * w for _ in range(2))
+        b0, mask = np.zeros(C_Z, f), np.ones(rows, f)
+        return lambda: of.gdp(x, wp, b0, wg, b0, mask, 0, 'bf16')
+    if name.startswith('layer_norm'):
+        return lambda: of.layer_norm_one_pass(x, ones, zeros, 1e-5, 'bf16')
+    if name.startswith('transition'):
+        w1T = rng.standard_normal((512, C_Z), dtype=f) * w
+        w2T = rng.standard_normal((512 * C_Z,), dtype=f) * 512 ** -0.5
+        b1, b2 = np.zeros(512, f), np.zeros(C_Z, f)
+        return lambda: of.transition(x, ones, zeros, w1T, b1, w2T, b2, None, 1e-5, True, 'bf16',
+                                     128)
+    raise KeyError(name)
+
+
+def _cpu_fusion_worker(args):
+    import numpy as np
+    name, seed, rows = args
+    fn = _fusion_cpu_inputs(name, rows, np.random.default_rng(seed))
+    t0 = time.perf_counter()
+    fn()
     return time.perf_counter() - t0
 
 
@@ -82,32 +158,63 @@ class CpuBaseline:
         for var in ('OMP_NUM_THREADS', 'OPENBLAS_NUM_THREADS', 'MKL_NUM_THREADS'):
             os.environ[var] = '1'
         self.pool = mp.get_context('spawn').Pool(self.cores)
-        self.pool.map(_cpu_worker, [(0, 1)] * self.cores)  # import and warm every worker
+        self.pool.map(_cpu_worker, [('msa', 0, 1)] * self.cores)  # import and warm every worker
 
-    def step(self, seqs=CPU_SAMPLE_SEQ):
-        """Seconds of wall time for `seqs` sequences, spread over the pool."""
+    def step(self, kind='msa', rows=None):
+        """Seconds of wall time for `rows` batch rows of a workload, spread over the pool."""
+        rows = CPU_SAMPLE[kind] if rows is None else rows
         t0 = time.perf_counter()
-        self.pool.map(_cpu_worker, [(i, 1) for i in range(seqs)])
+        self.pool.map(_cpu_worker, [(kind, i, 1) for i in range(rows)])
         return time.perf_counter() - t0
+
+    def fusion_step(self, name, rows=CPU_FUSION_ROWS):
+        share = -(-rows // self.cores)
+        t0 = time.perf_counter()
+        self.pool.map(_cpu_fusion_worker, [(name, i, share) for i in range(self.cores)])
+        return time.perf_counter() - t0, share * self.cores
 
     def close(self):
         self.pool.close()
         self.pool.join()
 
 
+def cpu_attention_line(cpu, kind, steps, warmup):
+    """The CPU baseline of an attention workload: TFLOP/s of the reference's closed form (float32
+    port) over a bounded sample of batch rows."""
+    for _ in range(warmup):
+        cpu.step(kind)
+    times = [cpu.step(kind) for _ in range(steps)]
+    t = sum(times) / len(times)
+    n = CPU_SAMPLE[kind]
+    h, s, _ = _attn_shape(kind)
+    flops = (4.0 if kind == 'inference' else 14.0) * n * h * s * s * HEAD_DIM
+    total = {'msa': N_SEQ, 'triangle': TRI_RES, 'inference': BIG_RES}[kind]
+    what = 'fwd only' if kind == 'inference' else 'fwd+bwd'
+    return {'value': flops / t / 1e12, 'unit': 'TFLOP/s', 'cores': cpu.cores, 'kind': 'port',
+            'sample': '%d of %d batch rows per step (%s, float32 numpy, one process per core), '
+                      '%.2f s per step' % (n, total, what, t)}, t
+
+
+def cpu_fusion_lines(cpu):
+    """The CPU baseline of each pair fusion: GB/s of the fusion oracle (oracle/fused.py, the
+    restatement of the reference kernels) over a bounded sample of rows, algorithmic bytes as the
+    GPU lines count them."""
+    out = {}
+    for name, per_row in FUSION_BYTES_PER_ROW.items():
+        t, rows = cpu.fusion_step(name)
+        out[name] = {'value': per_row * rows / t / 1e9, 'unit': 'GB/s', 'cores': cpu.cores,
+                     'kind': 'port',
+                     'sample': '%d of %d rows (numpy oracle, one process per core), %.2f s'
+                               % (rows, PAIR * PAIR, t)}
+    return out
+
+
 def cpu_sample_line(steps, warmup):
     cpu = CpuBaseline()
     try:
-        for _ in range(warmup):
-            cpu.step()
-        times = [cpu.step() for _ in range(steps)]
+        return cpu_attention_line(cpu, 'msa', steps, warmup)
     finally:
         cpu.close()
-    t = sum(times) / len(times)
-    return {'value': attn_flops(CPU_SAMPLE_SEQ) / t / 1e12, 'unit': 'TFLOP/s',
-            'cores': cpu.cores, 'kind': 'port',
-            'sample': '%d of %d sequences per step (fwd+bwd, float32 numpy, one process per '
-                      'core), %.2f s per step' % (CPU_SAMPLE_SEQ, N_SEQ, t)}, t
 
 
 def run_reference(args):
@@ -246,10 +353,21 @@ def run_ours(args):
             dist.destroy_process_group()
         return
 
-    cpu_line = None
+    cpu_line, cpu_more = None, {}
     if rank == 0 and world == 1 and not args.no_cpu:
-        # before any CUDA work: the pool is spawned, never forked
-        cpu_line, _ = cpu_sample_line(2, 1)
+        # before any CUDA work (the pool is spawned, never forked): the headline's CPU baseline,
+        # and those of the triangle, inference and fusion legs that this run includes
+        cpu = CpuBaseline()
+        try:
+            cpu_line, _ = cpu_attention_line(cpu, 'msa', 2, 1)
+            if not args.no_triangle:
+                cpu_more['triangle'] = cpu_attention_line(cpu, 'triangle', 2, 1)[0]
+            if not args.no_inference:
+                cpu_more['inference'] = cpu_attention_line(cpu, 'inference', 1, 0)[0]
+            if not args.no_fusions:
+                cpu_more['fusions'] = cpu_fusion_lines(cpu)
+        finally:
+            cpu.close()
 
     q, k, v, bias, kmask, dout = make_inputs(torch, dev, rank, world, args.n_seq)
     n_local = q.shape[0]
@@ -313,15 +431,26 @@ def run_ours(args):
     e2e = None if args.no_e2e else run_e2e(args, torch, dist, b200, dev, world, q, k, v, bias,
                                            kmask, dout, scale)
 
+    tri = None
+    if not args.no_triangle:
+        tri = bench_triangle(torch, b200, dev, rank, world, args.steps, args.warmup, flush, pk)
+        if 'triangle' in cpu_more:
+            tri['cpu_baseline'] = cpu_more['triangle']
+
     fusions = None
     if not args.no_fusions:
         fusions = bench_fusions(torch, b200, dev, rank, world, args.steps, args.warmup, flush,
                                 pk)
+        for name, line in cpu_more.get('fusions', {}).items():
+            if name in fusions:
+                fusions[name]['cpu_baseline'] = line
 
     big = None
     if not args.no_inference:
         big = bench_inference(torch, b200, dev, rank, world, max(2, args.steps // 3), 2, flush,
                               pk)
+        if 'inference' in cpu_more:
+            big['cpu_baseline'] = cpu_more['inference']
 
     if rank == 0:
         peak = pk['bf16_tflops']
@@ -352,6 +481,8 @@ def run_ours(args):
         }
         if cpu_line is not None:
             line['cpu_baseline'] = cpu_line
+        if tri is not None:
+            line['triangle_384'] = tri
         if fusions is not None:
             line['fusions'] = fusions
         if big is not None:
@@ -362,8 +493,89 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def make_triangle_inputs(torch, dev, rank, world):
+    """BASELINE configs[1]'s inputs, generated whole from one seed on every rank: pair z
+    [384, 384, 128] ~ N(0,1); q, k, v = LN(z) W with W ~ N(0, 1/sqrt(128)) reshaped to H=4, d=32
+    (starting node: row i attends along j, so batch row i holds q[i, h, j, :]); bias
+    [4, 384, 384] = LN(z) W_b; the last 38 residues masked as keys; upstream gradient ~ N(0,1).
+    Returns this rank's rows (q, k, v, dout, kmask) and the whole bias."""
+    from colabfold_legacy_kernels import distributed as cd
+    S, H, d = TRI_RES, TRI_H, HEAD_DIM
+    g = torch.Generator(device=dev)
+    g.manual_seed(2)
+    z = torch.randn(S, S, C_Z, generator=g, device=dev)
+    z = torch.nn.functional.layer_norm(z, (C_Z,)).to(torch.bfloat16)
+    proj = []
+    for _ in range(3):
+        w = (torch.randn(C_Z, H * d, generator=g, device=dev) * C_Z ** -0.5).to(torch.bfloat16)
+        proj.append((z @ w).view(S, S, H, d).permute(0, 2, 1, 3).contiguous())
+    wb = (torch.randn(C_Z, H, generator=g, device=dev) * C_Z ** -0.5).to(torch.bfloat16)
+    bias = (z @ wb).permute(2, 0, 1).contiguous()
+    dout = torch.randn(S, H, S, d, generator=g, device=dev).to(torch.bfloat16)
+    kmask = torch.ones(S, S, dtype=torch.uint8, device=dev)
+    kmask[:, S - TRI_MASKED:] = 0
+    a, b = cd.row_range(S, world, rank)
+    q, k, v = (x[a:b].contiguous() for x in proj)
+    return q, k, v, bias, kmask[a:b].contiguous(), dout[a:b].contiguous()
+
+
+def bench_triangle(torch, b200, dev, rank, world, steps, warmup, flush, pk):
+    """triangle attention (starting node) fwd+bwd with dBias reduced over
+    the 384 rows, rows sharded across ranks with the NCCL dBias all-reduce; the step is VoltaMma
+    (with lse) + VoltaMmaBwd (the gate is applied outside these targets, as the reference
+    composes it). TFLOP/s over device time (max over ranks), L2 flushed before every step."""
+    import torch.distributed as dist
+    from colabfold_legacy_kernels import distributed as cd
+    q, k, v, bias, kmask, dout = make_triangle_inputs(torch, dev, rank, world)
+    scale = HEAD_DIM ** -0.5
+
+    def step():
+        return cd.attention_fwd_bwd(q, k, v, bias, kmask, dout, scale=scale)[5]
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    evs = []
+    for _ in range(steps):
+        flush.fill_(7)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        step()
+        e1.record()
+        evs.append((e0, e1))
+    torch.cuda.synchronize()
+    ms = sum(x.elapsed_time(y) for x, y in evs) / steps
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    flops = 14.0 * TRI_RES * TRI_H * TRI_RES ** 2 * HEAD_DIM
+    tf = flops / (ms * 1e-3) / 1e12
+    if b200.device_status() != 0:
+        raise RuntimeError('a kernel reported a wait that gave up')
+    return {'ms': ms, 'TFLOP/s': tf, 'frac_bf16': tf / (pk['bf16_tflops'] * world),
+            'flops': flops, 'config': 'triangle attention (starting node) fwd+bwd with dBias, '
+            'pair 384x384, H=4, d=32, last 38 residues masked, rows sharded over %d GPU(s)'
+            % world}
+
+
 PAIR = 768            # BASELINE configs[3]: pair [768, 768, 128]
 C_Z = 128
+# algorithmic bytes per row of each pair fusion: every input read once, every output written
+# once (bf16; float32 for x_cm), weights (read once per launch) added separately
+FUSION_BYTES_PER_ROW = {
+    'ln_gated_dual_proj ci=64': C_Z * 2 + 2 + 2 * 64 * 2,
+    'ln_gated_dual_proj ci=128': C_Z * 2 + 2 + 2 * 128 * 2,
+    'trimul_epilogue C=64 CA=O=128 add_input': 64 * 4 + C_Z * 2 + C_Z * 2,
+    'trimul_epilogue C=128 CA=O=128 add_input': 128 * 4 + C_Z * 2 + C_Z * 2,
+    'ln_projection n=512 heads=4': C_Z * 2 + 512 * 2 + 4 * 2,
+    'output_projection 128->128 + residual': C_Z * 2 * 3,
+    'gated_dual_proj K=N=128 sigmoid': C_Z * 2 + C_Z * 2 + 2,
+    'layer_norm C=128': C_Z * 2 * 2,
+    'transition 128->512->128 add_input': C_Z * 2 * 2,
+}
 
 
 def bench_fusions(torch, b200, dev, rank, world, steps, warmup, flush, pk, only=None):
@@ -471,15 +683,14 @@ BWD_DRAM_BYTES_PER_SEQ = 144.56e6 / 64
 BIG_RES, BIG_H = 2048, 4
 
 
-def bench_inference(torch, b200, dev, rank, world, steps, warmup, flush, pk):
-    """BASELINE configs[4]: triangle attention forward only (want_lse off, one-element lse),
-    pair [2048, 2048, 128] ~ N(0,1), q/k/v = LN(z) W reshaped to H=4, d=32, bias [4, 2048, 2048]
-    ~ N(0,1), the last 5% of residues masked; rows sharded across ranks, then the output
-    all-gather. Reports the forward alone and forward + gather (device time, max over ranks)."""
-    import torch.distributed as dist
+def make_inference_inputs(torch, dev, rank, world, rows=None):
+    """BASELINE configs[4]'s inputs: pair z [2048, 2048, 128] ~ N(0,1) generated in row blocks
+    from one seed (every rank sees the same pair), q/k/v = LN(z) W reshaped to H=4, d=32 with
+    W ~ N(0, 1/sqrt(128)), bias [4, 2048, 2048] ~ N(0,1), the last 5% of residues masked; this
+    rank's rows [a, b) of the pair (or `rows` = (a, b) when given)."""
     from colabfold_legacy_kernels import distributed as cd
     S, H, d = BIG_RES, BIG_H, HEAD_DIM
-    a, b = cd.row_range(S, world, rank)
+    a, b = rows if rows is not None else cd.row_range(S, world, rank)
     n = b - a
     g = torch.Generator(device=dev)
     g.manual_seed(5)
@@ -498,8 +709,18 @@ def bench_inference(torch, b200, dev, rank, world, steps, warmup, flush, pk):
                 t[lo - a:hi - a] = (zz @ wt).view(hi - lo, S, H, d).permute(0, 2, 1, 3)
     kmask = torch.ones(n, S, dtype=torch.uint8, device=dev)
     kmask[:, int(S * 0.95):] = 0
+    return qkv[0], qkv[1], qkv[2], bias, kmask
+
+
+def bench_inference(torch, b200, dev, rank, world, steps, warmup, flush, pk):
+    """BASELINE configs[4]: triangle attention forward only (want_lse off, one-element lse),
+    pair [2048, 2048, 128] ~ N(0,1), q/k/v = LN(z) W reshaped to H=4, d=32, bias [4, 2048, 2048]
+    ~ N(0,1), the last 5% of residues masked; rows sharded across ranks, then the output
+    all-gather. Reports the forward alone and forward + gather (device time, max over ranks)."""
+    import torch.distributed as dist
+    S, H, d = BIG_RES, BIG_H, HEAD_DIM
+    q, k, v, bias, kmask = make_inference_inputs(torch, dev, rank, world)
     one = torch.empty(1, device=dev)
-    q, k, v = qkv
     scale = d ** -0.5
 
     def fwd():
@@ -646,6 +867,8 @@ def main():
     ap.add_argument('--no-e2e', action='store_true', help='skip the host-buffer end-to-end leg')
     ap.add_argument('--no-inference', action='store_true',
                     help='skip the large-protein inference leg (BASELINE configs[4])')
+    ap.add_argument('--no-triangle', action='store_true',
+                    help='skip the triangle-attention leg (BASELINE configs[1])')
     ap.add_argument('--only-fusion', default=None, metavar='NAME',
                     help='run only the pair-fusion lines whose name starts with NAME (e.g. '
                          'ln_projection, trimul_epilogue, transition) and print them')

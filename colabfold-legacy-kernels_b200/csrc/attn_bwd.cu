@@ -23,9 +23,8 @@
 //     16-bit pairs, the A operands of dV += P^T dout and dK += dS^T q (A read from TMEM);
 //   * dS also goes MN-major into swizzled shared memory for dQ = dS k (M=64), whose fp32 tile
 //     is added into the workspace accumulator with 16-byte vector atomics;
-//   * the bias is transposed once per call into the workspace as f16 [H][Sk][Sq'] (exact for
-//     f16 input; bf16 values are kept exactly within f16's range and clamped to +-65504 beyond
-//     it), so a key's bias values arrive by TMA as one contiguous 128-byte row;
+//   * the bias is transposed once per call into the workspace in its own 16-bit type
+//     [H][Sk][Sq'] (exact), so a key's bias values arrive by TMA as one contiguous 128-byte row;
 //   * dBias: each warpgroup stages its half-step's fp32 dS rows [32 queries][128 keys] in
 //     shared memory and one thread hands them to TMA as a single bulk reduce-add into dBias
 //     (full-line L2 reductions); an item's query steps start at a step that depends on its
@@ -37,6 +36,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdint>
 #include <string>
 
@@ -78,7 +78,7 @@ struct BGeom {
     static constexpr int QATOM = kBQ * ROWB;  // one atom of a 64-row (query) tile
     static constexpr int KTILE = NA * KATOM;
     static constexpr int QTILE = NA * QATOM;
-    static constexpr int BT = kBQ * kBK * 2;  // bias^T tile: [128 keys][64 queries] f16
+    static constexpr int BT = kBQ * kBK * 2;  // bias^T tile: [128 keys][64 queries], 16-bit
     static constexpr int DS = kBK * 128;      // dS, MN-major: 128 key rows of 64 queries
     static constexpr int DN = DP;
     // Step sets: consecutive 64-query steps alternate between NP sets (ping-pong). A set is two
@@ -531,8 +531,8 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
                     // queries 32 hf + qc .. +4: half of 16-byte chunk 4 hf + qc/8 of the key's row
                     const uint2 b2 = *reinterpret_cast<const uint2*>(
                         brow + (((4 * hf + (qc >> 3)) ^ (t & 7)) << 4) + (c & 1) * 8);
-                    const float2 b01 = __half22float2(*reinterpret_cast<const __half2*>(&b2.x));
-                    const float2 b23 = __half22float2(*reinterpret_cast<const __half2*>(&b2.y));
+                    const float2 b01 = E::unpack(b2.x);
+                    const float2 b23 = E::unpack(b2.y);
                     // the statistics are stored negated: -lse and -delta
                     const float4 l4 = *reinterpret_cast<const float4*>(lsh + qc);
                     const float4 d4 = *reinterpret_cast<const float4*>(dlh + qc);
@@ -723,9 +723,10 @@ __global__ void row_delta_kernel(const T* __restrict__ out, const T* __restrict_
     nlse[r] = -lse[r];
 }
 
-// bt[h][k][q] = log2e * bias[h][q][k] in fp32, queries padded to Sqp with zeros; 32x32 tiles
+// bt[h][k][q] = bias[h][q][k] in the bias's own 16-bit type (exact), queries padded to Sqp with
+// zeros; 32x32 tiles
 template <typename T>
-__global__ void bias_transpose_kernel(const T* __restrict__ bias, __half* __restrict__ bt, int Sq,
+__global__ void bias_transpose_kernel(const T* __restrict__ bias, T* __restrict__ bt, int Sq,
                                       int Sk, int Sqp) {
     __shared__ float tile[32][33];
     const int h = blockIdx.z, q0 = blockIdx.x * 32, k0 = blockIdx.y * 32;
@@ -736,12 +737,11 @@ __global__ void bias_transpose_kernel(const T* __restrict__ bias, __half* __rest
             (q < Sq && k < Sk) ? Elem<T>::to_f(src[(long long)q * Sk + k]) : 0.f;
     }
     __syncthreads();
-    __half* dst = bt + (long long)h * Sk * Sqp;
+    T* dst = bt + (long long)h * Sk * Sqp;
     for (int r = threadIdx.y; r < 32; r += blockDim.y) {
         const int k = k0 + r, q = q0 + threadIdx.x;
         if (k < Sk && q < Sqp) {
-            dst[(long long)k * Sqp + q] =
-                __float2half_rn(fminf(fmaxf(tile[threadIdx.x][r], -65504.f), 65504.f));
+            dst[(long long)k * Sqp + q] = Elem<T>::from_f(tile[threadIdx.x][r]);
         }
     }
 }
@@ -776,18 +776,29 @@ bool aligned16(const void* p) {
     return (reinterpret_cast<uintptr_t>(p) & 15) == 0;
 }
 
-// Workspace: dQ accumulator | -delta | -lse | bias^T (f16, queries padded to a multiple of 8),
-// each 256-byte aligned
+// Workspace: dQ accumulator | -delta | -lse | bias^T (16-bit, queries padded to a multiple of
+// 8), each 256-byte aligned. `ok` is false when a size product overflows 64 bits.
 struct Workspace {
-    size_t dq, delta, nlse, bt, total;
-    static Workspace of(size_t N, size_t H, size_t Sq, size_t Sk, size_t D) {
+    size_t dq = 0, delta = 0, nlse = 0, bt = 0, total = 0;
+    bool ok = false;
+    static Workspace of(uint64_t N, uint64_t H, uint64_t Sq, uint64_t Sk, uint64_t D) {
         Workspace w;
-        const size_t rows = N * H * Sq, sqp = (Sq + 7) & ~size_t(7);
+        uint64_t rows, dqb, btb;
+        const uint64_t sqp = (Sq + 7) & ~uint64_t(7);
+        if (Sq > (uint64_t(1) << 40) || __builtin_mul_overflow(N, H, &rows) ||
+            __builtin_mul_overflow(rows, Sq, &rows) || __builtin_mul_overflow(rows, D, &dqb) ||
+            __builtin_mul_overflow(dqb, uint64_t(4), &dqb) || rows > (uint64_t(1) << 60) ||
+            __builtin_mul_overflow(H, Sk, &btb) || __builtin_mul_overflow(btb, sqp, &btb) ||
+            __builtin_mul_overflow(btb, uint64_t(2), &btb) || dqb > (uint64_t(1) << 60) ||
+            btb > (uint64_t(1) << 60)) {
+            return w;
+        }
         w.dq = 0;
-        w.delta = align256(rows * D * sizeof(float));
+        w.delta = align256(dqb);
         w.nlse = w.delta + align256(rows * sizeof(float));
         w.bt = w.nlse + align256(rows * sizeof(float));
-        w.total = w.bt + align256(H * Sk * sqp * sizeof(__half));
+        w.total = w.bt + align256(btb);
+        w.ok = true;
         return w;
     }
 };
@@ -829,7 +840,7 @@ cudaError_t launch_dp(cudaStream_t stream, const CUtensorMap* maps, const BwdPar
 
 template <typename T>
 cudaError_t run_backward(cudaStream_t stream, const CUtensorMap* maps, const BwdParams& p,
-                         const void* bias, __half* bt, int Sqp, const void* out, const void* dout,
+                         const void* bias, void* bt, int Sqp, const void* out, const void* dout,
                          const float* lse, float* ndelta, float* nlse, void* dq, int dbias_mode) {
     const long long rows = (long long)p.N * p.H * p.Sq;
     cudaError_t e;
@@ -844,8 +855,9 @@ cudaError_t run_backward(cudaStream_t stream, const CUtensorMap* maps, const Bwd
     row_delta_kernel<T><<<(unsigned)((rows + 255) / 256), 256, 0, stream>>>(
         static_cast<const T*>(out), static_cast<const T*>(dout), lse, ndelta, nlse, rows, p.D);
     const dim3 tgrid((Sqp + 31) / 32, (p.Sk + 31) / 32, p.H);
-    bias_transpose_kernel<T><<<tgrid, dim3(32, 8), 0, stream>>>(static_cast<const T*>(bias), bt,
-                                                                 p.Sq, p.Sk, Sqp);
+    bias_transpose_kernel<T><<<tgrid, dim3(32, 8), 0, stream>>>(static_cast<const T*>(bias),
+                                                                 static_cast<T*>(bt), p.Sq, p.Sk,
+                                                                 Sqp);
     if ((e = cudaGetLastError()) != cudaSuccess) {
         return e;
     }
@@ -882,7 +894,11 @@ extern "C" int cflk_volta_mma_bwd_workspace_size(int64_t N, int64_t H, int64_t S
     if (N < 0 || H < 0 || Sq < 0 || Sk < 0 || D < 0 || bytes == nullptr) {
         return fail(kInvalidArgument, "volta_mma_bwd: bad sizes");
     }
-    *bytes = Workspace::of(N, H, Sq, Sk, D).total;
+    const Workspace ws = Workspace::of(N, H, Sq, Sk, D);
+    if (!ws.ok) {
+        return fail(kInvalidArgument, "volta_mma_bwd: sizes overflow the workspace size");
+    }
+    *bytes = ws.total;
     return kOk;
 }
 
@@ -903,10 +919,23 @@ extern "C" int cflk_volta_mma_bwd(void* stream_, int dtype, const void* q, const
     if (D != 8 && D != 16 && D != 24 && D != 32 && D != 48 && D != 64 && D != 96) {
         return fail(kInvalidArgument, "volta_mma_bwd: unsupported head dim");
     }
-    if (((Sk + kBK - 1) / kBK) * H * N * ((Sq + kBQ - 1) / kBQ) >= (int64_t(1) << 31)) {
-        return fail(kInvalidArgument, "volta_mma_bwd: more than 2^31 (key tile, query step) pairs");
+    {
+        // (key tile, query step) pairs, each factor below 2^31 so that no product wraps
+        int64_t pairs = 0;
+        if (N >= (int64_t(1) << 31) || H >= (int64_t(1) << 31) || Sq >= (int64_t(1) << 31) ||
+            Sk >= (int64_t(1) << 31) ||
+            __builtin_mul_overflow((Sk + kBK - 1) / kBK, H, &pairs) ||
+            __builtin_mul_overflow(pairs, N, &pairs) ||
+            __builtin_mul_overflow(pairs, (Sq + kBQ - 1) / kBQ, &pairs) ||
+            pairs >= (int64_t(1) << 31)) {
+            return fail(kInvalidArgument,
+                        "volta_mma_bwd: more than 2^31 (key tile, query step) pairs");
+        }
     }
     const Workspace ws = Workspace::of(N, H, Sq, Sk, D);
+    if (!ws.ok) {
+        return fail(kInvalidArgument, "volta_mma_bwd: sizes overflow the workspace size");
+    }
     if (workspace_bytes < ws.total || (ws.total > 0 && workspace == nullptr) ||
         (reinterpret_cast<uintptr_t>(workspace) & 255) != 0) {
         return fail(kInternal, "volta_mma_bwd: no scratch for the dQ accumulator");
@@ -920,7 +949,7 @@ extern "C" int cflk_volta_mma_bwd(void* stream_, int dtype, const void* q, const
     float* dq_acc = reinterpret_cast<float*>(wsb + ws.dq);
     float* ndelta = reinterpret_cast<float*>(wsb + ws.delta);
     float* nlse = reinterpret_cast<float*>(wsb + ws.nlse);
-    __half* bt = reinterpret_cast<__half*>(wsb + ws.bt);
+    void* bt = wsb + ws.bt;
     const int Sqp = (int)((Sq + 7) & ~int64_t(7));
     if (H == 0 || Sq == 0 || Sk == 0 || N == 0) {
         // nothing to differentiate: zero what exists
@@ -959,8 +988,7 @@ extern "C" int cflk_volta_mma_bwd(void* stream_, int dtype, const void* q, const
             !encode_tiled(&maps[1], tdt, 2, 4, k, dk4, sk4, boxk, sw) ||
             !encode_tiled(&maps[2], tdt, 2, 4, v, dk4, sk4, boxk, sw) ||
             !encode_tiled(&maps[3], tdt, 2, 4, dout, dq4, sq4, boxq, sw) ||
-            !encode_tiled(&maps[4], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, 3, bt, dbt, sbt, boxbt,
-                          CU_TENSOR_MAP_SWIZZLE_128B)) {
+            !encode_tiled(&maps[4], tdt, 2, 3, bt, dbt, sbt, boxbt, CU_TENSOR_MAP_SWIZZLE_128B)) {
             return fail(kInvalidArgument, "volta_mma_bwd: TMA descriptor rejected");
         }
     }
@@ -1017,10 +1045,13 @@ extern "C" int cflk_volta_mma_bwd(void* stream_, int dtype, const void* q, const
 static constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-// The array's device address on the current device, looked up once per device. The host-side
-// name g_noalloc_scratch is only a stand-in for the symbol, never a device pointer.
+// The array's device address on the current device, looked up on the first call on each device
+// and kept in an atomic slot (two host threads making that first call at once both look it up
+// and store the same value). The host-side name g_noalloc_scratch is only a stand-in for the
+// symbol, never a device pointer. A cudaDeviceReset unloads the module; the cached address is
+// then stale, so the library must not be used on that device after a reset.
 static int noalloc_scratch(void** out) {
-    static void* addr[cflk::kMaxDevices] = {};
+    static std::atomic<void*> addr[cflk::kMaxDevices] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) {
@@ -1030,17 +1061,17 @@ static int noalloc_scratch(void** out) {
     if (dev < 0 || dev >= cflk::kMaxDevices) {
         return cflk::fail(cflk::kInternal, "volta_mma_bwd_noalloc: device ordinal out of range");
     }
-    if (addr[dev] == nullptr) {
-        void* p = nullptr;
-        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-        if (e != cudaSuccess || p == nullptr) {
+    void* a = addr[dev].load(std::memory_order_acquire);
+    if (a == nullptr) {
+        e = cudaGetSymbolAddress(&a, g_noalloc_scratch);
+        if (e != cudaSuccess || a == nullptr) {
             return cflk::fail(cflk::kInternal,
                               std::string("volta_mma_bwd_noalloc: scratch address: ") +
                                   cudaGetErrorString(e));
         }
-        addr[dev] = p;
+        addr[dev].store(a, std::memory_order_release);
     }
-    *out = addr[dev];
+    *out = a;
     return cflk::kOk;
 }
 
@@ -1066,7 +1097,8 @@ extern "C" int cflk_volta_mma_bwd_noalloc(void* stream, int dtype, const void* q
                               " bytes of scratch, the static scratch holds " +
                               std::to_string(kNoAllocScratchBytes) +
                               " (cflk_volta_mma_bwd_workspace_size: about 4*N*H*Sq*(D+2) + "
-                              "2*H*Sk*Sq bytes); use cflk_volta_mma_bwd with a workspace");
+                              "2*H*Sk*Sq8 bytes, Sq8 = Sq rounded up to 8); use "
+                              "cflk_volta_mma_bwd with a workspace");
     }
     void* scratch = nullptr;
     rc = noalloc_scratch(&scratch);

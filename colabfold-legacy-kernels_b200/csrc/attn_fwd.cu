@@ -44,8 +44,11 @@ constexpr int kBQ = 128;   // query rows per CTA (= TMEM lanes)
 constexpr int kBK = 128;   // keys per tile
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kMaskedLogit = -1.0e4f;
+// log2 units: O and l are rescaled only when a tile raises the row max by more than this, so P
+// stays below 2^8 between rescales
 constexpr float kRescaleThreshold = 8.0f;
-constexpr int kFmaExpEvery = 4;  // share of a row's exponentials computed on the FMA pipe  // log2 units: P stays below 2^8 between rescales
+// one exponential pair in kFmaExpEvery is computed on the FMA pipe, the rest on the MUFU
+constexpr int kFmaExpEvery = 4;
 
 struct FwdParams {
     const void* bias;

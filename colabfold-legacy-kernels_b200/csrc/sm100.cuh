@@ -74,7 +74,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // set `code` in *status and return false. A set *abort (shared memory) makes the wait give up at
 // once: one timeout in a CTA is enough to know its data are bad.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned* status,
-                                          unsigned code, volatile int* abort) {
+                                          unsigned code, volatile int* abort,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
     const uint32_t b = smem_u32(bar);
     if (mbar_try_wait(b, parity)) {
         return true;
@@ -86,7 +87,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
                 return true;
             }
         }
-        if ((abort != nullptr && *abort) || globaltimer() - t0 > kWaitLimitNs) {
+        if ((abort != nullptr && *abort) || globaltimer() - t0 > limit_ns) {
             atomicOr(status, code);
             if (abort != nullptr) {
                 *abort = 1;

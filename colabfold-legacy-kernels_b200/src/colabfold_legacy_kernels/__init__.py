@@ -4,13 +4,15 @@ Same public surface as colabfold-legacy-kernels' resolver
 (src/colabfold_legacy_kernels/__init__.py:5-12,69-126): `available`, `library_path`, `symbol`,
 `kernel_dir`, `supported_capabilities` and `KERNELS`, with compute capability 100 added.
 
-For cc=100 every hot-path kernel lives in one library, libcflk_sm100.so, built from this
-repository's sm_100a sources. `symbol(kernel, 100)` gives the same XLA FFI target name as the
-reference (what the JAX caller registers); `c_symbol(kernel, 100)` gives the C-ABI entry point
-in the library that backs it (include/cflk_b200.h). Kernels outside the hot path (LayerNorm,
-the unfused gated dual projection, the outer product mean) have no cc=100 entry, so
-`available(100)` without a kernel is False while `available(100, 'attention')` is True once the
-library is built.
+For cc=100 every kernel built so far lives in one library, libcflk_sm100.so, built from this
+repository's sm_100a sources. That library exports plain C-ABI entry points
+(include/cflk_b200.h), not XLA FFI handlers: `c_symbol(kernel, 100)` names the entry point, and
+`symbol(kernel, 100)` names the XLA FFI target that a JAX caller registers for the kernel (the
+reference's own target name). The handler behind that target is a thin shim over the C entry
+point, compiled against XLA's FFI headers by the caller's build; this package does not ship it,
+because the headers are not part of this build's toolchain. The outer-product-mean kernels have
+no cc=100 entry yet, so `available(100)` without a kernel is False while
+`available(100, 'attention')` is True once the library is built.
 """
 
 from pathlib import Path
@@ -145,7 +147,8 @@ def library_path(kernel, cc):
 
 
 def symbol(kernel, cc):
-    """Give the XLA FFI target name that the library exports."""
+    """Give the XLA FFI target name of one kernel. The sm_70/sm_75 libraries export it; for
+    cc=100 it is the name an FFI shim over c_symbol(kernel, 100) registers."""
     cc, lib, sym = _resolve(kernel, cc)
     if sym is None:
         raise FileNotFoundError(

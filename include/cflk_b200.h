@@ -5,7 +5,7 @@
  * on the given CUDA stream (a cudaStream_t, NULL for the legacy default stream) on the current
  * device, does no host synchronisation and allocates nothing. Each one replaces one XLA FFI
  * target of the reference (named below with its file:line); an XLA FFI handler, where the XLA
- * headers exist, is a thin shim over these functions (INTEGRATION.md).
+ * headers exist, is a thin shim over these functions.
  *
  * 16-bit buffers hold `dtype` elements: CFLK_F16 (the reference's F16, bit-compatible) or
  * CFLK_BF16 (an extension). float buffers are float32. Pointers to 16-bit data must be 16-byte
@@ -73,7 +73,7 @@ CFLK_API int cflk_volta_mma_packed(void* stream, int dtype, const void* p, const
                                    int64_t block_q, int64_t block_k, int column);
 
 /* Bytes of device workspace cflk_volta_mma_bwd needs for these sizes: a float32 dQ accumulator,
- * the negated row statistics (-delta, -lse) and the bias transposed to f16
+ * the negated row statistics (-delta, -lse) and the bias transposed in its own 16-bit type
  * [H][Sk][Sq rounded up to 8] (the reference
  * takes its dQ accumulator and row statistic from XLA's ScratchAllocator,
  * cuda/volta_mma_attn_bwd.cu:346-361). */
@@ -178,6 +178,20 @@ CFLK_API int cflk_volta_layer_norm(void* stream, int dtype, const void* x, const
 CFLK_API int cflk_volta_gdp(void* stream, int dtype, const void* x, const void* wp,
                             const void* bp, const void* wg, const void* bg, const void* mask,
                             void* out, int64_t M, int64_t K, int64_t N, int64_t activation);
+
+/* ---- diagnostics (no counterpart in the reference) ------------------------------------- */
+
+/* Evaluates, for n float32 inputs x on the device, the FMA-pipe exponential 2^x that the attention
+ * kernels compute for part of their softmax (into fma_out) and the hardware ex2.approx (into
+ * mufu_out), so that a test can bound its error. */
+CFLK_API int cflk_diag_ex2_fma(void* stream, const float* x, float* fma_out, float* mufu_out,
+                               int64_t n);
+
+/* Runs one CTA that waits on an mbarrier nothing arrives on, for at most limit_ns (0 < limit_ns
+ * <= 2 s), the bounded wait every pipeline of the library uses. The wait gives up, ORs the code 4
+ * into *status and writes the nanoseconds it waited into *elapsed_ns (device pointers). */
+CFLK_API int cflk_diag_bounded_wait(void* stream, uint64_t limit_ns, unsigned* status,
+                                    unsigned long long* elapsed_ns);
 
 #ifdef __cplusplus
 }

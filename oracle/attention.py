@@ -100,6 +100,21 @@ def attention_grads_f32(q, k, v, bias, kmask, dout, scale):
     return out, lse2, dq, dk, dv, ds.sum(0)
 
 
+def attention_forward_f32(q, k, v, bias, kmask, scale):
+    """The forward alone (out, log2-domain lse) in float32 with batched matmuls: the CPU baseline
+    of the inference workload."""
+    f = np.float32
+    q, k, v, bias = (np.asarray(x, f) for x in (q, k, v, bias))
+    live = (np.asarray(kmask) != 0)[:, None, None, :]
+    logits = np.matmul(q, np.swapaxes(k, -1, -2)) * f(scale) + bias[None]
+    logits = np.where(live, logits, f(NEG))
+    mx = logits.max(-1, keepdims=True)
+    p = np.exp(logits - mx)
+    l = p.sum(-1, keepdims=True)
+    p /= l
+    return np.matmul(p, v), (np.log(l) + mx)[..., 0] * f(LOG2E)
+
+
 def trim_limits(kmask):
     """lims [N+1]: each batch row's last live key + 1, then their maximum
     (tests/test_packed_attention.py:53-57)."""

@@ -179,3 +179,25 @@ def test_rejects_bad_workspace_and_head_dim(cuda_device):
     rc = lib.cflk_volta_mma_bwd(m._stream(), 0, z, z, z, z, z, z, z, z, z, z, z, z, z, 0, 1, 1,
                                 8, 8, 32, 1.0, 1)
     assert rc == 2 and b'scratch' in lib.cflk_last_error()
+
+
+def test_bf16_bias_beyond_f16_range(cuda_device):
+    """A bf16 bias above f16's range (|b| > 65504) gives the backward the same P as the forward:
+    the bias keeps its own 16-bit type through the backward's transpose."""
+    q, k, v, bias, km, dout = inputs(2, 2, 96, 96, 32, 3, 'bf16')
+    rng = np.random.default_rng(7)
+    # about one key a row at +7e4 (bf16 69888 or 70144): it takes most of the row's softmax,
+    # which a bias clamped to 65504 in the backward alone would move to the other keys; float32
+    # resolves logits near 7e4 to 2^-7, so P keeps about 0.5% error in both passes
+    big = rng.random(bias.shape) < 0.01
+    bias = np.where(big, 7.0e4, bias)
+    bias = oa_round(bias)
+    want = oa.attention_grads(q, k, v, bias, km, dout, 32 ** -0.5)
+    out, lse, grads = run_both(q, k, v, bias, km, dout, 'bf16', cuda_device)
+    assert rel_max(host(out), want[0]) < 0.05
+    check_grads(grads, want[2:], 'bf16 big bias')
+
+
+def oa_round(x):
+    from oracle.numerics import round_to
+    return round_to(x, 'bf16')

@@ -92,6 +92,28 @@ def test_workspace_size():
     assert n.value == (align(rows * 32 * 4) + 2 * align(rows * 4) + align(3 * 7 * 16 * 2))
 
 
+def test_workspace_size_refuses_overflowing_sizes():
+    """Sizes whose byte counts overflow 64 bits are refused, not wrapped; the no-allocation
+    backward refuses them before it touches the GPU (its scratch size check relies on this)."""
+    l = lib()
+    l.cflk_last_error.restype = ctypes.c_char_p
+    n = ctypes.c_size_t(0)
+    i64 = ctypes.c_int64
+    big = i64(1 << 40)
+    assert l.cflk_volta_mma_bwd_workspace_size(big, big, i64(1 << 20), i64(8), i64(32),
+                                               ctypes.byref(n)) == 1
+    assert b'overflow' in l.cflk_last_error()
+    assert l.cflk_volta_mma_bwd_workspace_size(i64(1), big, i64(8), big, i64(32),
+                                               ctypes.byref(n)) == 1
+    f = l.cflk_volta_mma_bwd_noalloc
+    f.argtypes = [ctypes.c_void_p, ctypes.c_int] + [ctypes.c_void_p] * 12 + [ctypes.c_int64] * 5 \
+        + [ctypes.c_float, ctypes.c_int]
+    z = None
+    assert f(z, 1, *([z] * 12), 1 << 40, 1 << 40, 1 << 20, 8, 32, 0.17, 1) == 1
+    assert f(z, 1, *([z] * 12), 4096, 8, 512, 512, 32, 0.17, 1) == 1
+    assert b'static scratch' in l.cflk_last_error()
+
+
 def test_resolver_capabilities():
     assert clk.supported_capabilities() == (70, 75, 100)
     for k in ('attention', 'attention_bwd', 'ln_gated_dual_proj', 'trimul_epilogue',

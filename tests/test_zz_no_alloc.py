@@ -4,7 +4,8 @@ Hosts that own every device allocation, or code that must not call cudaMalloc, c
 backward a workspace; this entry point keeps its scratch in a static device array instead. The
 test calls it through the C ABI twice in a row and checks each result against the workspace
 entry point's, with the tolerances of the repeated-call test (dK and dV bitwise, dQ and dBias
-within 1e-3, since those two arrive by atomic adds), and checks that a problem larger than the
+within 1e-3, since those two arrive by atomic adds); it checks that those two calls leave both
+torch's allocator and the device's free memory unchanged, and that a problem larger than the
 array is refused. It lives in its own file, collected last, and passes on its own in a fresh
 process as well as after the other tests.
 """
@@ -44,15 +45,27 @@ def test_noalloc_matches_workspace_entry_point(cuda_device):
     scale = d ** -0.5
     out, lse = m.volta_mma(tq, tk, tv, tb, kmask, scale=scale)
     want = m.volta_mma_bwd(tq, tk, tv, tb, kmask, out, td, lse, scale=scale)
-    for _ in range(2):
-        dq, dk, dv = torch.empty_like(tq), torch.empty_like(tk), torch.empty_like(tv)
-        dbias = torch.full((h, s, s), 7.0, device=cuda_device)
+    outs = [(torch.empty_like(tq), torch.empty_like(tk), torch.empty_like(tv),
+             torch.full((h, s, s), 7.0, device=cuda_device)) for _ in range(3)]
+
+    def call(dq, dk, dv, dbias):
         rc = lib.cflk_volta_mma_bwd_noalloc(m._stream(), 1, P(tq), P(tk), P(tv), P(tb), P(kmask),
                                             P(out), P(td), P(lse), P(dq), P(dk), P(dv), P(dbias),
                                             n, h, s, s, d, scale, 1)
         assert rc == 0, lib.cflk_last_error()
+
+    # one call first, so that loading the library's kernels (which the driver may do lazily, on
+    # first use) is not counted; then the two checked calls must not change either figure
+    call(*outs[0])
+    torch.cuda.synchronize()
+    torch_bytes = torch.cuda.memory_allocated(cuda_device)
+    free_bytes = torch.cuda.mem_get_info(cuda_device)[0]
+    for dq, dk, dv, dbias in outs[1:]:
+        call(dq, dk, dv, dbias)
         torch.cuda.synchronize()
         assert m.device_status() == 0
+        assert torch.cuda.memory_allocated(cuda_device) == torch_bytes
+        assert torch.cuda.mem_get_info(cuda_device)[0] == free_bytes
         assert torch.equal(dk, want[1]) and torch.equal(dv, want[2])
         assert rel_max(host(dq), host(want[0])) < 1e-3
         assert rel_max(host(dbias), host(want[3])) < 1e-3
@@ -64,7 +77,8 @@ def test_noalloc_refuses_problems_beyond_its_scratch(cuda_device):
     cap = lib.cflk_volta_mma_bwd_noalloc_max_scratch()
     assert cap == 32 << 20
     z = ctypes.c_void_p(0)
-    # N*H*Sq*(D+1)*4 bytes: 4096 * 8 * 512 * 33 * 4 is far beyond 32 MiB; nothing is launched
+    # 4*N*H*Sq*(D+2) bytes alone: 4 * 4096 * 8 * 512 * 34 is far beyond 32 MiB; nothing is
+    # launched
     rc = lib.cflk_volta_mma_bwd_noalloc(m._stream(), 1, *([z] * 12), 4096, 8, 512, 512, 32,
                                         0.17, 1)
     assert rc == 1

@@ -325,6 +325,17 @@ def make_inputs(torch, dev, rank, world, n_seq=N_SEQ):
     return q, k, v, bias, kmask[sl].contiguous(), dout[sl].contiguous()
 
 
+def make_gate(torch, dev, shape):
+    """The gate of configs[2]'s gated attention: gate = LN(m) W_g, here a unit-variance bf16
+    tensor of q's shape drawn from its own seed (the q/k/v draws stay unchanged), and the gate
+    bias 1.0 that the config names, [H, d]."""
+    g = torch.Generator(device=dev)
+    g.manual_seed(3)
+    gate = torch.randn(*shape, generator=g, device=dev).to(torch.bfloat16)
+    gb = torch.ones(shape[1], shape[3], dtype=torch.bfloat16, device=dev)
+    return gate, gb
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -428,6 +439,20 @@ def run_ours(args):
     fwd_tf = 4.0 * n_local * HEADS * N_RES ** 2 * HEAD_DIM / (fwd_ms * 1e-3) / 1e12
     bwd_tf = 10.0 * n_local * HEADS * N_RES ** 2 * HEAD_DIM / (bwd_ms * 1e-3) / 1e12
 
+    # the gated training step of configs[2] (gate bias 1.0): the fused gated forward (with lse)
+    # and the gate-aware backward, which the reference composes from VoltaMma, an XLA gate and
+    # VoltaMmaBwd; same algorithmic FLOPs (the gate's elementwise work is not counted)
+    gate, gb = make_gate(torch, dev, q.shape)
+
+    def gated_step():
+        y, l2 = b200.volta_mma_gated(q, k, v, gate, gb, bias, kmask, scale=scale)
+        return b200.volta_mma_gated_bwd(q, k, v, gate, gb, bias, kmask, y, dout, l2,
+                                        scale=scale)
+
+    gated_step()
+    gated_ms = timed(gated_step, args.steps)
+    del gate, gb
+
     e2e = None if args.no_e2e else run_e2e(args, torch, dist, b200, dev, world, q, k, v, bias,
                                            kmask, dout, scale)
 
@@ -470,6 +495,10 @@ def run_ours(args):
                 'traffic_source': 'ncu dram__bytes_read.sum + dram__bytes_write.sum of '
                                   'attn_bwd_kernel at N_seq=64 (144.6 MB), scaled by the '
                                   'sequences processed'},
+            'gated_step': {'ms': gated_ms,
+                           'TFLOP/s': attn_flops(n_local) / (gated_ms * 1e-3) / 1e12,
+                           'what': 'VoltaMma-gated (with lse) + gated backward, gate bias 1.0, '
+                                   'this GPU\'s sequences'},
             'kernels': {'fwd_ms': fwd_ms, 'fwd_tflops': fwd_tf, 'fwd_frac': fwd_tf / peak,
                         'bwd_ms': bwd_ms, 'bwd_tflops': bwd_tf, 'bwd_frac': bwd_tf / peak,
                         'sequences_per_gpu': n_local},

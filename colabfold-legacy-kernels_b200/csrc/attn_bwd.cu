@@ -723,6 +723,79 @@ __global__ void row_delta_kernel(const T* __restrict__ out, const T* __restrict_
     nlse[r] = -lse[r];
 }
 
+// The gated backward's prologue (the attention output is y = o * s, s = sigmoid(gate + gate_bias)):
+// dO = dy * s, the attention gradient the main kernel differentiates; dgate = dy * o * s (1 - s)
+// = dy * y * (1 - s); the row statistic delta = sum_c o dO = sum_c y dy; and dgate_bias summed
+// over the block's 64 queries in a fixed order, then added into [H, D] with one float atomic a
+// column. Grid (ceil(Sq / 64), H, N); a block is 64 queries x D/8 threads, a thread 8 columns.
+template <typename T>
+__global__ void gate_prologue_kernel(const T* __restrict__ y, const T* __restrict__ dy,
+                                     const T* __restrict__ gate, const T* __restrict__ gate_bias,
+                                     const float* __restrict__ lse, T* __restrict__ dog,
+                                     T* __restrict__ dgate, float* __restrict__ dgate_bias,
+                                     float* __restrict__ ndelta, float* __restrict__ nlse, int H,
+                                     int Sq, int D) {
+    using E = Elem<T>;
+    extern __shared__ float gsh[];  // [64][D] dgate (float32), then [64][D/8] partial deltas
+    const int cpr = D >> 3;
+    const int tid = threadIdx.x, rloc = tid / cpr, chunk = tid - rloc * cpr, c8 = chunk * 8;
+    const int h = blockIdx.y, n = blockIdx.z, s = blockIdx.x * 64 + rloc;
+    float dg[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    float part = 0.f;
+    if (s < Sq) {
+        const long long off = (((long long)n * H + h) * Sq + s) * D + c8;
+        const uint4 yv = *reinterpret_cast<const uint4*>(y + off);
+        const uint4 dv = *reinterpret_cast<const uint4*>(dy + off);
+        const uint4 gv = *reinterpret_cast<const uint4*>(gate + off);
+        const uint4 bv = *reinterpret_cast<const uint4*>(gate_bias + (long long)h * D + c8);
+        const uint32_t yw[4] = {yv.x, yv.y, yv.z, yv.w}, dw[4] = {dv.x, dv.y, dv.z, dv.w};
+        const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
+        uint32_t ow[4], qw[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 yy = E::unpack(yw[i]), dd = E::unpack(dw[i]), gg = E::unpack(gw[i]),
+                         bb = E::unpack(bw[i]);
+            // the forward's sigmoid: 1 / (1 + 2^(-log2e (g + gb)))
+            const float s0 = __fdividef(1.f, 1.f + ex2(-kLog2e * (gg.x + bb.x)));
+            const float s1 = __fdividef(1.f, 1.f + ex2(-kLog2e * (gg.y + bb.y)));
+            ow[i] = E::pack(dd.x * s0, dd.y * s1);
+            dg[2 * i] = dd.x * yy.x * (1.f - s0);
+            dg[2 * i + 1] = dd.y * yy.y * (1.f - s1);
+            qw[i] = E::pack(dg[2 * i], dg[2 * i + 1]);
+            part = fmaf(yy.x, dd.x, part);
+            part = fmaf(yy.y, dd.y, part);
+        }
+        *reinterpret_cast<uint4*>(dog + off) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+        *reinterpret_cast<uint4*>(dgate + off) = make_uint4(qw[0], qw[1], qw[2], qw[3]);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        gsh[rloc * D + c8 + i] = dg[i];
+    }
+    float* psh = gsh + 64 * D;
+    psh[rloc * cpr + chunk] = part;
+    __syncthreads();
+    if (tid < 64) {
+        const int s2 = blockIdx.x * 64 + tid;
+        if (s2 < Sq) {
+            float d = 0.f;
+            for (int c = 0; c < cpr; ++c) {
+                d += psh[tid * cpr + c];
+            }
+            const long long row = ((long long)n * H + h) * Sq + s2;
+            ndelta[row] = -d;
+            nlse[row] = -lse[row];
+        }
+    }
+    if (tid < D) {
+        float acc = 0.f;
+        for (int r = 0; r < 64; ++r) {
+            acc += gsh[r * D + tid];
+        }
+        atomicAdd(dgate_bias + (long long)h * D + tid, acc);
+    }
+}
+
 // bt[h][k][q] = bias[h][q][k] in the bias's own 16-bit type (exact), queries padded to Sqp with
 // zeros; 32x32 tiles
 template <typename T>
@@ -777,11 +850,13 @@ bool aligned16(const void* p) {
 }
 
 // Workspace: dQ accumulator | -delta | -lse | bias^T (16-bit, queries padded to a multiple of
-// 8), each 256-byte aligned. `ok` is false when a size product overflows 64 bits.
+// 8) | (gated backward only) dO = dy * sigmoid(gate + gate_bias), 16-bit [N,H,Sq,D]; each part
+// 256-byte aligned. `ok` is false when a size product overflows 64 bits.
 struct Workspace {
-    size_t dq = 0, delta = 0, nlse = 0, bt = 0, total = 0;
+    size_t dq = 0, delta = 0, nlse = 0, bt = 0, dog = 0, total = 0;
     bool ok = false;
-    static Workspace of(uint64_t N, uint64_t H, uint64_t Sq, uint64_t Sk, uint64_t D) {
+    static Workspace of(uint64_t N, uint64_t H, uint64_t Sq, uint64_t Sk, uint64_t D,
+                        bool gated = false) {
         Workspace w;
         uint64_t rows, dqb, btb;
         const uint64_t sqp = (Sq + 7) & ~uint64_t(7);
@@ -797,7 +872,8 @@ struct Workspace {
         w.delta = align256(dqb);
         w.nlse = w.delta + align256(rows * sizeof(float));
         w.bt = w.nlse + align256(rows * sizeof(float));
-        w.total = w.bt + align256(btb);
+        w.dog = w.bt + align256(btb);
+        w.total = w.dog + (gated ? align256(dqb / 2) : 0);
         w.ok = true;
         return w;
     }
@@ -838,10 +914,20 @@ cudaError_t launch_dp(cudaStream_t stream, const CUtensorMap* maps, const BwdPar
                              : launch_main<T, DP, kDbiasNone>(stream, maps, p);
 }
 
+// The gated backward's extra buffers (all null for the plain backward)
+struct GateIO {
+    const void* gate = nullptr;       // [N,H,Sq,D]
+    const void* gate_bias = nullptr;  // [H,D]
+    void* dgate = nullptr;            // [N,H,Sq,D]
+    float* dgate_bias = nullptr;      // [H,D] float32
+    void* dog = nullptr;              // workspace: dO = dy * sigmoid(gate + gate_bias)
+};
+
 template <typename T>
 cudaError_t run_backward(cudaStream_t stream, const CUtensorMap* maps, const BwdParams& p,
                          const void* bias, void* bt, int Sqp, const void* out, const void* dout,
-                         const float* lse, float* ndelta, float* nlse, void* dq, int dbias_mode) {
+                         const float* lse, float* ndelta, float* nlse, void* dq, int dbias_mode,
+                         const GateIO* g) {
     const long long rows = (long long)p.N * p.H * p.Sq;
     cudaError_t e;
     if ((e = cudaMemsetAsync(p.dbias, 0, sizeof(float) * (size_t)p.H * p.Sq * p.Sk, stream)) !=
@@ -852,8 +938,23 @@ cudaError_t run_backward(cudaStream_t stream, const CUtensorMap* maps, const Bwd
         cudaSuccess) {
         return e;
     }
-    row_delta_kernel<T><<<(unsigned)((rows + 255) / 256), 256, 0, stream>>>(
-        static_cast<const T*>(out), static_cast<const T*>(dout), lse, ndelta, nlse, rows, p.D);
+    if (g == nullptr) {
+        row_delta_kernel<T><<<(unsigned)((rows + 255) / 256), 256, 0, stream>>>(
+            static_cast<const T*>(out), static_cast<const T*>(dout), lse, ndelta, nlse, rows, p.D);
+    } else {
+        if ((e = cudaMemsetAsync(g->dgate_bias, 0, sizeof(float) * (size_t)p.H * p.D, stream)) !=
+            cudaSuccess) {
+            return e;
+        }
+        const int cpr = p.D / 8;
+        const dim3 ggrid((p.Sq + 63) / 64, p.H, p.N);
+        gate_prologue_kernel<T><<<ggrid, 64 * cpr, (size_t)64 * (p.D + cpr) * sizeof(float),
+                                  stream>>>(
+            static_cast<const T*>(out), static_cast<const T*>(dout),
+            static_cast<const T*>(g->gate), static_cast<const T*>(g->gate_bias), lse,
+            static_cast<T*>(g->dog), static_cast<T*>(g->dgate), g->dgate_bias, ndelta, nlse, p.H,
+            p.Sq, p.D);
+    }
     const dim3 tgrid((Sqp + 31) / 32, (p.Sk + 31) / 32, p.H);
     bias_transpose_kernel<T><<<tgrid, dim3(32, 8), 0, stream>>>(static_cast<const T*>(bias),
                                                                  static_cast<T*>(bt), p.Sq, p.Sk,
@@ -902,13 +1003,15 @@ extern "C" int cflk_volta_mma_bwd_workspace_size(int64_t N, int64_t H, int64_t S
     return kOk;
 }
 
-extern "C" int cflk_volta_mma_bwd(void* stream_, int dtype, const void* q, const void* k,
-                                  const void* v, const void* bias, const uint8_t* kmask,
-                                  const void* out, const void* dout, const float* lse, void* dq,
-                                  void* dk, void* dv, float* dbias, void* workspace,
-                                  size_t workspace_bytes, int64_t N, int64_t H, int64_t Sq,
-                                  int64_t Sk, int64_t D, float scale, int want_dbias) {
-    clear_error();
+namespace cflk {
+namespace {
+
+// VoltaMmaBwd, and with g the gated backward: out is then the gated output y, dout dy.
+int backward(void* stream_, int dtype, const void* q, const void* k, const void* v,
+             const void* bias, const uint8_t* kmask, const void* out, const void* dout,
+             const float* lse, void* dq, void* dk, void* dv, float* dbias, void* workspace,
+             size_t workspace_bytes, int64_t N, int64_t H, int64_t Sq, int64_t Sk, int64_t D,
+             float scale, int want_dbias, GateIO* g) {
     cudaStream_t stream = static_cast<cudaStream_t>(stream_);
     if (dtype != kF16 && dtype != kBF16) {
         return fail(kInvalidArgument, "volta_mma_bwd: dtype must be f16 or bf16");
@@ -932,9 +1035,14 @@ extern "C" int cflk_volta_mma_bwd(void* stream_, int dtype, const void* q, const
                         "volta_mma_bwd: more than 2^31 (key tile, query step) pairs");
         }
     }
-    const Workspace ws = Workspace::of(N, H, Sq, Sk, D);
+    const Workspace ws = Workspace::of(N, H, Sq, Sk, D, g != nullptr);
     if (!ws.ok) {
         return fail(kInvalidArgument, "volta_mma_bwd: sizes overflow the workspace size");
+    }
+    if (g != nullptr &&
+        (!aligned16(g->gate) || !aligned16(g->gate_bias) || !aligned16(g->dgate) ||
+         g->dgate_bias == nullptr)) {
+        return fail(kInvalidArgument, "volta_mma_gated_bwd: gate buffers must be 16-byte aligned");
     }
     if (workspace_bytes < ws.total || (ws.total > 0 && workspace == nullptr) ||
         (reinterpret_cast<uintptr_t>(workspace) & 255) != 0) {
@@ -963,10 +1071,21 @@ extern "C" int cflk_volta_mma_bwd(void* stream_, int dtype, const void* q, const
             cudaMemsetAsync(dk, 0, (size_t)N * H * Sk * D * 2, stream);
             cudaMemsetAsync(dv, 0, (size_t)N * H * Sk * D * 2, stream);
         }
+        if (g != nullptr) {
+            if (rows > 0) {
+                cudaMemsetAsync(g->dgate, 0, rows * D * 2, stream);
+            }
+            if (H > 0) {
+                cudaMemsetAsync(g->dgate_bias, 0, sizeof(float) * (size_t)H * D, stream);
+            }
+        }
         const cudaError_t e = cudaGetLastError();
         return e == cudaSuccess ? kOk
                                 : fail(kInternal, std::string("volta_mma_bwd launch: ") +
                                                       cudaGetErrorString(e));
+    }
+    if (g != nullptr) {
+        g->dog = wsb + ws.dog;
     }
     const CUtensorMapDataType tdt =
         dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -987,7 +1106,7 @@ extern "C" int cflk_volta_mma_bwd(void* stream_, int dtype, const void* q, const
         if (!encode_tiled(&maps[0], tdt, 2, 4, q, dq4, sq4, boxq, sw) ||
             !encode_tiled(&maps[1], tdt, 2, 4, k, dk4, sk4, boxk, sw) ||
             !encode_tiled(&maps[2], tdt, 2, 4, v, dk4, sk4, boxk, sw) ||
-            !encode_tiled(&maps[3], tdt, 2, 4, dout, dq4, sq4, boxq, sw) ||
+            !encode_tiled(&maps[3], tdt, 2, 4, g != nullptr ? g->dog : dout, dq4, sq4, boxq, sw) ||
             !encode_tiled(&maps[4], tdt, 2, 3, bt, dbt, sbt, boxbt, CU_TENSOR_MAP_SWIZZLE_128B)) {
             return fail(kInvalidArgument, "volta_mma_bwd: TMA descriptor rejected");
         }
@@ -1020,13 +1139,59 @@ extern "C" int cflk_volta_mma_bwd(void* stream_, int dtype, const void* q, const
     p.scale = scale;
     const cudaError_t e =
         dtype == kBF16 ? run_backward<__nv_bfloat16>(stream, maps, p, bias, bt, Sqp, out, dout,
-                                                     lse, ndelta, nlse, dq, dbias_mode)
+                                                     lse, ndelta, nlse, dq, dbias_mode, g)
                        : run_backward<__half>(stream, maps, p, bias, bt, Sqp, out, dout, lse,
-                                              ndelta, nlse, dq, dbias_mode);
+                                              ndelta, nlse, dq, dbias_mode, g);
     if (e != cudaSuccess) {
         return fail(kInternal, std::string("volta_mma_bwd launch: ") + cudaGetErrorString(e));
     }
     return kOk;
+}
+
+}  // namespace
+}  // namespace cflk
+
+extern "C" int cflk_volta_mma_bwd(void* stream, int dtype, const void* q, const void* k,
+                                  const void* v, const void* bias, const uint8_t* kmask,
+                                  const void* out, const void* dout, const float* lse, void* dq,
+                                  void* dk, void* dv, float* dbias, void* workspace,
+                                  size_t workspace_bytes, int64_t N, int64_t H, int64_t Sq,
+                                  int64_t Sk, int64_t D, float scale, int want_dbias) {
+    clear_error();
+    return backward(stream, dtype, q, k, v, bias, kmask, out, dout, lse, dq, dk, dv, dbias,
+                    workspace, workspace_bytes, N, H, Sq, Sk, D, scale, want_dbias, nullptr);
+}
+
+extern "C" int cflk_volta_mma_gated_bwd_workspace_size(int64_t N, int64_t H, int64_t Sq,
+                                                       int64_t Sk, int64_t D, size_t* bytes) {
+    clear_error();
+    if (N < 0 || H < 0 || Sq < 0 || Sk < 0 || D < 0 || bytes == nullptr) {
+        return fail(kInvalidArgument, "volta_mma_gated_bwd: bad sizes");
+    }
+    const Workspace ws = Workspace::of(N, H, Sq, Sk, D, true);
+    if (!ws.ok) {
+        return fail(kInvalidArgument, "volta_mma_gated_bwd: sizes overflow the workspace size");
+    }
+    *bytes = ws.total;
+    return kOk;
+}
+
+extern "C" int cflk_volta_mma_gated_bwd(void* stream, int dtype, const void* q, const void* k,
+                                        const void* v, const void* gate, const void* gate_bias,
+                                        const void* bias, const uint8_t* kmask, const void* y,
+                                        const void* dy, const float* lse, void* dq, void* dk,
+                                        void* dv, void* dgate, float* dgate_bias, float* dbias,
+                                        void* workspace, size_t workspace_bytes, int64_t N,
+                                        int64_t H, int64_t Sq, int64_t Sk, int64_t D,
+                                        float scale, int want_dbias) {
+    clear_error();
+    GateIO g;
+    g.gate = gate;
+    g.gate_bias = gate_bias;
+    g.dgate = dgate;
+    g.dgate_bias = dgate_bias;
+    return backward(stream, dtype, q, k, v, bias, kmask, y, dy, lse, dq, dk, dv, dbias,
+                    workspace, workspace_bytes, N, H, Sq, Sk, D, scale, want_dbias, &g);
 }
 
 // ---------------------------------------------------------------------------------------------

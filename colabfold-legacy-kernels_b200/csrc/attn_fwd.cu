@@ -918,3 +918,22 @@ extern "C" int cflk_volta_mma_packed(void* stream, int dtype, const void* p, con
                         kmask, out, nullptr, lay, (int)N, (int)H, (int)S, (int)S, (int)D, scale,
                         false, lims ? "volta_mma_packed_trim" : "volta_mma_packed");
 }
+
+extern "C" int cflk_volta_mma_gated(void* stream, int dtype, const void* q, const void* k,
+                                    const void* v, const void* gate, const void* gate_bias,
+                                    const void* bias, const uint8_t* kmask, void* out, float* lse,
+                                    int64_t N, int64_t H, int64_t Sq, int64_t Sk, int64_t D,
+                                    float scale, int want_lse) {
+    clear_error();
+    if (N < 0 || H < 0 || Sq < 0 || Sk < 0 || D < 0) {
+        return fail(kInvalidArgument, "q must be [N,H,S,D]");
+    }
+    if (gate == nullptr || gate_bias == nullptr) {
+        return fail(kInvalidArgument, "volta_mma_gated: gate [N,H,Sq,D] and gate_bias [H,D]");
+    }
+    // the gate shares q's layout [N,H,Sq,D]
+    const Layout4 lay{H * Sq * D, Sq * D, D, H * Sk * D, Sk * D, D, H * Sq * D, Sq * D, D};
+    return attn_forward(static_cast<cudaStream_t>(stream), dtype, q, k, v, gate, gate_bias,
+                        nullptr, bias, kmask, out, want_lse ? lse : nullptr, lay, (int)N, (int)H,
+                        (int)Sq, (int)Sk, (int)D, scale, want_lse != 0, "volta_mma_gated");
+}

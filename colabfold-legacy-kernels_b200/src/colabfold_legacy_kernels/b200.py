@@ -29,6 +29,12 @@ _SIGS = {
     'cflk_volta_mma_bwd_workspace_size': [_i64, _i64, _i64, _i64, _i64, _C.POINTER(_C.c_size_t)],
     'cflk_volta_mma_bwd': [_p, _int, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p,
                            _C.c_size_t, _i64, _i64, _i64, _i64, _i64, _f32, _int],
+    'cflk_volta_mma_gated': [_p, _int, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64,
+                             _i64, _i64, _f32, _int],
+    'cflk_volta_mma_gated_bwd_workspace_size': [_i64, _i64, _i64, _i64, _i64,
+                                                _C.POINTER(_C.c_size_t)],
+    'cflk_volta_mma_gated_bwd': [_p, _int] + [_p] * 17 + [_C.c_size_t, _i64, _i64, _i64, _i64,
+                                                          _i64, _f32, _int],
     'cflk_volta_ln_gdp': [_p, _int, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64,
                           _f32],
     'cflk_volta_trimul_epilogue': [_p, _int, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p,
@@ -184,6 +190,56 @@ def volta_mma_bwd(q, k, v, bias, kmask, out, dout, lse, *, scale, want_dbias=Tru
                                   float(scale), int(bool(want_dbias)))
     _check(rc, 'volta_mma_bwd')
     return dq, dk, dv, dbias
+
+
+def volta_mma_gated(q, k, v, gate, gate_bias, bias, kmask, *, scale, want_lse=True, out=None,
+                    lse=None):
+    """Gated attention: (y [N,H,Sq,D] = attention * sigmoid(gate + gate_bias[h]), lse)."""
+    if q.dim() != 4 or gate.shape != q.shape:
+        raise ValueError('q and gate must be [N,H,S,D]')
+    N, H, Sq, D = q.shape
+    Sk = k.shape[2]
+    if tuple(gate_bias.shape) != (H, D):
+        raise ValueError('volta_mma_gated: gate_bias must be [H,D]')
+    dt = _dtype_code(q, k, v, gate, gate_bias, bias)
+    if out is None:
+        out = torch.empty_like(q)
+    if lse is None:
+        lse = torch.empty((N, H, Sq) if want_lse else (1,), dtype=torch.float32, device=q.device)
+    rc = lib().cflk_volta_mma_gated(_stream(), dt, _ptr(q), _ptr(k), _ptr(v), _ptr(gate),
+                                    _ptr(gate_bias), _ptr(bias), _ptr(kmask), _ptr(out), _ptr(lse),
+                                    N, H, Sq, Sk, D, float(scale), int(bool(want_lse)))
+    _check(rc, 'volta_mma_gated')
+    return out, lse
+
+
+def volta_mma_gated_bwd(q, k, v, gate, gate_bias, bias, kmask, y, dy, lse, *, scale,
+                        want_dbias=True):
+    """Gradients of volta_mma_gated: (dq, dk, dv, dgate, dgate_bias [H,D] float32,
+    dbias [H,Sq,Sk] float32)."""
+    if q.dim() != 4 or gate.shape != q.shape or y.shape != q.shape or dy.shape != q.shape:
+        raise ValueError('volta_mma_gated_bwd: q, gate, y and dy must be [N,H,Sq,D]')
+    N, H, Sq, D = q.shape
+    Sk = k.shape[2]
+    if v.shape != k.shape or tuple(lse.shape) != (N, H, Sq) or tuple(bias.shape) != (H, Sq, Sk):
+        raise ValueError('volta_mma_gated_bwd: shapes do not match')
+    if tuple(gate_bias.shape) != (H, D):
+        raise ValueError('volta_mma_gated_bwd: gate_bias must be [H,D]')
+    dt = _dtype_code(q, k, v, gate, gate_bias, bias, y, dy)
+    dq, dk, dv, dgate = (torch.empty_like(t) for t in (q, k, v, gate))
+    dgate_bias = torch.empty((H, D), dtype=torch.float32, device=q.device)
+    dbias = torch.empty((H, Sq, Sk), dtype=torch.float32, device=q.device)
+    n = _C.c_size_t(0)
+    _check(lib().cflk_volta_mma_gated_bwd_workspace_size(N, H, Sq, Sk, D, _C.byref(n)),
+           'volta_mma_gated_bwd')
+    ws = torch.empty(max(n.value, 1), dtype=torch.uint8, device=q.device)
+    rc = lib().cflk_volta_mma_gated_bwd(
+        _stream(), dt, _ptr(q), _ptr(k), _ptr(v), _ptr(gate), _ptr(gate_bias), _ptr(bias),
+        _ptr(kmask), _ptr(y), _ptr(dy), _f32_ptr(lse, 'lse', 'volta_mma_gated_bwd'), _ptr(dq),
+        _ptr(dk), _ptr(dv), _ptr(dgate), _ptr(dgate_bias), _ptr(dbias), _ptr(ws), n.value, N, H,
+        Sq, Sk, D, float(scale), int(bool(want_dbias)))
+    _check(rc, 'volta_mma_gated_bwd')
+    return dq, dk, dv, dgate, dgate_bias, dbias
 
 
 # ---- fused pair-stack ops -------------------------------------------------------------------

@@ -111,6 +111,40 @@ CFLK_API int cflk_volta_mma_bwd_noalloc(void* stream, int dtype, const void* q, 
                                         int64_t H, int64_t Sq, int64_t Sk, int64_t D,
                                         float scale, int want_dbias);
 
+/* ---- gated attention training path (no counterpart in the reference) ------------------ */
+/* The reference applies the gate of gated attention only in its forward-only packed targets;
+ * for training it composes VoltaMma, an elementwise gate in XLA and VoltaMmaBwd
+ * (cuda/volta_mma_attn.cu:544-575 for the gate's form). These two entry points fuse the gate.
+ *
+ * cflk_volta_mma_gated: y = attention(q, k, v, bias, kmask) * sigmoid(gate + gate_bias[h, c]),
+ * with the log2-domain lse of the attention as cflk_volta_mma returns it (want_lse as there).
+ * gate [N,H,Sq,D] (q's layout), gate_bias [H,D], both 16-bit; other arguments as cflk_volta_mma
+ * (no tile hints). */
+CFLK_API int cflk_volta_mma_gated(void* stream, int dtype, const void* q, const void* k,
+                                  const void* v, const void* gate, const void* gate_bias,
+                                  const void* bias, const uint8_t* kmask, void* out, float* lse,
+                                  int64_t N, int64_t H, int64_t Sq, int64_t Sk, int64_t D,
+                                  float scale, int want_lse);
+
+/* Workspace bytes of cflk_volta_mma_gated_bwd: that of cflk_volta_mma_bwd plus a 16-bit
+ * [N,H,Sq,D] buffer for dy * sigmoid(gate + gate_bias). */
+CFLK_API int cflk_volta_mma_gated_bwd_workspace_size(int64_t N, int64_t H, int64_t Sq,
+                                                     int64_t Sk, int64_t D, size_t* bytes);
+
+/* The gradients of cflk_volta_mma_gated: given y (its output), dy and lse, dq, dk, dv and dbias
+ * as cflk_volta_mma_bwd gives them for the attention, dgate [N,H,Sq,D] (16-bit) =
+ * dy * y * (1 - sigmoid(gate + gate_bias)) and dgate_bias [H,D] float32 = dgate summed over the
+ * batch and the queries (accumulated with float atomics: like dq and dbias, equal run to run
+ * within float rounding; dk and dv are bitwise deterministic). */
+CFLK_API int cflk_volta_mma_gated_bwd(void* stream, int dtype, const void* q, const void* k,
+                                      const void* v, const void* gate, const void* gate_bias,
+                                      const void* bias, const uint8_t* kmask, const void* y,
+                                      const void* dy, const float* lse, void* dq, void* dk,
+                                      void* dv, void* dgate, float* dgate_bias, float* dbias,
+                                      void* workspace, size_t workspace_bytes, int64_t N,
+                                      int64_t H, int64_t Sq, int64_t Sk, int64_t D, float scale,
+                                      int want_dbias);
+
 /* ---- LayerNorm-folded pair-stack fusions ------------------------------------------------ */
 /* keep [M] (16-bit) or NULL: per row tile, compute when a row of keep is above zero, write
  * padding (zeros, or nothing where the output aliases its input) when the tile is all zero,

@@ -115,6 +115,25 @@ def attention_forward_f32(q, k, v, bias, kmask, scale):
     return np.matmul(p, v), (np.log(l) + mx)[..., 0] * f(LOG2E)
 
 
+def gated_attention_grads(q, k, v, gate, gate_bias, bias, kmask, dy, scale):
+    """The gated attention y = o * sigmoid(gate + gate_bias[h]) (o = the attention output,
+    gate [N,H,Sq,D], gate_bias [H,D]) and its gradients, float64: (y, lse2, dq, dk, dv, dgate,
+    dgate_bias [H,D], dbias [H,Sq,Sk]).
+
+    The reference composes this from VoltaMma (o, lse), an XLA gate and VoltaMmaBwd
+    (cuda/volta_mma_attn.cu:544-575 applies the same gate in its forward-only packed targets);
+    this is the autodiff of that composition: dO = dy * s with s = sigmoid(gate + gate_bias),
+    the attention gradients from attention_grads with dout = dO, dgate = dy * o * s * (1 - s),
+    dgate_bias = dgate summed over the batch and the queries.
+    """
+    g = np.asarray(gate, np.float64) + np.asarray(gate_bias, np.float64)[None, :, None, :]
+    s = 1.0 / (1.0 + np.exp(-g))
+    dy = np.asarray(dy, np.float64)
+    o, lse2, dq, dk, dv, dbias = attention_grads(q, k, v, bias, kmask, dy * s, scale)
+    dgate = dy * o * s * (1.0 - s)
+    return o * s, lse2, dq, dk, dv, dgate, dgate.sum(axis=(0, 2)), dbias
+
+
 def trim_limits(kmask):
     """lims [N+1]: each batch row's last live key + 1, then their maximum
     (tests/test_packed_attention.py:53-57)."""

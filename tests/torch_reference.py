@@ -75,3 +75,14 @@ def grads(q, k, v, bias, kmask, dout, scale, chunk=16):
             dbias += ds.sum(0)
     return (torch.cat(outs), torch.cat(lses), torch.cat(dqs), torch.cat(dks), torch.cat(dvs),
             dbias)
+
+
+def gated_grads(q, k, v, gate, gate_bias, bias, kmask, dy, scale, chunk=16):
+    """The gated attention y = o * sigmoid(gate + gate_bias[h]) and its gradients in float32:
+    (y, lse2, dq, dk, dv, dgate, dgate_bias [H,D], dbias), the autodiff of the composition the
+    reference's callers build from VoltaMma, an elementwise gate and VoltaMmaBwd."""
+    s = torch.sigmoid(gate.float() + gate_bias.float()[None, :, None, :])
+    dyf = dy.float()
+    o, lse, dq, dk, dv, dbias = grads(q, k, v, bias, kmask, dyf * s, scale, chunk)
+    dgate = dyf * o * s * (1.0 - s)
+    return o * s, lse, dq, dk, dv, dgate, dgate.sum(dim=(0, 2)), dbias

@@ -70,7 +70,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Wait for the phase with the given parity to complete, for at most kWaitLimitNs. On a timeout
+// The same test with a suspend-time hint: a thread whose phase is not complete is suspended until
+// the phase completes or hint_ns nanoseconds pass (it does not spin on the issue slots).
+__device__ __forceinline__ bool mbar_try_wait_hint(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
+// Wait for the phase with the given parity to complete, for at most kWaitLimitNs. After a first
+// test the thread waits suspended (a 1 ms hint, woken when the phase completes) rather than
+// spinning, so waiting warps leave the issue slots to the working ones. On a timeout
 // set `code` in *status and return false. A set *abort (shared memory) makes the wait give up at
 // once: one timeout in a CTA is enough to know its data are bad.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned* status,
@@ -82,10 +98,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
     }
     const unsigned long long t0 = globaltimer();
     while (true) {
-        for (int i = 0; i < 32; ++i) {
-            if (mbar_try_wait(b, parity)) {
-                return true;
-            }
+        if (mbar_try_wait_hint(b, parity, 1000000u)) {
+            return true;
         }
         if ((abort != nullptr && *abort) || globaltimer() - t0 > limit_ns) {
             atomicOr(status, code);

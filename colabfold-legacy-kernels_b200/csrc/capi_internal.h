@@ -1,6 +1,7 @@
 // Status codes, dtype codes and the last-error message shared by the C-ABI entry points.
 #pragma once
 
+#include <cstdint>
 #include <string>
 
 namespace cflk {
@@ -20,5 +21,11 @@ void clear_error();
 unsigned read_and_clear_status_fwd();
 unsigned read_and_clear_status_bwd();
 unsigned read_and_clear_status_fused();
+unsigned read_and_clear_status_gemm();
+
+// VoltaGdp through the tile GEMM (widths the resident-weight row-tile kernel does not take)
+int gdp_general(void* stream, int dtype, const void* x, const void* wp, const void* bp,
+                const void* wg, const void* bg, const void* mask, void* out, int64_t M,
+                int64_t K, int64_t N, int64_t activation);
 
 }  // namespace cflk

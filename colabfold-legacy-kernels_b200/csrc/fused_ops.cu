@@ -2290,15 +2290,16 @@ extern "C" int cflk_volta_gdp(void* stream, int dtype, const void* x, const void
     if (N % 8) {
         return fail(kInvalidArgument, "gdp: N must be a multiple of 8");
     }
-    if ((K != 64 && K != 128) || (N != 64 && N != 128)) {
-        return fail(kInvalidArgument, "gdp: this library takes K and N of 64 or 128");
-    }
     if (M == 0) {
         return kOk;
     }
     if (!aligned16(x) || !aligned16(wp) || !aligned16(wg) || !aligned16(out) || bp == nullptr ||
         bg == nullptr || mask == nullptr) {
         return fail(kInvalidArgument, "gdp: buffers must be 16-byte aligned");
+    }
+    if ((K != 64 && K != 128) || (N != 64 && N != 128)) {
+        // other widths: the tile GEMM (K a multiple of 8, N of 8)
+        return gdp_general(stream, dtype, x, wp, bp, wg, bg, mask, out, M, K, N, activation);
     }
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     cudaError_t e;

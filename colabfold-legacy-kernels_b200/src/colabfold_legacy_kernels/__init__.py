@@ -10,9 +10,9 @@ repository's sm_100a sources. That library exports plain C-ABI entry points
 `symbol(kernel, 100)` names the XLA FFI target that a JAX caller registers for the kernel (the
 reference's own target name). The handler behind that target is a thin shim over the C entry
 point, compiled against XLA's FFI headers by the caller's build; this package does not ship it,
-because the headers are not part of this build's toolchain. The outer-product-mean kernels have
-no cc=100 entry yet, so `available(100)` without a kernel is False while
-`available(100, 'attention')` is True once the library is built.
+because the headers are not part of this build's toolchain. The outer-product
+mean's outer kernel (opm_outer) has no cc=100 entry yet, so `available(100)` without a kernel is
+False while `available(100, 'attention')` is True once the library is built.
 """
 
 from pathlib import Path
@@ -83,6 +83,7 @@ _TABLE = {
         (70, "libvolta_gdp_wmma.so", "VoltaTransitionWmma"),
     ),
     "opm_update": (
+        (100, _SM100_LIB, "VoltaOpmUpdate"),
         (75, "libvolta_ops.so", "VoltaOpmUpdate"),
         (70, "libvolta_gdp_wmma.so", "VoltaOpmUpdateWmma"),
     ),
@@ -103,6 +104,7 @@ _C_SYMBOLS = {
     "VoltaTransition": "cflk_volta_transition",
     "VoltaLayerNorm": "cflk_volta_layer_norm",
     "VoltaGdp": "cflk_volta_gdp",
+    "VoltaOpmUpdate": "cflk_volta_opm_update",
 }
 
 KERNELS = tuple(_TABLE)

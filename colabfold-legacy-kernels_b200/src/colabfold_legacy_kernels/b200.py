@@ -46,6 +46,8 @@ _SIGS = {
                               _f32, _int],
     'cflk_volta_layer_norm': [_p, _int, _p, _p, _p, _p, _i64, _i64, _f32],
     'cflk_volta_gdp': [_p, _int, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64],
+    'cflk_volta_opm_update': [_p, _int, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _f32],
+    'cflk_trimul_contract': [_p, _int, _p, _p, _p, _i64, _i64, _i64, _i64, _int],
 }
 
 _lib = None
@@ -263,6 +265,64 @@ def volta_gdp(x, wp, bp, wg, bg, mask, *, activation=0, out=None):
         return out
     rc = lib().cflk_volta_gdp(_stream(), dt, _ptr(x), _ptr(wp), _ptr(bp), _ptr(wg), _ptr(bg),
                               _ptr(mask), _ptr(out), M, K, N, int(activation))
+    _check(rc, who)
+    return out
+
+
+def volta_opm_update(lhs, t, bias, norm, residual=None, *, eps, out=None):
+    """VoltaOpmUpdate: out [B,D,F] = (lhs @ t[:, d, :] + bias) / (eps + norm[b, d]) (+ residual);
+    lhs [B,K], t [K,D,F], bias [F] and norm [B,D] float32, residual [B,D,F] or None."""
+    who = 'opm_update'
+    if lhs.dim() != 2 or t.dim() != 3 or t.shape[0] != lhs.shape[1]:
+        raise ValueError('opm_update: lhs must be [B,K] and t [K,D,F]')
+    B, K = lhs.shape
+    _, D, F = t.shape
+    if K % 32 or F not in (16, 32, 64, 128) or D > 65535:
+        raise ValueError(
+            'opm_update: K must be a multiple of 32, F 16, 32, 64 or 128, D at most 65535')
+    if (bias.numel() != F or norm.numel() != B * D or
+            (residual is not None and residual.numel() != B * D * F)):
+        raise ValueError('opm_update: shapes do not match')
+    dt = _dtype_code(lhs, t, *(() if residual is None else (residual,)))
+    if out is None:
+        out = torch.empty((B, D, F), dtype=lhs.dtype, device=lhs.device)
+    if out.numel() != B * D * F or out.dtype != lhs.dtype:
+        raise ValueError('opm_update: shapes do not match')
+    if B == 0 or D == 0:
+        return out
+    rc = lib().cflk_volta_opm_update(_stream(), dt, _ptr(lhs), _ptr(t),
+                                     _f32_ptr(bias, 'bias', who), _f32_ptr(norm, 'norm', who),
+                                     _ptr(residual), _ptr(out), B, K, D, F, float(eps))
+    _check(rc, who)
+    return out
+
+
+def trimul_contract(a, b, *, incoming=False, out=None):
+    """The triangle multiplication's contraction, float32 out [C,I,J]: outgoing
+    out[c,i,j] = sum_k a[c,i,k] b[c,j,k] (a [C,I,K], b [C,J,K]); incoming
+    out[c,i,j] = sum_k a[c,k,i] b[c,k,j] (a [C,K,I], b [C,K,J])."""
+    who = 'trimul_contract'
+    if a.dim() != 3 or b.dim() != 3 or a.shape[0] != b.shape[0]:
+        raise ValueError('trimul_contract: a and b must be [C,*,*] with the same C')
+    if incoming:
+        C, K, I = a.shape
+        if b.shape[1] != K:
+            raise ValueError('trimul_contract: a [C,K,I] and b [C,K,J] must share K')
+        J = b.shape[2]
+    else:
+        C, I, K = a.shape
+        if b.shape[2] != K:
+            raise ValueError('trimul_contract: a [C,I,K] and b [C,J,K] must share K')
+        J = b.shape[1]
+    dt = _dtype_code(a, b)
+    if out is None:
+        out = torch.empty((C, I, J), dtype=torch.float32, device=a.device)
+    if out.dtype != torch.float32 or out.numel() != C * I * J:
+        raise ValueError('trimul_contract: out must be float32 [C,I,J]')
+    if C == 0 or I == 0 or J == 0:
+        return out
+    rc = lib().cflk_trimul_contract(_stream(), dt, _ptr(a), _ptr(b), _ptr(out), C, I, J, K,
+                                    int(bool(incoming)))
     _check(rc, who)
     return out
 

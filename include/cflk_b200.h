@@ -207,11 +207,39 @@ CFLK_API int cflk_volta_layer_norm(void* stream, int dtype, const void* x, const
 
 /* VoltaGdp: out [M,N] = mask * (x wp + bp) * act(x wg + bg), act = sigmoid (activation 0) or
  * swish g * sigmoid(g) (1), the row mask unclamped. x [M,K]; wp, wg [K,N] row-major; bp, bg
- * [N]; mask [M]. This library takes K and N of 64 or 128 (the reference: any K, N % 8 == 0).
- * Replaces VoltaGdp, cuda/volta_ops.cu:108-205,212-265. */
+ * [N]; mask [M]. Any K >= 1 and N % 8 == 0, as the reference: K and N of 64 or 128 run the
+ * resident-weight row-tile kernel, other widths the persistent tcgen05 tile GEMM with both
+ * products in one pass (K % 8 == 0) or, for K % 8 != 0, a CUDA-core tile kernel. x, wp, wg and
+ * out 16-byte aligned. Replaces VoltaGdp, cuda/volta_ops.cu:108-205,212-265. */
 CFLK_API int cflk_volta_gdp(void* stream, int dtype, const void* x, const void* wp,
                             const void* bp, const void* wg, const void* bg, const void* mask,
                             void* out, int64_t M, int64_t K, int64_t N, int64_t activation);
+
+/* VoltaOpmUpdate: out [B,D,F] = (lhs @ t[:, d, :] + bias) / (eps + norm[b, d]) (+ residual when
+ * residual is not NULL). lhs [B,K] and t [K,D,F] 16-bit, bias [F] and norm [B,D] float32,
+ * residual and out [B,D,F] 16-bit (out may be the residual's buffer). K a multiple of 32, F 16, 32, 64 or 128, D at most 65535 (the
+ * reference's limits); lhs, t, residual and out 16-byte aligned. One persistent tcgen05 tile GEMM
+ * (128 x 128 output tiles, the epilogue fused). Replaces VoltaOpmUpdate,
+ * cuda/volta_fused_ffi.h:261-298, kernel cuda/volta_ops.cu:647-699. */
+CFLK_API int cflk_volta_opm_update(void* stream, int dtype, const void* lhs, const void* t,
+                                   const float* bias, const float* norm, const void* residual,
+                                   void* out, int64_t B, int64_t K, int64_t D, int64_t F,
+                                   float eps);
+
+/* The triangle multiplication's contraction between VoltaLnGdp and VoltaTrimulEpilogue (in the
+ * reference an XLA einsum with a float32 result, tests/test_fused.py:135): for each channel c,
+ *   incoming = 0 (AF2's outgoing edges): out[c,i,j] = sum_k a[c,i,k] b[c,j,k], a [C,I,K], b [C,J,K];
+ *   incoming = 1 (incoming edges):       out[c,i,j] = sum_k a[c,k,i] b[c,k,j], a [C,K,I], b [C,K,J]
+ * (AF2's incoming form passes its right projection as a and its left as b). a and b 16-bit
+ * (the channel-major left/right that VoltaLnGdp writes), out [C,I,J] float32 (the x_cm that
+ * VoltaTrimulEpilogue reads). Products accumulate in float32. The persistent tcgen05 tile GEMM
+ * (128 x 128 tiles of one channel, K- or MN-major operands through TMA) runs when the rows are
+ * 16-byte multiples (K % 8 == 0, or I % 8 == 0 and J % 8 == 0 for incoming; J % 4 == 0) and the
+ * buffers 16-byte aligned; other sizes run a CUDA-core tile kernel. C at most 65535. No reference
+ * kernel: the reference's callers run this einsum in XLA. */
+CFLK_API int cflk_trimul_contract(void* stream, int dtype, const void* a, const void* b,
+                                  float* out, int64_t C, int64_t I, int64_t J, int64_t K,
+                                  int incoming);
 
 /* ---- diagnostics (no counterpart in the reference) ------------------------------------- */
 

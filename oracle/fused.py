@@ -78,15 +78,27 @@ def opm_update(lhs, t, bias, norm, residual, eps, dtype):
     """VoltaOpmUpdate (cuda/volta_fused_ffi.h:261-298, kernel cuda/volta_ops.cu:647-699):
     out [B, D, F] = (lhs @ t[:, d, :] + bias) / (eps + norm[b, d]) (+ residual), lhs [B, K],
     t [K, D, F], bias [F] and norm [B, D] float32; products in float32, the result rounded to
-    `dtype`; float64 out. No cc=100 kernel yet: the oracle for the next row."""
+    `dtype`; float64 out."""
     l32 = np.asarray(lhs, np.float32)
     t32 = np.asarray(t, np.float32)
-    prod = np.einsum('bk,kdf->bdf', l32, t32).astype(np.float32)
+    K, D, F = t32.shape
+    prod = (l32 @ t32.reshape(K, D * F)).reshape(-1, D, F)
     den = np.float32(eps) + np.asarray(norm, np.float32)[:, :, None]
     out = (prod + np.asarray(bias, np.float32)) / den
     if residual is not None:
         out = out + np.asarray(residual, np.float32)
     return round_to(out.astype(np.float64), dtype)
+
+
+def trimul_contract(a, b, incoming):
+    """The triangle multiplication's contraction (tests/test_fused.py:135 of the reference, an
+    XLA einsum with preferred_element_type float32): outgoing einsum('cik,cjk->cij'), incoming
+    einsum('cki,ckj->cij'); float64 sums of the 16-bit inputs, float64 out."""
+    a64 = np.asarray(a, np.float64)
+    b64 = np.asarray(b, np.float64)
+    if incoming:
+        return np.einsum('cki,ckj->cij', a64, b64, optimize=True)
+    return np.einsum('cik,cjk->cij', a64, b64, optimize=True)
 
 
 def opm_outer(left, right, wT, dtype):

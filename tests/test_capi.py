@@ -118,7 +118,7 @@ def test_resolver_capabilities():
     assert clk.supported_capabilities() == (70, 75, 100)
     for k in ('attention', 'attention_bwd', 'ln_gated_dual_proj', 'trimul_epilogue',
               'ln_projection', 'output_projection', 'transition', 'layer_norm',
-              'gated_dual_proj'):
+              'gated_dual_proj', 'opm_update'):
         assert clk.available(100, k)
         assert clk.library_path(k, 100).endswith('sm100/libcflk_sm100.so')
     assert clk.symbol('attention', 100) == 'VoltaMma'
@@ -129,15 +129,17 @@ def test_resolver_capabilities():
     assert clk.symbol('attention', 75) == 'VoltaMma'
     assert clk.symbol('attention', 70) == 'VoltaWmma'
     assert clk.symbol('transition', 70) == 'VoltaTransitionWmma'
-    # out-of-scope kernels have no cc=100 library, so the all-kernel check is False
+    # opm_outer has no cc=100 entry yet, so the all-kernel check is False
     assert not clk.available(100)
     assert not clk.available(100, 'opm_outer')
     assert not clk.available(80)
     assert clk.symbol('layer_norm', 100) == 'VoltaLayerNorm'
     assert clk.c_symbol('layer_norm', 100) == 'cflk_volta_layer_norm'
     assert clk.symbol('gated_dual_proj', 100) == 'VoltaGdp'
+    assert clk.symbol('opm_update', 100) == 'VoltaOpmUpdate'
+    assert clk.c_symbol('opm_update', 100) == 'cflk_volta_opm_update'
     with pytest.raises(FileNotFoundError):
-        clk.symbol('opm_update', 100)
+        clk.symbol('opm_outer', 100)
     with pytest.raises(KeyError):
         clk.library_path('nonexistent', 100)
     assert clk.kernel_dir(100).endswith('sm100')

@@ -122,10 +122,32 @@ def test_gdp_refusals(cuda_device):
     m = torch.ones(10, dtype=torch.bfloat16, device=d)
     with pytest.raises(ValueError, match='activation is 0'):
         b200().volta_gdp(x, w, b, w, b, m, activation=2)
-    w3 = torch.zeros(128, 96, dtype=torch.bfloat16, device=d)
-    b3 = torch.zeros(96, dtype=torch.bfloat16, device=d)
-    with pytest.raises(ValueError, match='K and N of 64 or 128'):
+    w3 = torch.zeros(128, 100, dtype=torch.bfloat16, device=d)
+    b3 = torch.zeros(100, dtype=torch.bfloat16, device=d)
+    with pytest.raises(ValueError, match='N must be a multiple of 8'):
         b200().volta_gdp(x, w3, b3, w3, b3, m)
+
+
+@pytest.mark.parametrize('act', [0, 1])
+@pytest.mark.parametrize('dt', ['bf16', 'f16'])
+@pytest.mark.parametrize('M', (1, 59, 4101))
+@pytest.mark.parametrize('K,N', [(256, 256), (32, 8), (96, 200), (512, 136), (8, 64), (100, 96),
+                                 (3, 16), (130, 256)])
+def test_gdp_general_widths(K, N, M, dt, act, cuda_device):
+    """VoltaGdp at widths outside 64/128 (any K, N a multiple of 8, as the reference takes): the
+    tcgen05 tile GEMM for K % 8 == 0 (partial K slices, N tiles and row tiles clipped), the
+    CUDA-core tile kernel for K % 8 != 0."""
+    g = Gen(12, dt)
+    x = g.h(M, K, s=1.)
+    wp, wg = g.h(K, N, s=K ** -.5), g.h(K, N, s=K ** -.5)
+    bp, bg = g.h(N, s=.1), g.h(N, s=.1)
+    mask = round_to(np.resize(np.array([1.0, 0.0, -1.0, 0.5, 2.0]), M), dt)
+    want = of.gdp(x, wp, bp, wg, bg, mask, act, dt)
+    d = cuda_device
+    got = b200().volta_gdp(dev16(x, dt, d), dev16(wp, dt, d), dev16(bp, dt, d), dev16(wg, dt, d),
+                           dev16(bg, dt, d), dev16(mask, dt, d), activation=act)
+    assert b200().device_status() == 0
+    close('gdp %dx%d' % (K, N), host(got), want)
 
 
 # ---- ln_gated_dual_proj ---------------------------------------------------------------------

@@ -144,6 +144,23 @@ def test_opm_update_and_outer():
     np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-3)
 
 
+def test_trimul_contract_directions():
+    """The triangle contraction restatement against plain loops: outgoing sums over the shared
+    last index (a[c,i,k] b[c,j,k]), incoming over the shared first (a[c,k,i] b[c,k,j])."""
+    rng = np.random.default_rng(9)
+    C, I, J, K = 2, 3, 4, 5
+    a = rng.standard_normal((C, I, K))
+    b = rng.standard_normal((C, J, K))
+    want = np.zeros((C, I, J))
+    for c in range(C):
+        for i in range(I):
+            for j in range(J):
+                want[c, i, j] = sum(a[c, i, k] * b[c, j, k] for k in range(K))
+    np.testing.assert_allclose(of.trimul_contract(a, b, False), want, rtol=1e-12)
+    np.testing.assert_allclose(of.trimul_contract(a.transpose(0, 2, 1), b.transpose(0, 2, 1),
+                                                  True), want, rtol=1e-12)
+
+
 def test_tile_work():
     keep = np.array([1, 0, -1, -1, 0, 0, -1, -1, -1, -1], np.float32)
     assert of.tile_work(keep, 10, 2, -1.0) == ['compute', 'skip', 'padding', 'skip', 'skip']

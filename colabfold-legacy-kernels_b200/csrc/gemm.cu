@@ -31,7 +31,7 @@ namespace {
 
 __device__ unsigned g_status;
 
-constexpr int GBM = 128, GBN = 128, GBK = 64;
+constexpr int GBM = 128, GBK = 64;
 constexpr int kGemmThreads = 256;
 constexpr int kEpiWarp0 = 4;
 // a wait for copies or MMAs already issued, at the end of a CTA (the pipeline's own waits give up
@@ -58,18 +58,27 @@ struct GemmArgs {
 
 template <int KIND>
 struct GemmCfg {
-    static constexpr int NB = KIND == kGdpDual ? 2 : 1;  // B matrices
-    static constexpr int A_BYTES = GBM * GBK * 2;         // [128 rows][64] K-major, 128B swizzle
-    static constexpr int B_BYTES = GBK * GBN * 2;         // two [64 k][64 n] N-major atoms
+    static constexpr int NB = KIND == kGdpDual ? 2 : 1;   // B matrices
+    // output tile 128 x BN: the contraction takes 256 columns, halving its A re-reads from L2
+    static constexpr int BN = KIND == kContract ? 256 : 128;
+    static constexpr int A_BYTES = GBM * GBK * 2;          // [128 rows][64 k] or two [64 k][64 m]
+    static constexpr int B_BYTES = GBK * BN * 2;           // [BN rows][64 k] or BN/64 [64 k][64 n]
     static constexpr int STAGE_BYTES = A_BYTES + NB * B_BYTES;
-    static constexpr int STAGES = NB == 2 ? 3 : 4;
-    // output staging: two [128 rows][64] 16-bit halves, or four [128 rows][32] float32 quarters
+    static constexpr int STAGES = KIND == kOpmUpdate ? 4 : 3;
     static constexpr int OUT_ELEM = KIND == kContract ? 4 : 2;
-    static constexpr int OUT_BYTES = GBM * GBN * OUT_ELEM;
+    // output staging in boxes of 128 rows x 128 bytes (64 16-bit or 32 float32 columns):
+    // VoltaOpmUpdate two tiles' boxes (the next tile's residual lands in the other pair while
+    // this tile's outputs are written), VoltaGdp one tile's, the contraction a ring of four
+    static constexpr int BOX_BYTES = GBM * 128;
+    static constexpr int BOX_COLS = 128 / OUT_ELEM;
+    static constexpr int BOXES = BN / BOX_COLS;
+    static constexpr int STAGE_BOXES = KIND == kGdpDual ? 2 : 4;
     static constexpr int OUT_OFF = STAGES * STAGE_BYTES;
-    static constexpr int SMEM = OUT_OFF + OUT_BYTES + 1024;
-    static constexpr int ACC_COLS = NB * GBN;             // one accumulator buffer
+    static constexpr int SMEM = OUT_OFF + STAGE_BOXES * BOX_BYTES + 1024;
+    static constexpr int ACC_COLS = NB * BN;               // one accumulator buffer
     static constexpr uint32_t ALLOC = 2 * ACC_COLS <= 256 ? 256 : 512;
+    static_assert(2 * ACC_COLS <= 512, "tensor memory");
+    static_assert(KIND != kContract || BOXES == BN / 32, "one float32 box per 32 columns");
     static_assert(SMEM <= 227 * 1024, "shared memory");
 };
 
@@ -80,11 +89,16 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t sr
             "l"(map),
         "r"(src), "r"(c0), "r"(c1), "r"(c2)
         : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() {
     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
 
+// until at most N of this thread's committed bulk groups still read shared memory
+template <int N>
 __device__ __forceinline__ void bulk_wait_read() {
-    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
 }
 
 __device__ __forceinline__ void bulk_wait_all() {
@@ -93,7 +107,7 @@ __device__ __forceinline__ void bulk_wait_all() {
 
 // A_MN: A is stored M-major ([K][M], M contiguous) instead of K-major ([M][K]); B_MN: B is
 // stored N-major ([K][N]) instead of K-major ([N][K]). Every map is 3-D, the outer dimension the
-// batch.
+// batch. tb1 is VoltaGdp's second B and VoltaOpmUpdate's residual (a map shaped as the output).
 template <typename T, int KIND, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb0,
@@ -101,15 +115,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 const GemmArgs a) {
     using C = GemmCfg<KIND>;
     using E = Elem<T>;
+    constexpr int BN = C::BN;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    __shared__ uint64_t full[C::STAGES], empty[C::STAGES], acc_full[2], acc_empty[2], drain;
+    __shared__ uint64_t full[C::STAGES], empty[C::STAGES], acc_full[2], acc_empty[2], drain,
+        res_full[2];
     __shared__ uint32_t tmem_sh;
     __shared__ int abort_flag;
+    // per-column epilogue constants: VoltaOpmUpdate's bias [F] (F <= 128), VoltaGdp's bp and bg
+    // of the tile's 128 columns
+    __shared__ __align__(16) float colv[2][128];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int ntm = (a.M + GBM - 1) / GBM, ntn = (a.N + GBN - 1) / GBN;
+    const int ntm = (a.M + GBM - 1) / GBM, ntn = (a.N + BN - 1) / BN;
     const int per_batch = ntm * ntn;
     const int ntiles = per_batch * a.batch;
     const int nk = (a.K + GBK - 1) / GBK;
@@ -123,6 +142,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             for (int i = 0; i < 2; ++i) {
                 mbar_init(&acc_full[i], 1);
                 mbar_init(&acc_empty[i], 128);
+                mbar_init(&res_full[i], 1);
             }
             mbar_init(&drain, 1);
             abort_flag = 0;
@@ -131,6 +151,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         __syncwarp();
         tmem_alloc(&tmem_sh, C::ALLOC);
         tmem_relinquish();
+    } else if (warp >= kEpiWarp0 && KIND == kOpmUpdate) {
+        const int i = threadIdx.x - kEpiWarp0 * 32;
+        if (i < a.F) {
+            colv[0][i] = a.bias_f[i];
+        }
     }
     tc_fence_before();
     __syncthreads();
@@ -144,7 +169,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         bool ok = true;
         for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x) {
             const int bt = tile / per_batch, rem = tile - bt * per_batch;
-            const int m0 = (rem % ntm) * GBM, n0 = (rem / ntm) * GBN;
+            const int m0 = (rem % ntm) * GBM, n0 = (rem / ntm) * BN;
             for (int kb = 0; kb < nk; ++kb, ++g) {
                 const int s = g % C::STAGES;
                 if (g >= C::STAGES &&
@@ -169,8 +194,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     const CUtensorMap* tb = j == 0 ? &tb0 : &tb1;
                     uint8_t* bj = b + j * C::B_BYTES;
                     if constexpr (B_MN) {
-                        tma_load_3d(bj, tb, &full[s], n0, k0, bt);
-                        tma_load_3d(bj + C::B_BYTES / 2, tb, &full[s], n0 + 64, k0, bt);
+#pragma unroll
+                        for (int h = 0; h < BN / 64; ++h) {
+                            tma_load_3d(bj + h * (64 * 128), tb, &full[s], n0 + 64 * h, k0, bt);
+                        }
                     } else {
                         tma_load_3d(bj, tb, &full[s], k0, n0, bt);
                     }
@@ -183,11 +210,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                       nullptr, kDrainLimitNs);
         }
     } else if (warp == 1 && lane == 0) {
-        // MMA: M = 128, N = 128, K = 16 per instruction; A K-major (128-byte rows), B N-major
-        // (two 64-column atoms 8 KB apart, K steps of 16 rows 2 KB apart)
-        const uint32_t idesc = idesc_f16(E::kBf16, GBM, GBN, A_MN, B_MN);
-        // K-major operand: 128 rows of 128 bytes (8-row groups 1 KB apart), a K step of 16 is
-        // 32 bytes along the row; MN-major: two 64-wide atoms 8 KB apart, K steps of 16 rows 2 KB
+        // MMA: M = 128, N = BN, K = 16 per instruction
+        const uint32_t idesc = idesc_f16(E::kBf16, GBM, BN, A_MN, B_MN);
+        // K-major operand: rows of 128 bytes (8-row groups 1 KB apart), a K step of 16 is 32
+        // bytes along the row; MN-major: 64-wide atoms 8 KB apart, K steps of 16 rows 2 KB apart
         const auto desc = [](uint32_t base, int ks, bool mn) -> uint64_t {
             return mn ? smem_desc(base + ks * 16 * 128, 64 * 128, 1024, kSwizzle128B)
                       : smem_desc(base + 32 * ks, 16, 1024, kSwizzle128B);
@@ -218,7 +244,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     const uint32_t acc_on = (kb > 0 || ks > 0) ? 1u : 0u;
                     mma_ss(acc, ad, desc(sb, ks, B_MN), idesc, acc_on);
                     if constexpr (C::NB == 2) {
-                        mma_ss(acc + GBN, ad, desc(sb + C::B_BYTES, ks, B_MN), idesc, acc_on);
+                        mma_ss(acc + BN, ad, desc(sb + C::B_BYTES, ks, B_MN), idesc, acc_on);
                     }
                 }
                 mma_commit(&empty[s]);
@@ -233,99 +259,166 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     } else if (warp >= kEpiWarp0) {
         // epilogue: thread r owns tile row r (tensor-memory lane r)
         const int r = ((warp & 3) << 5) | lane;
+        const bool leader = threadIdx.x == kEpiWarp0 * 32;
         const uint32_t lane_base = tmem_lane_base(warp);
         uint8_t* ostage = smem + C::OUT_OFF;
-        int lt = 0;
+        [[maybe_unused]] const bool has_res = KIND == kOpmUpdate && a.residual != nullptr;
+        const auto tile_origin = [&](int tile, int& bt, int& m0, int& n0) {
+            bt = tile / per_batch;
+            const int rem = tile - bt * per_batch;
+            m0 = (rem % ntm) * GBM;
+            n0 = (rem / ntm) * BN;
+        };
+        // VoltaOpmUpdate: the residual tile by TMA into staging pair p (expect the bytes of
+        // both boxes; columns or rows past the ends read as zero)
+        int res_issued[2] = {0, 0};  // residual loads per staging pair (the leader's count)
+        const auto load_res = [&](int tile, int p) {
+            int bt, m0, n0;
+            tile_origin(tile, bt, m0, n0);
+            ++res_issued[p];
+            mbar_arrive_expect_tx(&res_full[p], 2 * C::BOX_BYTES);
+            tma_load_3d(ostage + (2 * p) * C::BOX_BYTES, &tb1, &res_full[p], n0, m0, bt);
+            tma_load_3d(ostage + (2 * p + 1) * C::BOX_BYTES, &tb1, &res_full[p], n0 + 64, m0,
+                        bt);
+        };
+        if constexpr (KIND == kOpmUpdate) {
+            if (has_res && leader && blockIdx.x < ntiles) {
+                load_res(blockIdx.x, 0);
+            }
+        }
+        int lt = 0, box = 0;
         for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++lt) {
             const int buf = lt & 1;
-            const int bt = tile / per_batch, rem = tile - bt * per_batch;
-            const int m0 = (rem % ntm) * GBM, n0 = (rem / ntm) * GBN;
+            int bt, m0, n0;
+            tile_origin(tile, bt, m0, n0);
             const int m = m0 + r;
-            mbar_wait(&acc_full[buf], (lt >> 1) & 1, &g_status, kStatusMmaWait, &abort_flag);
-            tc_fence_after();
-            // the previous tile's stores have read the staging
-            if (threadIdx.x == kEpiWarp0 * 32) {
-                bulk_wait_read();
+            // the previous tile's stores have read their staging (not for the contraction,
+            // whose ring is released box by box)
+            if constexpr (KIND != kContract) {
+                if (leader) {
+                    bulk_wait_read<0>();
+                    if constexpr (KIND == kOpmUpdate) {
+                        if (has_res && tile + (int)gridDim.x < ntiles) {
+                            load_res(tile + gridDim.x, buf ^ 1);
+                        }
+                    }
+                }
+            }
+            if constexpr (KIND == kGdpDual) {
+                // this tile's bp and bg, one column a thread
+                const int n = n0 + r;
+                colv[0][r] = n < a.N ? E::to_f(static_cast<const T*>(a.bp)[n]) : 0.f;
+                colv[1][r] = n < a.N ? E::to_f(static_cast<const T*>(a.bg)[n]) : 0.f;
             }
             named_sync(1, 128);
-            const uint32_t acc = tmem + buf * C::ACC_COLS + lane_base;
-            float mval = 0.f;
+            [[maybe_unused]] float mval = 0.f;
+            [[maybe_unused]] float rden[8];
             if constexpr (KIND == kGdpDual) {
                 mval = m < a.M ? E::to_f(static_cast<const T*>(a.mask)[m]) : 0.f;
             }
-#pragma unroll 1
-            for (int ch = 0; ch < GBN / 32; ++ch) {
+            if constexpr (KIND == kOpmUpdate) {
+                // 1 / (eps + norm[m, d]) for the tile's 128 / F values of d (at most 8)
+                const int d0 = n0 / a.F, nd = 128 / a.F;
+                const float* nrow = a.norm + (long long)m * a.D;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    rden[i] = (i < nd && m < a.M && d0 + i < a.D)
+                                  ? __frcp_rn(a.eps + __ldg(nrow + d0 + i))
+                                  : 0.f;
+                }
+                if (has_res) {
+                    mbar_wait(&res_full[buf], (lt >> 1) & 1, &g_status, kStatusTmaWait,
+                              &abort_flag);
+                }
+            }
+            mbar_wait(&acc_full[buf], (lt >> 1) & 1, &g_status, kStatusMmaWait, &abort_flag);
+            tc_fence_after();
+            const uint32_t acc = tmem + buf * C::ACC_COLS + lane_base;
+#pragma unroll
+            for (int ch = 0; ch < BN / 32; ++ch) {
                 uint32_t r0[32];
                 [[maybe_unused]] uint32_t r1[32];
                 tmem_ld32(acc + 32 * ch, r0);
                 if constexpr (KIND == kGdpDual) {
-                    tmem_ld32(acc + GBN + 32 * ch, r1);
+                    tmem_ld32(acc + BN + 32 * ch, r1);
                 }
                 tmem_wait_ld();
-                const int nb = n0 + 32 * ch;
-                [[maybe_unused]] float v[32];
                 if constexpr (KIND == kContract) {
-                    // the float32 products as they are: 32 columns = quarter ch of the staging,
-                    // row r, 8 pieces of 4 floats at piece (p ^ (r % 8))
-                    uint8_t* row = ostage + ch * (GBM * 128) + r * 128;
+                    // the float32 products as they are: box ch in ring slot ch % 4, row r,
+                    // 8 pieces of 4 floats at piece (p ^ (r % 8)); the slot is free once the
+                    // store of the box four before it has read it
+                    if (leader) {
+                        bulk_wait_read<3>();
+                    }
+                    named_sync(1, 128);
+                    uint8_t* slot = ostage + (box & 3) * C::BOX_BYTES;
+                    uint8_t* row = slot + r * 128;
 #pragma unroll
                     for (int p = 0; p < 8; ++p) {
                         *reinterpret_cast<uint4*>(row + ((p ^ (r & 7)) << 4)) =
                             make_uint4(r0[4 * p], r0[4 * p + 1], r0[4 * p + 2], r0[4 * p + 3]);
                     }
-                } else if constexpr (KIND == kOpmUpdate) {
-                    // (acc + bias[f]) / (eps + norm[m, d]) (+ residual), n = d F + f: F is at
-                    // least 16, so the 32 columns span at most two d (columns 0-15 and 16-31)
-                    const bool row_ok = m < a.M;
-                    const int la = a.F == 16 ? 4 : a.F == 32 ? 5 : a.F == 64 ? 6 : 7;
-                    const int d0 = nb >> la, d1 = (nb + 16) >> la;
-                    const float* nrow = a.norm + (long long)m * a.D;
-                    const float den0 = row_ok && d0 < a.D ? a.eps + nrow[d0] : 1.f;
-                    const float den1 = row_ok && d1 < a.D ? a.eps + nrow[d1] : 1.f;
-                    uint4 res[4];
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const int n = nb + 8 * q;
-                        res[q] = (a.residual != nullptr && row_ok && n < a.N)
-                                     ? __ldg(reinterpret_cast<const uint4*>(
-                                           static_cast<const T*>(a.residual) +
-                                           (long long)m * a.N + n))
-                                     : make_uint4(0, 0, 0, 0);
+                    if (ch == BN / 32 - 1) {
+                        // every column is in registers or staging: the buffer is free
+                        tc_fence_before();
+                        mbar_arrive(&acc_empty[buf]);
                     }
-                    const float* brow = a.bias_f + (nb & (a.F - 1));
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        // F = 16: columns 16-31 take bias[0..15] again
-                        const float bias = nb + i < a.N ? __ldg(brow + (i & (a.F - 1))) : 0.f;
-                        v[i] = (__uint_as_float(r0[i]) + bias) / (i < 16 ? den0 : den1);
+                    fence_async_smem();
+                    named_sync(1, 128);
+                    if (leader) {
+                        if (n0 + 32 * ch < a.N) {
+                            tma_store_3d(&to, smem_u32(slot), n0 + 32 * ch, m0, bt);
+                        }
+                        bulk_commit();
                     }
+                    ++box;
+                } else {
+                    const int nb = n0 + 32 * ch;
+                    float v[32];
+                    // staging pieces of these 32 columns: box (ch / 2) of the tile's pair, row r,
+                    // pieces 4 (ch % 2) + q at (c ^ (r % 8))
+                    const int pair = KIND == kOpmUpdate ? 2 * buf : 0;
+                    uint8_t* row = ostage + (pair + (ch >> 1)) * C::BOX_BYTES + r * 128;
+                    if constexpr (KIND == kOpmUpdate) {
+                        // (acc + bias[f]) / (eps + norm[m, d]) (+ residual), n = d F + f: the 32
+                        // columns span at most two d (F = 16)
+                        const int i0 = (32 * ch) / a.F, i1 = (32 * ch + 16) / a.F;
+                        float rd0 = 0.f, rd1 = 0.f;
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const uint32_t w4[4] = {res[q].x, res[q].y, res[q].z, res[q].w};
+                        for (int i = 0; i < 8; ++i) {  // selects, not a local-memory index
+                            rd0 = i == i0 ? rden[i] : rd0;
+                            rd1 = i == i1 ? rden[i] : rd1;
+                        }
+                        const float* bias = &colv[0][nb & (a.F - 1)];
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const float2 rr = E::unpack(w4[e]);
-                            v[8 * q + 2 * e] += rr.x;
-                            v[8 * q + 2 * e + 1] += rr.y;
+                        for (int q = 0; q < 4; ++q) {
+                            const int c = 4 * (ch & 1) + q;
+                            uint4 res = make_uint4(0, 0, 0, 0);
+                            if (has_res) {
+                                res = *reinterpret_cast<const uint4*>(row + ((c ^ (r & 7)) << 4));
+                            }
+                            const uint32_t w4[4] = {res.x, res.y, res.z, res.w};
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                const int i = 8 * q + 2 * e;
+                                // F = 16: columns 16-31 take bias[0..15] again
+                                const float b0 = bias[i & (a.F - 1)], b1 = bias[(i + 1) & (a.F - 1)];
+                                const float rd = i < 16 ? rd0 : rd1;
+                                const float2 rr = E::unpack(w4[e]);
+                                v[i] = fmaf(__uint_as_float(r0[i]) + b0, rd, rr.x);
+                                v[i + 1] = fmaf(__uint_as_float(r0[i + 1]) + b1, rd, rr.y);
+                            }
+                        }
+                    } else {
+                        // mask * (p + bp) * act(g + bg)
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            const float p = __uint_as_float(r0[i]) + colv[0][32 * ch + i];
+                            const float g = __uint_as_float(r1[i]) + colv[1][32 * ch + i];
+                            const float sg = fused::sigmoid_fast(g);
+                            v[i] = mval * p * (a.act == 0 ? sg : g * sg);
                         }
                     }
-                } else {
-                    // mask * (p + bp) * act(g + bg)
-                    const T* bp = static_cast<const T*>(a.bp);
-                    const T* bg = static_cast<const T*>(a.bg);
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const int n = nb + i;
-                        const float p = __uint_as_float(r0[i]) + (n < a.N ? E::to_f(bp[n]) : 0.f);
-                        const float g = __uint_as_float(r1[i]) + (n < a.N ? E::to_f(bg[n]) : 0.f);
-                        const float sg = fused::sigmoid_fast(g);
-                        v[i] = mval * p * (a.act == 0 ? sg : g * sg);
-                    }
-                }
-                if constexpr (KIND != kContract) {
-                    // 32 columns = 4 pieces of 16 bytes in half (ch / 2) of the staging, row r,
-                    // piece (c ^ (r % 8)) (the 128-byte swizzle of the store map)
-                    uint8_t* row = ostage + (ch >> 1) * (GBM * 128) + r * 128;
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
                         const int c = 4 * (ch & 1) + q;
@@ -338,25 +431,37 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     }
                 }
             }
-            // the accumulator buffer is free; the staged tile goes out by TMA
-            tc_fence_before();
-            mbar_arrive(&acc_empty[buf]);
-            fence_async_smem();
-            named_sync(1, 128);
-            if (threadIdx.x == kEpiWarp0 * 32) {
-                // boxes of 128 bytes a row: 64 16-bit or 32 float32 columns
-                constexpr int kBoxCols = 128 / C::OUT_ELEM;
+            if constexpr (KIND != kContract) {
+                // the accumulator buffer is free; the staged tile goes out by TMA
+                tc_fence_before();
+                mbar_arrive(&acc_empty[buf]);
+                fence_async_smem();
+                named_sync(1, 128);
+                if (leader) {
+                    const int pair = KIND == kOpmUpdate ? 2 * buf : 0;
 #pragma unroll
-                for (int q = 0; q < GBN / kBoxCols; ++q) {
-                    if (n0 + q * kBoxCols < a.N) {
-                        tma_store_3d(&to, smem_u32(ostage + q * (GBM * 128)), n0 + q * kBoxCols,
-                                     m0, bt);
+                    for (int q = 0; q < C::BOXES; ++q) {
+                        if (n0 + q * C::BOX_COLS < a.N) {
+                            tma_store_3d(&to, smem_u32(ostage + (pair + q) * C::BOX_BYTES),
+                                         n0 + q * C::BOX_COLS, m0, bt);
+                        }
                     }
+                    bulk_commit();
                 }
             }
         }
-        if (threadIdx.x == kEpiWarp0 * 32) {
+        if (leader) {
             bulk_wait_all();
+            // every residual load has landed before the CTA exits (after an abort a wait may
+            // have given up on one still in flight)
+            if constexpr (KIND == kOpmUpdate) {
+                for (int p = 0; p < 2; ++p) {
+                    if (res_issued[p] > 0) {
+                        mbar_wait(&res_full[p], (res_issued[p] - 1) & 1, &g_status,
+                                  kStatusTmaWait, nullptr, kDrainLimitNs);
+                    }
+                }
+            }
         }
     }
     tc_fence_before();
@@ -378,12 +483,12 @@ cudaError_t launch_gemm(cudaStream_t stream, int dtype, const void* A, const voi
     // A: [batch][M][K] (box 64 k x 128 m) or [batch][K][M] (box 64 m x 64 k)
     const uint64_t da[3] = {A_MN ? M : K, A_MN ? K : M, Bt}, sa[2] = {A_MN ? M : K, M * K};
     const uint32_t boxa[3] = {64, A_MN ? 64u : (uint32_t)GBM, 1};
-    // B: [batch][N][K] (box 64 k x 128 n) or [batch][K][N] (box 64 n x 64 k)
+    // B: [batch][N][K] (box 64 k x BN n) or [batch][K][N] (box 64 n x 64 k)
     const uint64_t db[3] = {B_MN ? N : K, B_MN ? K : N, Bt}, sb[2] = {B_MN ? N : K, N * K};
-    const uint32_t boxb[3] = {64, B_MN ? 64u : (uint32_t)GBN, 1};
-    // out: [batch][M][N], boxes of 128 bytes a row
+    const uint32_t boxb[3] = {64, B_MN ? 64u : (uint32_t)C::BN, 1};
+    // out (and VoltaOpmUpdate's residual): [batch][M][N], boxes of 128 bytes a row
     const uint64_t dout[3] = {N, M, Bt}, sout[2] = {N, M * N};
-    const uint32_t boxo[3] = {(uint32_t)(128 / C::OUT_ELEM), GBM, 1};
+    const uint32_t boxo[3] = {(uint32_t)C::BOX_COLS, GBM, 1};
     const CUtensorMapDataType odt = KIND == kContract ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : tdt;
     map_ok = encode_tiled(&ta, tdt, 2, 3, A, da, sa, boxa, CU_TENSOR_MAP_SWIZZLE_128B) &&
              encode_tiled(&tb0, tdt, 2, 3, B0, db, sb, boxb, CU_TENSOR_MAP_SWIZZLE_128B) &&
@@ -392,6 +497,10 @@ cudaError_t launch_gemm(cudaStream_t stream, int dtype, const void* A, const voi
     tb1 = tb0;
     if (map_ok && KIND == kGdpDual) {
         map_ok = encode_tiled(&tb1, tdt, 2, 3, B1, db, sb, boxb, CU_TENSOR_MAP_SWIZZLE_128B);
+    }
+    if (map_ok && KIND == kOpmUpdate && a.residual != nullptr) {
+        map_ok = encode_tiled(&tb1, tdt, 2, 3, a.residual, dout, sout, boxo,
+                              CU_TENSOR_MAP_SWIZZLE_128B);
     }
     if (!map_ok) {
         return cudaSuccess;
@@ -414,7 +523,7 @@ cudaError_t launch_gemm(cudaStream_t stream, int dtype, const void* A, const voi
     }
     const int nsm = dev < kMaxDevices && sms[dev] > 0 ? sms[dev] : 148;
     const long long tiles =
-        (long long)((a.M + GBM - 1) / GBM) * ((a.N + GBN - 1) / GBN) * a.batch;
+        (long long)((a.M + GBM - 1) / GBM) * ((a.N + C::BN - 1) / C::BN) * a.batch;
     const dim3 grid((unsigned)std::min<long long>(tiles, nsm));
     kern<<<grid, kGemmThreads, C::SMEM, stream>>>(ta, tb0, tb1, to, a);
     return cudaGetLastError();
@@ -617,7 +726,7 @@ int gdp_general(void* stream_, int dtype, const void* x, const void* wp, const v
         const cudaError_t e = cudaGetLastError();
         return e == cudaSuccess ? kOk : fail(kInternal, std::string("gdp launch: ") + cudaGetErrorString(e));
     }
-    if (((M + GBM - 1) / GBM) * ((N + GBN - 1) / GBN) >= (int64_t(1) << 31)) {
+    if (((M + GBM - 1) / GBM) * ((N + 127) / 128) >= (int64_t(1) << 31)) {
         return fail(kInvalidArgument, "gdp: too many output tiles");
     }
     GemmArgs a{};
@@ -690,7 +799,7 @@ extern "C" int cflk_volta_opm_update(void* stream, int dtype, const void* lhs, c
         return e == cudaSuccess ? kOk
                                 : fail(kInternal, std::string("opm_update launch: ") + cudaGetErrorString(e));
     }
-    if (((B + GBM - 1) / GBM) * ((D * F + GBN - 1) / GBN) >= (int64_t(1) << 31)) {
+    if (((B + GBM - 1) / GBM) * ((D * F + 127) / 128) >= (int64_t(1) << 31)) {
         return fail(kInvalidArgument, "opm_update: too many output tiles");
     }
     GemmArgs a{};
@@ -738,7 +847,7 @@ extern "C" int cflk_trimul_contract(void* stream, int dtype, const void* a, cons
         return fail(kInvalidArgument,
                     "trimul_contract: C at most 65535, I, J and K below 2^31");
     }
-    if (a == nullptr || b == nullptr || out == nullptr) {
+    if (out == nullptr || (K > 0 && (a == nullptr || b == nullptr))) {
         return fail(kInvalidArgument, "trimul_contract: null buffer");
     }
     cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -752,7 +861,7 @@ extern "C" int cflk_trimul_contract(void* stream, int dtype, const void* a, cons
     // multiple of 8 elements, the float32 output rows of 4
     const bool rows16 = incoming ? (I % 8 == 0 && J % 8 == 0) : (K % 8 == 0);
     const bool tma = rows16 && J % 4 == 0 && aligned16(a) && aligned16(b) && aligned16(out) &&
-                     ((I + GBM - 1) / GBM) * ((J + GBN - 1) / GBN) * C < (int64_t(1) << 31);
+                     ((I + GBM - 1) / GBM) * ((J + 255) / 256) * C < (int64_t(1) << 31);
     cudaError_t e = cudaSuccess;
     if (tma) {
         GemmArgs g{};

@@ -140,6 +140,75 @@ def _fusion_cpu_inputs(name, rows, rng):
     raise KeyError(name)
 
 
+# The next rows (the triangle contraction, the outer product mean, VoltaGdp at the channel-major
+# width) on BASELINE configs[3]'s pair: name -> (units of the workload, the unit's name, units a
+# CPU worker takes). Algorithmic bytes and FLOPs in next_row_work().
+OPM_K, OPM_C, OPM_F = 16 * 32, 32, 128   # 16 MSA rows x 32 channels, c_z out
+NEXT_ROWS = {
+    'trimul_contract outgoing C=128': (128, 'channels', 1),
+    'trimul_contract incoming C=128': (128, 'channels', 1),
+    'opm_update K=512 F=128': (768, 'rows of b', 8),
+    'opm_outer C=E=32 F=128': (768, 'rows of b', 4),
+    'gated_dual_proj K=128 N=256 sigmoid': (768 * 768, 'rows', 1 << 14),
+}
+
+
+def next_row_work(name, units):
+    """(algorithmic bytes, FLOPs) of `units` units of a next-row workload: every input read once
+    and every output written once (16-bit; float32 x_cm and OPM norms), intermediates none."""
+    n = PAIR
+    if name.startswith('trimul_contract'):
+        return units * n * n * (2 + 2 + 4), 2.0 * units * n ** 3
+    if name.startswith('opm_update'):
+        return (units * OPM_K * 2 + OPM_K * n * OPM_F * 2 + 2 * units * n * OPM_F * 2 +
+                units * n * 4), 2.0 * units * OPM_K * n * OPM_F
+    if name.startswith('opm_outer'):
+        ce = OPM_C * 32
+        return ((16 * units * OPM_C + 16 * n * 32 + OPM_F * ce + units * n * OPM_F) * 2,
+                2.0 * units * n * ce * (16 + OPM_F))
+    if name.startswith('gated_dual_proj'):
+        return units * (C_Z * 2 + 256 * 2 + 2) + 2 * C_Z * 256 * 2, 2.0 * units * C_Z * 256 * 2
+    raise KeyError(name)
+
+
+def _next_cpu_inputs(name, units, rng):
+    """Inputs of `units` units of a next-row workload and the oracle call that computes them."""
+    import numpy as np
+    from oracle import fused as of
+    f = np.float32
+    n = PAIR
+    if name.startswith('trimul_contract'):
+        a = rng.standard_normal((units, n, n), dtype=f)
+        b = rng.standard_normal((units, n, n), dtype=f)
+        return lambda: of.trimul_contract(a, b, 'incoming' in name)
+    if name.startswith('opm_update'):
+        lhs = rng.standard_normal((units, OPM_K), dtype=f)
+        t = rng.standard_normal((OPM_K, n, OPM_F), dtype=f) * OPM_K ** -0.5
+        bias, norm = np.zeros(OPM_F, f), np.ones((units, n), f)
+        res = rng.standard_normal((units, n, OPM_F), dtype=f)
+        return lambda: of.opm_update(lhs, t, bias, norm, res, 1e-3, 'bf16')
+    if name.startswith('opm_outer'):
+        left = rng.standard_normal((16, units, OPM_C), dtype=f)
+        right = rng.standard_normal((16, n, 32), dtype=f)
+        wT = rng.standard_normal((OPM_F, OPM_C * 32), dtype=f) * (OPM_C * 32) ** -0.5
+        return lambda: of.opm_outer(left, right, wT, 'bf16')
+    if name.startswith('gated_dual_proj'):
+        x = rng.standard_normal((units, C_Z), dtype=f)
+        wp, wg = (rng.standard_normal((C_Z, 256), dtype=f) * C_Z ** -0.5 for _ in range(2))
+        b0, mask = np.zeros(256, f), np.ones(units, f)
+        return lambda: of.gdp(x, wp, b0, wg, b0, mask, 0, 'bf16')
+    raise KeyError(name)
+
+
+def _cpu_next_worker(args):
+    import numpy as np
+    name, seed, units = args
+    fn = _next_cpu_inputs(name, units, np.random.default_rng(seed))
+    t0 = time.perf_counter()
+    fn()
+    return time.perf_counter() - t0
+
+
 def _cpu_fusion_worker(args):
     import numpy as np
     name, seed, rows = args
@@ -171,6 +240,12 @@ class CpuBaseline:
         share = -(-rows // self.cores)
         t0 = time.perf_counter()
         self.pool.map(_cpu_fusion_worker, [(name, i, share) for i in range(self.cores)])
+        return time.perf_counter() - t0, share * self.cores
+
+    def next_step(self, name):
+        share = NEXT_ROWS[name][2]
+        t0 = time.perf_counter()
+        self.pool.map(_cpu_next_worker, [(name, i, share) for i in range(self.cores)])
         return time.perf_counter() - t0, share * self.cores
 
     def close(self):
@@ -206,6 +281,20 @@ def cpu_fusion_lines(cpu):
                      'kind': 'port',
                      'sample': '%d of %d rows (numpy oracle, one process per core), %.2f s'
                                % (rows, PAIR * PAIR, t)}
+    return out
+
+
+def cpu_next_lines(cpu):
+    """The CPU baseline of each next-row workload: the oracle over a bounded sample of its units,
+    GB/s and TFLOP/s as the GPU lines count them."""
+    out = {}
+    for name, (total, unit, _) in NEXT_ROWS.items():
+        t, units = cpu.next_step(name)
+        nbytes, flops = next_row_work(name, units)
+        out[name] = {'value': nbytes / t / 1e9, 'unit': 'GB/s', 'TFLOP/s': flops / t / 1e12,
+                     'cores': cpu.cores, 'kind': 'port',
+                     'sample': '%d of %d %s (numpy oracle, one process per core), %.2f s'
+                               % (units, total, unit, t)}
     return out
 
 
@@ -377,6 +466,8 @@ def run_ours(args):
                 cpu_more['inference'] = cpu_attention_line(cpu, 'inference', 1, 0)[0]
             if not args.no_fusions:
                 cpu_more['fusions'] = cpu_fusion_lines(cpu)
+            if not args.no_next:
+                cpu_more['next'] = cpu_next_lines(cpu)
         finally:
             cpu.close()
 
@@ -470,6 +561,13 @@ def run_ours(args):
             if name in fusions:
                 fusions[name]['cpu_baseline'] = line
 
+    nxt = None
+    if not args.no_next:
+        nxt = bench_next_rows(torch, b200, dev, rank, world, args.steps, args.warmup, flush, pk)
+        for name, line in cpu_more.get('next', {}).items():
+            if name in nxt:
+                nxt[name]['cpu_baseline'] = line
+
     big = None
     if not args.no_inference:
         big = bench_inference(torch, b200, dev, rank, world, max(2, args.steps // 3), 2, flush,
@@ -514,6 +612,8 @@ def run_ours(args):
             line['triangle_384'] = tri
         if fusions is not None:
             line['fusions'] = fusions
+        if nxt is not None:
+            line['next_rows'] = nxt
         if big is not None:
             line['inference_2048'] = big
         print(json.dumps(line), flush=True)
@@ -701,6 +801,91 @@ def bench_fusions(torch, b200, dev, rank, world, steps, warmup, flush, pk, only=
                          'bytes': nbytes * world, 'rows': M_all}
     if b200.device_status() != 0:
         raise RuntimeError('a fused kernel reported a wait that gave up')
+    return res_out
+
+
+def bench_next_rows(torch, b200, dev, rank, world, steps, warmup, flush, pk, only=None):
+    """The next rows on BASELINE configs[3]'s pair (768 residues, bf16, N(0,1) activations,
+    weights ~ N(0, 1/sqrt(fan-in))): the triangle contraction of ln_gdp's ci = 128 halves (both
+    edge directions, float32 out), VoltaOpmUpdate (16 MSA rows x 32 channels contracted against
+    t [512, 768, 128], norms 1, with the residual), VoltaOpmOuter (16 rows, C = E = 32, F = 128),
+    VoltaGdp at the channel-major width K = 128, N = 256 on the pair's rows. Each rank takes its
+    share of the leading units. 'roofline_frac' = max(bytes / measured HBM, FLOPs / measured
+    bf16 peak) / device time."""
+    import torch.distributed as dist
+    n = PAIR
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    bf = torch.bfloat16
+
+    def rn(*shape, s=1.0, dt=bf):
+        return (torch.randn(*shape, generator=g, device=dev) * s).to(dt)
+
+    ops = []
+    for name, (total, _, _) in NEXT_ROWS.items():
+        if only is not None and not name.startswith(only):
+            continue
+        units = total // world
+        if name.startswith('trimul_contract'):
+            a, b = rn(units, n, n), rn(units, n, n)
+            out = torch.empty(units, n, n, device=dev)
+            inc = 'incoming' in name
+            fn = (lambda a=a, b=b, out=out, inc=inc: b200.trimul_contract(a, b, incoming=inc,
+                                                                          out=out))
+        elif name.startswith('opm_update'):
+            lhs, t = rn(units, OPM_K), rn(OPM_K, n, OPM_F, s=OPM_K ** -0.5)
+            bias, norm = torch.zeros(OPM_F, device=dev), torch.ones(units, n, device=dev)
+            res, out = rn(units, n, OPM_F), torch.empty(units, n, OPM_F, dtype=bf, device=dev)
+            fn = (lambda lhs=lhs, t=t, bias=bias, norm=norm, res=res, out=out:
+                  b200.volta_opm_update(lhs, t, bias, norm, res, eps=1e-3, out=out))
+        elif name.startswith('opm_outer'):
+            left, right = rn(16, units, OPM_C), rn(16, n, 32)
+            wT = rn(OPM_F, OPM_C * 32, s=(OPM_C * 32) ** -0.5)
+            out = torch.empty(units, n, OPM_F, dtype=bf, device=dev)
+            wsn = b200.opm_outer_workspace_size(units, OPM_C, n, 32)
+            ws = torch.empty(wsn, dtype=torch.uint8, device=dev)
+            fn = (lambda left=left, right=right, wT=wT, out=out, ws=ws:
+                  b200.volta_opm_outer(left, right, wT, out=out, workspace=ws))
+        else:
+            x = rn(units, C_Z)
+            wp, wg = rn(C_Z, 256, s=C_Z ** -0.5), rn(C_Z, 256, s=C_Z ** -0.5)
+            bp, bg = rn(256, s=0.1), rn(256, s=0.1)
+            mask = torch.ones(units, dtype=bf, device=dev)
+            out = torch.empty(units, 256, dtype=bf, device=dev)
+            fn = (lambda x=x, wp=wp, bp=bp, wg=wg, bg=bg, mask=mask, out=out:
+                  b200.volta_gdp(x, wp, bp, wg, bg, mask, activation=0, out=out))
+        nbytes, flops = next_row_work(name, units)
+        ops.append((name, fn, nbytes, flops))
+    res_out = {}
+    for name, fn, nbytes, flops in ops:
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        evs = []
+        for _ in range(steps):
+            flush.fill_(3)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            evs.append((a, b))
+        torch.cuda.synchronize()
+        ms = sum(a.elapsed_time(b) for a, b in evs) / steps
+        t = torch.tensor([ms], device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        gbs = nbytes * world / (ms * 1e-3) / 1e9
+        tf = flops * world / (ms * 1e-3) / 1e12
+        t_hbm = nbytes / (pk['hbm_gbs'] * 1e9)
+        t_tc = flops / (pk['bf16_tflops'] * 1e12)
+        res_out[name] = {'ms': ms, 'GB/s': gbs, 'frac_hbm': gbs / (pk['hbm_gbs'] * world),
+                         'TFLOP/s': tf, 'frac_bf16': tf / (pk['bf16_tflops'] * world),
+                         'bound': 'hbm' if t_hbm >= t_tc else 'tensor',
+                         'roofline_frac': max(t_hbm, t_tc) / (ms * 1e-3),
+                         'bytes': nbytes * world, 'flops': flops * world}
+    if b200.device_status() != 0:
+        raise RuntimeError('a next-row kernel reported a wait that gave up')
     return res_out
 
 
@@ -893,6 +1078,8 @@ def main():
     ap.add_argument('--impl', choices=('ours', 'reference'), default='ours')
     ap.add_argument('--no-cpu', action='store_true', help='skip the cpu_baseline sample')
     ap.add_argument('--no-fusions', action='store_true', help='skip the pair-fusion lines')
+    ap.add_argument('--no-next', action='store_true',
+                    help='skip the next-row lines (triangle contraction, OPM, wide Gdp)')
     ap.add_argument('--no-e2e', action='store_true', help='skip the host-buffer end-to-end leg')
     ap.add_argument('--no-inference', action='store_true',
                     help='skip the large-protein inference leg (BASELINE configs[4])')

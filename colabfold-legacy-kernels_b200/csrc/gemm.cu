@@ -38,11 +38,17 @@ constexpr int kEpiWarp0 = 4;
 // after 2 s and set the abort flag; these then bound the drain)
 constexpr unsigned long long kDrainLimitNs = 200000000ull;
 
-enum GemmKind : int { kOpmUpdate = 0, kGdpDual = 1, kContract = 2 };
+// kOpmOuterG / kPlain: the two products of VoltaOpmOuter. kOpmOuterG: G [(b,c), (d,e)] =
+// left^T right over the 16 MSA rows, rounded to the 16-bit type and written as G2 [b][d][c][e]
+// (a 4-D box store: a tile's 128 rows are 128/C whole b, its 128 columns 4 whole d); kPlain:
+// out = A B rounded, no epilogue arithmetic (G2 as [B*D][C*E] times wT).
+enum GemmKind : int { kOpmUpdate = 0, kGdpDual = 1, kContract = 2, kOpmOuterG = 3, kPlain = 4 };
 
 struct GemmArgs {
     int M, N, K;
     int batch;  // independent products (kContract: the channels), each [M, N]
+    int opm_c;  // kOpmOuterG: C (16, 32, 64 or 128), the rows of one b
+    long long lda;  // A's row stride in elements when it is not the default (0)
     // VoltaOpmUpdate: bias [F] float32, norm [M, D] float32, residual [M, N] (or null)
     const float* bias_f;
     const float* norm;
@@ -64,7 +70,7 @@ struct GemmCfg {
     static constexpr int A_BYTES = GBM * GBK * 2;          // [128 rows][64 k] or two [64 k][64 m]
     static constexpr int B_BYTES = GBK * BN * 2;           // [BN rows][64 k] or BN/64 [64 k][64 n]
     static constexpr int STAGE_BYTES = A_BYTES + NB * B_BYTES;
-    static constexpr int STAGES = KIND == kOpmUpdate ? 4 : 3;
+    static constexpr int STAGES = NB == 1 && BN == 128 ? 4 : 3;
     static constexpr int OUT_ELEM = KIND == kContract ? 4 : 2;
     // output staging in boxes of 128 rows x 128 bytes (64 16-bit or 32 float32 columns):
     // VoltaOpmUpdate two tiles' boxes (the next tile's residual lands in the other pair while
@@ -72,7 +78,7 @@ struct GemmCfg {
     static constexpr int BOX_BYTES = GBM * 128;
     static constexpr int BOX_COLS = 128 / OUT_ELEM;
     static constexpr int BOXES = BN / BOX_COLS;
-    static constexpr int STAGE_BOXES = KIND == kGdpDual ? 2 : 4;
+    static constexpr int STAGE_BOXES = KIND == kOpmUpdate || KIND == kContract ? 4 : 2;
     static constexpr int OUT_OFF = STAGES * STAGE_BYTES;
     static constexpr int SMEM = OUT_OFF + STAGE_BOXES * BOX_BYTES + 1024;
     static constexpr int ACC_COLS = NB * BN;               // one accumulator buffer
@@ -88,6 +94,15 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t sr
         "cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::
             "l"(map),
         "r"(src), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, uint32_t src, int c0, int c1,
+                                             int c2, int c3) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4, %5}], "
+        "[%1];" ::"l"(map),
+        "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
         : "memory");
 }
 
@@ -238,8 +253,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 tc_fence_after();
                 const uint32_t sa = smem_u32(smem + s * C::STAGE_BYTES);
                 const uint32_t sb = sa + C::A_BYTES;
+                // K steps past K (zero-filled) are skipped: VoltaOpmOuter's first product has K 16
+                const int ksteps = min(GBK / 16, (a.K - kb * GBK + 15) / 16);
 #pragma unroll
                 for (int ks = 0; ks < GBK / 16; ++ks) {
+                    if (ks >= ksteps) {
+                        break;
+                    }
                     const uint64_t ad = desc(sa, ks, A_MN);
                     const uint32_t acc_on = (kb > 0 || ks > 0) ? 1u : 0u;
                     mma_ss(acc, ad, desc(sb, ks, B_MN), idesc, acc_on);
@@ -372,6 +392,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         bulk_commit();
                     }
                     ++box;
+                } else if constexpr (KIND == kOpmOuterG) {
+                    // row r = (b_l, c), columns 32 ch.. = d_l ch, e 0..31: 64 bytes at
+                    // [b_l][d_l][c][e] of the [128/C][4][C][32] box (plain layout, a warp's 32
+                    // rows are 32 consecutive 64-byte runs)
+                    const int bl = r / a.opm_c, cl = r - bl * a.opm_c;
+                    uint8_t* dst = ostage + (((bl * 4 + ch) * a.opm_c) + cl) * 64;
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        uint4 w;
+                        w.x = E::pack(__uint_as_float(r0[8 * q]), __uint_as_float(r0[8 * q + 1]));
+                        w.y = E::pack(__uint_as_float(r0[8 * q + 2]),
+                                      __uint_as_float(r0[8 * q + 3]));
+                        w.z = E::pack(__uint_as_float(r0[8 * q + 4]),
+                                      __uint_as_float(r0[8 * q + 5]));
+                        w.w = E::pack(__uint_as_float(r0[8 * q + 6]),
+                                      __uint_as_float(r0[8 * q + 7]));
+                        *reinterpret_cast<uint4*>(dst + 16 * q) = w;
+                    }
                 } else {
                     const int nb = n0 + 32 * ch;
                     float v[32];
@@ -409,6 +447,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                 v[i + 1] = fmaf(__uint_as_float(r0[i + 1]) + b1, rd, rr.y);
                             }
                         }
+                    } else if constexpr (KIND == kPlain) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            v[i] = __uint_as_float(r0[i]);
+                        }
                     } else {
                         // mask * (p + bp) * act(g + bg)
 #pragma unroll
@@ -438,12 +481,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 fence_async_smem();
                 named_sync(1, 128);
                 if (leader) {
-                    const int pair = KIND == kOpmUpdate ? 2 * buf : 0;
+                    if constexpr (KIND == kOpmOuterG) {
+                        // the whole tile as one [128/C b][4 d][C c][32 e] box of G2
+                        tma_store_4d(&to, smem_u32(ostage), 0, 0, n0 / 32, m0 / a.opm_c);
+                    } else {
+                        const int pair = KIND == kOpmUpdate ? 2 * buf : 0;
 #pragma unroll
-                    for (int q = 0; q < C::BOXES; ++q) {
-                        if (n0 + q * C::BOX_COLS < a.N) {
-                            tma_store_3d(&to, smem_u32(ostage + (pair + q) * C::BOX_BYTES),
-                                         n0 + q * C::BOX_COLS, m0, bt);
+                        for (int q = 0; q < C::BOXES; ++q) {
+                            if (n0 + q * C::BOX_COLS < a.N) {
+                                tma_store_3d(&to, smem_u32(ostage + (pair + q) * C::BOX_BYTES),
+                                             n0 + q * C::BOX_COLS, m0, bt);
+                            }
                         }
                     }
                     bulk_commit();
@@ -481,7 +529,8 @@ cudaError_t launch_gemm(cudaStream_t stream, int dtype, const void* A, const voi
     const uint64_t M = a.M, N = a.N, K = a.K, Bt = a.batch;
     CUtensorMap ta, tb0, tb1, to;
     // A: [batch][M][K] (box 64 k x 128 m) or [batch][K][M] (box 64 m x 64 k)
-    const uint64_t da[3] = {A_MN ? M : K, A_MN ? K : M, Bt}, sa[2] = {A_MN ? M : K, M * K};
+    const uint64_t lda = a.lda > 0 ? (uint64_t)a.lda : (A_MN ? M : K);
+    const uint64_t da[3] = {A_MN ? M : K, A_MN ? K : M, Bt}, sa[2] = {lda, lda * (A_MN ? K : M)};
     const uint32_t boxa[3] = {64, A_MN ? 64u : (uint32_t)GBM, 1};
     // B: [batch][N][K] (box 64 k x BN n) or [batch][K][N] (box 64 n x 64 k)
     const uint64_t db[3] = {B_MN ? N : K, B_MN ? K : N, Bt}, sb[2] = {B_MN ? N : K, N * K};
@@ -491,9 +540,17 @@ cudaError_t launch_gemm(cudaStream_t stream, int dtype, const void* A, const voi
     const uint32_t boxo[3] = {(uint32_t)C::BOX_COLS, GBM, 1};
     const CUtensorMapDataType odt = KIND == kContract ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : tdt;
     map_ok = encode_tiled(&ta, tdt, 2, 3, A, da, sa, boxa, CU_TENSOR_MAP_SWIZZLE_128B) &&
-             encode_tiled(&tb0, tdt, 2, 3, B0, db, sb, boxb, CU_TENSOR_MAP_SWIZZLE_128B) &&
-             encode_tiled(&to, odt, C::OUT_ELEM, 3, out, dout, sout, boxo,
-                          CU_TENSOR_MAP_SWIZZLE_128B);
+             encode_tiled(&tb0, tdt, 2, 3, B0, db, sb, boxb, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (map_ok && KIND == kOpmOuterG) {
+        // G2 [b][d][c][e]: M = B C rows (b, c), N = D 32 columns (d, e)
+        const uint64_t Cc = a.opm_c, D = N / 32, Bb = M / Cc;
+        const uint64_t dg[4] = {32, Cc, D, Bb}, sg[3] = {32, 32 * Cc, 32 * Cc * D};
+        const uint32_t boxg[4] = {32, (uint32_t)Cc, 4, (uint32_t)(GBM / Cc)};
+        map_ok = encode_tiled(&to, tdt, 2, 4, out, dg, sg, boxg, CU_TENSOR_MAP_SWIZZLE_NONE);
+    } else if (map_ok) {
+        map_ok = encode_tiled(&to, odt, C::OUT_ELEM, 3, out, dout, sout, boxo,
+                              CU_TENSOR_MAP_SWIZZLE_128B);
+    }
     tb1 = tb0;
     if (map_ok && KIND == kGdpDual) {
         map_ok = encode_tiled(&tb1, tdt, 2, 3, B1, db, sb, boxb, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -677,6 +734,38 @@ __global__ void __launch_bounds__(256) contract_simt_kernel(const T* a, const T*
                 oc[(long long)i * J + j] = acc[u][w];
             }
         }
+    }
+}
+
+// VoltaOpmOuter's first product on the CUDA cores, for C that does not divide 128: one block a
+// (d, b) pair, G2[b][d][c][e] = h(sum_a left[a, b0 + b, c] right[a, d, e]) for every (c, e)
+template <typename T>
+__global__ void __launch_bounds__(256) opm_outer_g_simt_kernel(const T* left, const T* right,
+                                                               T* g2, int Bfull, int C, int D,
+                                                               int b0) {
+    using E = Elem<T>;
+    extern __shared__ float sh[];  // left rows [16][C], right rows [16][32]
+    float* ls = sh;
+    float* rs = sh + 16 * C;
+    const int d = blockIdx.x, b = blockIdx.y;
+    for (int i = threadIdx.x; i < 16 * C; i += blockDim.x) {
+        const int arow = i / C, c = i - arow * C;
+        ls[i] = E::to_f(left[((long long)arow * Bfull + b0 + b) * C + c]);
+    }
+    for (int i = threadIdx.x; i < 16 * 32; i += blockDim.x) {
+        const int arow = i / 32, e = i - arow * 32;
+        rs[i] = E::to_f(right[((long long)arow * D + d) * 32 + e]);
+    }
+    __syncthreads();
+    T* dst = g2 + ((long long)b * D + d) * C * 32;
+    for (int i = threadIdx.x; i < C * 32; i += blockDim.x) {
+        const int c = i / 32, e = i - c * 32;
+        float acc = 0.f;
+#pragma unroll
+        for (int arow = 0; arow < 16; ++arow) {
+            acc = fmaf(ls[arow * C + c], rs[arow * 32 + e], acc);
+        }
+        dst[i] = E::from_f(acc);
     }
 }
 
@@ -908,6 +997,141 @@ extern "C" int cflk_trimul_contract(void* stream, int dtype, const void* a, cons
     }
     if (e != cudaSuccess) {
         return fail(kInternal, std::string("trimul_contract launch: ") + cudaGetErrorString(e));
+    }
+    return kOk;
+}
+
+namespace {
+
+constexpr size_t kOpmOuterChunkBytes = size_t(64) << 20;  // G2 per chunk: stays in L2
+
+// b rows a chunk must hold whole: a stage-1 tile covers 128 / C values of b
+int64_t opm_outer_block(int64_t C) {
+    return (C == 16 || C == 32 || C == 64 || C == 128) ? 128 / C : 1;
+}
+
+}  // namespace
+
+extern "C" int cflk_volta_opm_outer_workspace_size(int64_t B, int64_t C, int64_t D, int64_t E,
+                                                   size_t* bytes) {
+    clear_error();
+    if (bytes == nullptr || B < 0 || C < 0 || D < 0 || E != 32) {
+        return fail(kInvalidArgument, "opm_outer: left must be [16,B,C], right [16,D,E], E 32");
+    }
+    int64_t per_b = 0;
+    if (__builtin_mul_overflow(D, C * E * 2, &per_b)) {
+        return fail(kInvalidArgument, "opm_outer: workspace size overflows");
+    }
+    if (per_b == 0 || B == 0) {
+        *bytes = 0;
+        return kOk;
+    }
+    const int64_t blk = opm_outer_block(C);
+    int64_t bc = (int64_t)(kOpmOuterChunkBytes / (size_t)per_b) / blk * blk;
+    bc = std::max(bc, blk);
+    bc = std::min(bc, B);
+    int64_t total = 0;
+    if (__builtin_mul_overflow(bc, per_b, &total)) {
+        return fail(kInvalidArgument, "opm_outer: workspace size overflows");
+    }
+    *bytes = (size_t)total;
+    return kOk;
+}
+
+extern "C" int cflk_volta_opm_outer(void* stream, int dtype, const void* left, const void* right,
+                                    const void* wT, void* out, int64_t B, int64_t C, int64_t D,
+                                    int64_t E, int64_t F, void* workspace, size_t ws_bytes) {
+    clear_error();
+    if (dtype != kF16 && dtype != kBF16) {
+        return fail(kInvalidArgument, "opm_outer: dtype must be f16 or bf16");
+    }
+    if (B < 0 || C < 0 || D < 0 || E < 0 || F < 0) {
+        return fail(kInvalidArgument,
+                    "opm_outer: left must be [16,B,C], right [16,D,E], wT [F,C*E]");
+    }
+    if (C % 16 || E != 32 || D % 4 || D / 4 > 65535 ||
+        (F != 16 && F != 32 && F != 64 && F != 128)) {
+        return fail(kInvalidArgument,
+                    "opm_outer: C a multiple of 16, E 32, D a multiple of 4, F 16, 32, 64 or 128");
+    }
+    if (B == 0 || D == 0 || C == 0) {
+        return kOk;
+    }
+    const int64_t blk = opm_outer_block(C);
+    if (blk == 1 && C > 512) {
+        return fail(kInvalidArgument, "opm_outer: C above 512 must be 16, 32, 64 or 128");
+    }
+    if (B * C >= (int64_t(1) << 31) || B * D >= (int64_t(1) << 31) ||
+        D * 32 >= (int64_t(1) << 31)) {
+        return fail(kInvalidArgument, "opm_outer: sizes must be below 2^31");
+    }
+    if (!aligned16(left) || !aligned16(right) || !aligned16(wT) || !aligned16(out) ||
+        !aligned16(workspace)) {
+        return fail(kInvalidArgument, "opm_outer: buffers must be 16-byte aligned");
+    }
+    const int64_t per_b = D * C * 64;  // G2 bytes of one b
+    // b rows a chunk: all of them, or whole multiples of 128 / C
+    int64_t bc = (int64_t)(ws_bytes / (size_t)per_b);
+    bc = bc >= B ? B : bc / blk * blk;
+    if (bc <= 0) {
+        return fail(kInvalidArgument,
+                    "opm_outer: workspace below one chunk (cflk_volta_opm_outer_workspace_size)");
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const auto run = [&](auto tag) -> cudaError_t {
+        using T = decltype(tag);
+        for (int64_t b0 = 0; b0 < B; b0 += bc) {
+            const int64_t nb = std::min(bc, B - b0);
+            bool ok = true;
+            cudaError_t e = cudaSuccess;
+            if (blk > 1) {
+                GemmArgs g{};
+                g.batch = 1;
+                g.M = (int)(nb * C);
+                g.N = (int)(D * 32);
+                g.K = 16;
+                g.opm_c = (int)C;
+                g.lda = B * C;
+                e = launch_gemm<T, kOpmOuterG, true, true>(
+                    s, dtype, static_cast<const T*>(left) + b0 * C, right, nullptr, workspace, g,
+                    ok);
+            } else {
+                const dim3 grid((unsigned)D, (unsigned)nb);
+                opm_outer_g_simt_kernel<T><<<grid, 256, (size_t)(16 * C + 512) * sizeof(float),
+                                             s>>>(static_cast<const T*>(left),
+                                                  static_cast<const T*>(right),
+                                                  static_cast<T*>(workspace), (int)B, (int)C,
+                                                  (int)D, (int)b0);
+                e = cudaGetLastError();
+            }
+            if (!ok) {
+                return cudaErrorInvalidValue;
+            }
+            if (e != cudaSuccess) {
+                return e;
+            }
+            GemmArgs g2{};
+            g2.batch = 1;
+            g2.M = (int)(nb * D);
+            g2.N = (int)F;
+            g2.K = (int)(C * 32);
+            e = launch_gemm<T, kPlain, false, false>(s, dtype, workspace, wT, nullptr,
+                                                    static_cast<T*>(out) + b0 * D * F, g2, ok);
+            if (!ok) {
+                return cudaErrorInvalidValue;
+            }
+            if (e != cudaSuccess) {
+                return e;
+            }
+        }
+        return cudaSuccess;
+    };
+    const cudaError_t e = dtype == kBF16 ? run(__nv_bfloat16{}) : run(__half{});
+    if (e == cudaErrorInvalidValue) {
+        return fail(kInvalidArgument, "opm_outer: TMA descriptor rejected");
+    }
+    if (e != cudaSuccess) {
+        return fail(kInternal, std::string("opm_outer launch: ") + cudaGetErrorString(e));
     }
     return kOk;
 }

@@ -88,6 +88,7 @@ _TABLE = {
         (70, "libvolta_gdp_wmma.so", "VoltaOpmUpdateWmma"),
     ),
     "opm_outer": (
+        (100, _SM100_LIB, "VoltaOpmOuter"),
         (75, "libvolta_ops.so", "VoltaOpmOuter"),
         (70, "libvolta_gdp_wmma.so", "VoltaOpmOuterWmma"),
     ),
@@ -105,6 +106,7 @@ _C_SYMBOLS = {
     "VoltaLayerNorm": "cflk_volta_layer_norm",
     "VoltaGdp": "cflk_volta_gdp",
     "VoltaOpmUpdate": "cflk_volta_opm_update",
+    "VoltaOpmOuter": "cflk_volta_opm_outer",
 }
 
 KERNELS = tuple(_TABLE)

@@ -48,6 +48,9 @@ _SIGS = {
     'cflk_volta_gdp': [_p, _int, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64],
     'cflk_volta_opm_update': [_p, _int, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _f32],
     'cflk_trimul_contract': [_p, _int, _p, _p, _p, _i64, _i64, _i64, _i64, _int],
+    'cflk_volta_opm_outer_workspace_size': [_i64, _i64, _i64, _i64, _C.POINTER(_C.c_size_t)],
+    'cflk_volta_opm_outer': [_p, _int, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p,
+                             _C.c_size_t],
 }
 
 _lib = None
@@ -293,6 +296,44 @@ def volta_opm_update(lhs, t, bias, norm, residual=None, *, eps, out=None):
     rc = lib().cflk_volta_opm_update(_stream(), dt, _ptr(lhs), _ptr(t),
                                      _f32_ptr(bias, 'bias', who), _f32_ptr(norm, 'norm', who),
                                      _ptr(residual), _ptr(out), B, K, D, F, float(eps))
+    _check(rc, who)
+    return out
+
+
+def opm_outer_workspace_size(B, C, D, E=32):
+    """Bytes of VoltaOpmOuter's recommended workspace (one chunk of its rounded outer products)."""
+    n = _C.c_size_t(0)
+    _check(lib().cflk_volta_opm_outer_workspace_size(B, C, D, E, _C.byref(n)), 'opm_outer')
+    return n.value
+
+
+def volta_opm_outer(left, right, wT, *, out=None, workspace=None):
+    """VoltaOpmOuter on 16 MSA rows: out [B,D,F] = sum_{c,e} h(sum_a left[a,b,c] right[a,d,e])
+    wT[f, c*E+e]; left [16,B,C], right [16,D,E], wT [F,C*E]. `workspace` (uint8, on the device)
+    defaults to cflk_volta_opm_outer_workspace_size bytes."""
+    who = 'opm_outer'
+    if (left.dim() != 3 or right.dim() != 3 or wT.dim() != 2 or left.shape[0] != 16 or
+            right.shape[0] != 16):
+        raise ValueError('opm_outer: left must be [16,B,C], right [16,D,E], wT [F,C*E]')
+    _, B, C = left.shape
+    _, D, E = right.shape
+    F = wT.shape[0]
+    if C % 16 or E != 32 or D % 4 or D // 4 > 65535 or wT.shape[1] != C * E or \
+            F not in (16, 32, 64, 128):
+        raise ValueError(
+            'opm_outer: C a multiple of 16, E 32, D a multiple of 4, F 16, 32, 64 or 128')
+    dt = _dtype_code(left, right, wT)
+    if out is None:
+        out = torch.empty((B, D, F), dtype=left.dtype, device=left.device)
+    if out.numel() != B * D * F or out.dtype != left.dtype:
+        raise ValueError('opm_outer: shapes do not match')
+    if B == 0 or D == 0 or C == 0:
+        return out
+    if workspace is None:
+        workspace = torch.empty(max(opm_outer_workspace_size(B, C, D, E), 16), dtype=torch.uint8,
+                                device=left.device)
+    rc = lib().cflk_volta_opm_outer(_stream(), dt, _ptr(left), _ptr(right), _ptr(wT), _ptr(out),
+                                    B, C, D, E, F, _ptr(workspace), workspace.numel())
     _check(rc, who)
     return out
 

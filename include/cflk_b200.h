@@ -226,6 +226,24 @@ CFLK_API int cflk_volta_opm_update(void* stream, int dtype, const void* lhs, con
                                    void* out, int64_t B, int64_t K, int64_t D, int64_t F,
                                    float eps);
 
+/* VoltaOpmOuter on 16 MSA rows: out [B,D,F] = sum over c, e of h(sum_a left[a,b,c] right[a,d,e])
+ * wT[f, c*E + e], h the rounding of the float32 inner product to the 16-bit type (AF2's order).
+ * left [16,B,C], right [16,D,E], wT [F,C*E], out [B,D,F], all 16-bit. The reference's limits: C a
+ * multiple of 16, E 32, D a multiple of 4 with D/4 at most 65535, F 16, 32, 64 or 128. Two
+ * persistent tcgen05 tile GEMMs per chunk of b: the outer products (K = 16, rounded, written
+ * as G2 [b][d][c][e] into the workspace; a CUDA-core kernel when C does not divide 128) and
+ * G2 [b*D, C*E] times wT. The workspace holds one chunk of G2 (whole multiples of 128/C rows
+ * of b, about 64 MB, so a chunk stays in L2 between the two products):
+ * cflk_volta_opm_outer_workspace_size gives the recommended size; a smaller workspace (at least
+ * one chunk of 128/C rows) runs more chunks. Buffers 16-byte aligned. Replaces VoltaOpmOuter,
+ * cuda/volta_fused_ffi.h:300-335, kernel cuda/volta_ops.cu:710-787 (whose handler takes no
+ * scratch: an FFI shim takes the workspace from XLA's scratch allocator). */
+CFLK_API int cflk_volta_opm_outer_workspace_size(int64_t B, int64_t C, int64_t D, int64_t E,
+                                                 size_t* bytes);
+CFLK_API int cflk_volta_opm_outer(void* stream, int dtype, const void* left, const void* right,
+                                  const void* wT, void* out, int64_t B, int64_t C, int64_t D,
+                                  int64_t E, int64_t F, void* workspace, size_t ws_bytes);
+
 /* The triangle multiplication's contraction between VoltaLnGdp and VoltaTrimulEpilogue (in the
  * reference an XLA einsum with a float32 result, tests/test_fused.py:135): for each channel c,
  *   incoming = 0 (AF2's outgoing edges): out[c,i,j] = sum_k a[c,i,k] b[c,j,k], a [C,I,K], b [C,J,K];

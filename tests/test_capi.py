@@ -114,11 +114,28 @@ def test_workspace_size_refuses_overflowing_sizes():
     assert b'static scratch' in l.cflk_last_error()
 
 
+def test_opm_outer_workspace_size():
+    """One chunk of G2 [b][d][c][e] (16-bit), whole multiples of 128 / C rows of b, about 64 MB
+    (or the whole problem when smaller); refusals before any CUDA call."""
+    l = lib()
+    n = ctypes.c_size_t(0)
+    i64 = ctypes.c_int64
+    per_b = 512 * 32 * 32 * 2
+    assert l.cflk_volta_opm_outer_workspace_size(i64(512), i64(32), i64(512), i64(32),
+                                                 ctypes.byref(n)) == 0
+    assert n.value == (64 << 20) // per_b // 4 * 4 * per_b
+    assert l.cflk_volta_opm_outer_workspace_size(i64(3), i64(32), i64(8), i64(32),
+                                                 ctypes.byref(n)) == 0
+    assert n.value == 3 * 8 * 32 * 32 * 2
+    assert l.cflk_volta_opm_outer_workspace_size(i64(3), i64(32), i64(8), i64(16),
+                                                 ctypes.byref(n)) == 1
+
+
 def test_resolver_capabilities():
     assert clk.supported_capabilities() == (70, 75, 100)
     for k in ('attention', 'attention_bwd', 'ln_gated_dual_proj', 'trimul_epilogue',
               'ln_projection', 'output_projection', 'transition', 'layer_norm',
-              'gated_dual_proj', 'opm_update'):
+              'gated_dual_proj', 'opm_update', 'opm_outer'):
         assert clk.available(100, k)
         assert clk.library_path(k, 100).endswith('sm100/libcflk_sm100.so')
     assert clk.symbol('attention', 100) == 'VoltaMma'
@@ -129,17 +146,15 @@ def test_resolver_capabilities():
     assert clk.symbol('attention', 75) == 'VoltaMma'
     assert clk.symbol('attention', 70) == 'VoltaWmma'
     assert clk.symbol('transition', 70) == 'VoltaTransitionWmma'
-    # opm_outer has no cc=100 entry yet, so the all-kernel check is False
-    assert not clk.available(100)
-    assert not clk.available(100, 'opm_outer')
+    # every kernel has a cc=100 entry; sm_80 has none
+    assert clk.available(100)
     assert not clk.available(80)
     assert clk.symbol('layer_norm', 100) == 'VoltaLayerNorm'
     assert clk.c_symbol('layer_norm', 100) == 'cflk_volta_layer_norm'
     assert clk.symbol('gated_dual_proj', 100) == 'VoltaGdp'
     assert clk.symbol('opm_update', 100) == 'VoltaOpmUpdate'
     assert clk.c_symbol('opm_update', 100) == 'cflk_volta_opm_update'
-    with pytest.raises(FileNotFoundError):
-        clk.symbol('opm_outer', 100)
+    assert clk.c_symbol('opm_outer', 100) == 'cflk_volta_opm_outer'
     with pytest.raises(KeyError):
         clk.library_path('nonexistent', 100)
     assert clk.kernel_dir(100).endswith('sm100')

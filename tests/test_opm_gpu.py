@@ -1,5 +1,5 @@
-"""VoltaOpmUpdate on the B200 (the tcgen05 tile GEMM with the fused epilogue) against the CPU
-oracle (oracle/fused.py opm_update).
+"""VoltaOpmUpdate and VoltaOpmOuter on the B200 (the tcgen05 tile GEMMs) against the CPU oracle
+(oracle/fused.py opm_update, opm_outer).
 
 The grid and recipe follow the reference's tests/test_opm.py: B 1, 37 and 260, D 4, 64 and 260,
 K 32, 64 and 512, F 128 and 64 (here also 16 and 32), lhs ~ N(0,1), t ~ N(0,1) K^-1/2, bias ~ 0.1
@@ -106,3 +106,63 @@ def test_opm_update_refusals(cuda_device):
         b200().volta_opm_update(z(4, 32), z(32, 3, 16), f(16), f(4, 4), eps=1e-3)
     with pytest.raises(ValueError, match='must be float32'):
         b200().volta_opm_update(z(4, 32), z(32, 3, 16), z(16), f(4, 3), eps=1e-3)
+
+
+# ---- opm_outer (VoltaOpmOuter) ----------------------------------------------------------------
+
+def outer_case(B, D, C, F, dt, seed):
+    rng = np.random.default_rng(seed)
+    left = round_to(rng.standard_normal((16, B, C)), dt)
+    right = round_to(rng.standard_normal((16, D, 32)), dt)
+    wT = round_to(rng.standard_normal((F, C * 32)) * (C * 32) ** -.5, dt)
+    return left, right, wT
+
+
+def run_outer(left, right, wT, dt, d, workspace=None):
+    h = lambda a: torch.tensor(np.asarray(a, np.float32), dtype=TD[dt], device=d)
+    got = b200().volta_opm_outer(h(left), h(right), h(wT), workspace=workspace)
+    assert b200().device_status() == 0
+    return got.float().cpu().numpy().astype(np.float64)
+
+
+@pytest.mark.parametrize('F', [128, 64])
+@pytest.mark.parametrize('B,D', [(1, 4), (37, 64), (260, 260), (1, 260), (260, 4)])
+def test_opm_outer_f16(B, D, F, cuda_device):
+    """The reference's grid (tests/test_opm.py:112-125): B and D of 1/37/260 and 4/64/260 on 16
+    rows with AF2's 32 channels, against the outer product rounded to f16 then contracted in
+    float32 (its outer_f32), rel-max 2e-3."""
+    left, right, wT = outer_case(B, D, 32, F, 'f16', B + D + F)
+    want = of.opm_outer(left, right, wT, 'f16')
+    close('opm_outer B=%d D=%d F=%d' % (B, D, F), run_outer(left, right, wT, 'f16', cuda_device),
+          want, 'f16')
+
+
+@pytest.mark.parametrize('C', [16, 64, 128, 48])
+@pytest.mark.parametrize('F', [16, 32, 128])
+def test_opm_outer_channels_bf16(C, F, cuda_device):
+    """Other channel counts (C = 48 does not divide 128: the CUDA-core first product) and F, bf16."""
+    left, right, wT = outer_case(45, 36, C, F, 'bf16', C + F)
+    want = of.opm_outer(left, right, wT, 'bf16')
+    close('opm_outer C=%d F=%d' % (C, F), run_outer(left, right, wT, 'bf16', cuda_device), want,
+          'bf16')
+
+
+def test_opm_outer_chunked_workspace(cuda_device):
+    """A workspace of one chunk (128 / C rows of b) runs the batch in many chunks, the same result."""
+    left, right, wT = outer_case(70, 68, 32, 128, 'f16', 3)
+    want = of.opm_outer(left, right, wT, 'f16')
+    ws = torch.empty(4 * 68 * 32 * 32 * 2, dtype=torch.uint8, device=cuda_device)
+    close('opm_outer chunked', run_outer(left, right, wT, 'f16', cuda_device, ws), want, 'f16')
+    with pytest.raises(ValueError, match='workspace below one chunk'):
+        run_outer(left, right, wT, 'f16', cuda_device, ws[:4 * 68 * 32 * 32 * 2 - 16])
+
+
+def test_opm_outer_refusals(cuda_device):
+    d = cuda_device
+    z = lambda *s: torch.zeros(s, dtype=torch.float16, device=d)
+    with pytest.raises(ValueError, match='C a multiple of 16'):
+        b200().volta_opm_outer(z(16, 4, 24), z(16, 4, 32), z(16, 24 * 32))
+    with pytest.raises(ValueError, match='D a multiple of 4'):
+        b200().volta_opm_outer(z(16, 4, 32), z(16, 6, 32), z(16, 32 * 32))
+    with pytest.raises(ValueError, match='left must be'):
+        b200().volta_opm_outer(z(8, 4, 32), z(16, 4, 32), z(16, 32 * 32))

@@ -441,13 +441,19 @@ def run_ours(args):
                                 device_id=dev)
     pk, pk_kind = peaks()
 
-    if args.only_fusion:
-        # one pair-fusion line alone (profiling runs): its warm-up and timed launches only
+    if args.only_fusion or args.only_next:
+        # one pair-fusion or next-row line alone (profiling runs): its warm-up and timed
+        # launches only
         flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-        res = bench_fusions(torch, b200, dev, rank, world, args.steps, args.warmup, flush, pk,
-                            only=args.only_fusion)
+        if args.only_fusion:
+            res = {'fusions': bench_fusions(torch, b200, dev, rank, world, args.steps,
+                                            args.warmup, flush, pk, only=args.only_fusion)}
+        else:
+            only = None if args.only_next == 'all' else args.only_next
+            res = {'next_rows': bench_next_rows(torch, b200, dev, rank, world, args.steps,
+                                                args.warmup, flush, pk, only=only)}
         if rank == 0:
-            print(json.dumps({'fusions': res}), flush=True)
+            print(json.dumps(res), flush=True)
         if world > 1:
             dist.barrier()
             dist.destroy_process_group()
@@ -1078,6 +1084,8 @@ def main():
     ap.add_argument('--impl', choices=('ours', 'reference'), default='ours')
     ap.add_argument('--no-cpu', action='store_true', help='skip the cpu_baseline sample')
     ap.add_argument('--no-fusions', action='store_true', help='skip the pair-fusion lines')
+    ap.add_argument('--only-next', default=None, metavar='NAME',
+                    help="run only the next-row line whose name starts with NAME ('all': each)")
     ap.add_argument('--no-next', action='store_true',
                     help='skip the next-row lines (triangle contraction, OPM, wide Gdp)')
     ap.add_argument('--no-e2e', action='store_true', help='skip the host-buffer end-to-end leg')

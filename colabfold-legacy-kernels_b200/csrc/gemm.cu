@@ -32,7 +32,7 @@ namespace {
 __device__ unsigned g_status;
 
 constexpr int GBM = 128, GBK = 64;
-constexpr int kGemmThreads = 256;
+constexpr int kGemmThreads = 384;  // TMA warp, MMA warp, two idle, two epilogue warpgroups
 constexpr int kEpiWarp0 = 4;
 // a wait for copies or MMAs already issued, at the end of a CTA (the pipeline's own waits give up
 // after 2 s and set the abort flag; these then bound the drain)
@@ -135,12 +135,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     __shared__ uint64_t full[C::STAGES], empty[C::STAGES], acc_full[2], acc_empty[2], drain,
-        res_full[2];
+        res_full[2][2];
     __shared__ uint32_t tmem_sh;
     __shared__ int abort_flag;
-    // per-column epilogue constants: VoltaOpmUpdate's bias [F] (F <= 128), VoltaGdp's bp and bg
-    // of the tile's 128 columns
-    __shared__ __align__(16) float colv[2][128];
+    // per-column epilogue constants: VoltaOpmUpdate's bias [F] (F <= 128); VoltaGdp's bp and bg
+    // of each epilogue warpgroup's 64 columns of the tile
+    __shared__ __align__(16) float bias_sh[128];
+    __shared__ __align__(16) float colv[2][2][64];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ntm = (a.M + GBM - 1) / GBM, ntn = (a.N + BN - 1) / BN;
@@ -156,8 +157,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
             for (int i = 0; i < 2; ++i) {
                 mbar_init(&acc_full[i], 1);
-                mbar_init(&acc_empty[i], 128);
-                mbar_init(&res_full[i], 1);
+                mbar_init(&acc_empty[i], 256);  // both epilogue warpgroups
+                mbar_init(&res_full[0][i], 1);
+                mbar_init(&res_full[1][i], 1);
             }
             mbar_init(&drain, 1);
             abort_flag = 0;
@@ -169,7 +171,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     } else if (warp >= kEpiWarp0 && KIND == kOpmUpdate) {
         const int i = threadIdx.x - kEpiWarp0 * 32;
         if (i < a.F) {
-            colv[0][i] = a.bias_f[i];
+            bias_sh[i] = a.bias_f[i];
         }
     }
     tc_fence_before();
@@ -277,9 +279,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         mma_commit(&drain);
         mbar_wait(&drain, 0, &g_status, kStatusMmaWait, nullptr, kDrainLimitNs);
     } else if (warp >= kEpiWarp0) {
-        // epilogue: thread r owns tile row r (tensor-memory lane r)
+        // epilogue: two warpgroups, each over all 128 rows (thread r = row r = tensor-memory
+        // lane r) and half of the tile's columns: warpgroup g takes the 32-column chunks
+        // [g NCH/2, (g+1) NCH/2), its own staging boxes, named barrier 1 + g and leader thread
+        constexpr int NCH = BN / 32, HCH = NCH / 2;
+        const int g = (warp - kEpiWarp0) >> 2;
         const int r = ((warp & 3) << 5) | lane;
-        const bool leader = threadIdx.x == kEpiWarp0 * 32;
+        const bool leader = lane == 0 && (warp & 3) == 0;
         const uint32_t lane_base = tmem_lane_base(warp);
         uint8_t* ostage = smem + C::OUT_OFF;
         [[maybe_unused]] const bool has_res = KIND == kOpmUpdate && a.residual != nullptr;
@@ -289,17 +295,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             m0 = (rem % ntm) * GBM;
             n0 = (rem / ntm) * BN;
         };
-        // VoltaOpmUpdate: the residual tile by TMA into staging pair p (expect the bytes of
-        // both boxes; columns or rows past the ends read as zero)
+        // 16-bit kinds: warpgroup g's 64 columns are one box, VoltaOpmUpdate's in staging pair
+        // p (box 2p + g), the others' box g
+        const auto box16 = [&](int p) -> uint8_t* {
+            return ostage + ((KIND == kOpmUpdate ? 2 * p : 0) + g) * C::BOX_BYTES;
+        };
+        // VoltaOpmUpdate: this warpgroup's residual box of a tile by TMA into pair p (columns or
+        // rows past the ends read as zero)
         int res_issued[2] = {0, 0};  // residual loads per staging pair (the leader's count)
         const auto load_res = [&](int tile, int p) {
             int bt, m0, n0;
             tile_origin(tile, bt, m0, n0);
             ++res_issued[p];
-            mbar_arrive_expect_tx(&res_full[p], 2 * C::BOX_BYTES);
-            tma_load_3d(ostage + (2 * p) * C::BOX_BYTES, &tb1, &res_full[p], n0, m0, bt);
-            tma_load_3d(ostage + (2 * p + 1) * C::BOX_BYTES, &tb1, &res_full[p], n0 + 64, m0,
-                        bt);
+            mbar_arrive_expect_tx(&res_full[g][p], C::BOX_BYTES);
+            tma_load_3d(box16(p), &tb1, &res_full[g][p], n0 + 64 * g, m0, bt);
         };
         if constexpr (KIND == kOpmUpdate) {
             if (has_res && leader && blockIdx.x < ntiles) {
@@ -325,12 +334,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 }
             }
             if constexpr (KIND == kGdpDual) {
-                // this tile's bp and bg, one column a thread
-                const int n = n0 + r;
-                colv[0][r] = n < a.N ? E::to_f(static_cast<const T*>(a.bp)[n]) : 0.f;
-                colv[1][r] = n < a.N ? E::to_f(static_cast<const T*>(a.bg)[n]) : 0.f;
+                // this warpgroup's 64 columns of bp and bg
+                if (r < 64) {
+                    const int n = n0 + 64 * g + r;
+                    colv[g][0][r] = n < a.N ? E::to_f(static_cast<const T*>(a.bp)[n]) : 0.f;
+                    colv[g][1][r] = n < a.N ? E::to_f(static_cast<const T*>(a.bg)[n]) : 0.f;
+                }
             }
-            named_sync(1, 128);
+            named_sync(1 + g, 128);
             [[maybe_unused]] float mval = 0.f;
             [[maybe_unused]] float rden[8];
             if constexpr (KIND == kGdpDual) {
@@ -347,7 +358,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                   : 0.f;
                 }
                 if (has_res) {
-                    mbar_wait(&res_full[buf], (lt >> 1) & 1, &g_status, kStatusTmaWait,
+                    mbar_wait(&res_full[g][buf], (lt >> 1) & 1, &g_status, kStatusTmaWait,
                               &abort_flag);
                 }
             }
@@ -355,7 +366,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             tc_fence_after();
             const uint32_t acc = tmem + buf * C::ACC_COLS + lane_base;
 #pragma unroll
-            for (int ch = 0; ch < BN / 32; ++ch) {
+            for (int hc = 0; hc < HCH; ++hc) {
+                const int ch = g * HCH + hc;  // the chunk of the tile's columns
                 uint32_t r0[32];
                 [[maybe_unused]] uint32_t r1[32];
                 tmem_ld32(acc + 32 * ch, r0);
@@ -364,27 +376,29 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 }
                 tmem_wait_ld();
                 if constexpr (KIND == kContract) {
-                    // the float32 products as they are: box ch in ring slot ch % 4, row r,
-                    // 8 pieces of 4 floats at piece (p ^ (r % 8)); the slot is free once the
-                    // store of the box four before it has read it
+                    // the float32 products as they are: the warpgroup's boxes alternate between
+                    // its two ring slots (2g, 2g + 1), row r, 8 pieces of 4 floats at piece
+                    // (p ^ (r % 8)); a slot is free once the store of the box two before it has
+                    // read it
                     if (leader) {
-                        bulk_wait_read<3>();
+                        bulk_wait_read<1>();
                     }
-                    named_sync(1, 128);
-                    uint8_t* slot = ostage + (box & 3) * C::BOX_BYTES;
+                    named_sync(1 + g, 128);
+                    uint8_t* slot = ostage + (2 * g + (box & 1)) * C::BOX_BYTES;
                     uint8_t* row = slot + r * 128;
 #pragma unroll
                     for (int p = 0; p < 8; ++p) {
                         *reinterpret_cast<uint4*>(row + ((p ^ (r & 7)) << 4)) =
                             make_uint4(r0[4 * p], r0[4 * p + 1], r0[4 * p + 2], r0[4 * p + 3]);
                     }
-                    if (ch == BN / 32 - 1) {
-                        // every column is in registers or staging: the buffer is free
+                    if (hc == HCH - 1) {
+                        // every column of this warpgroup is in staging: its share of the
+                        // buffer is free
                         tc_fence_before();
                         mbar_arrive(&acc_empty[buf]);
                     }
                     fence_async_smem();
-                    named_sync(1, 128);
+                    named_sync(1 + g, 128);
                     if (leader) {
                         if (n0 + 32 * ch < a.N) {
                             tma_store_3d(&to, smem_u32(slot), n0 + 32 * ch, m0, bt);
@@ -393,11 +407,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     }
                     ++box;
                 } else if constexpr (KIND == kOpmOuterG) {
-                    // row r = (b_l, c), columns 32 ch.. = d_l ch, e 0..31: 64 bytes at
-                    // [b_l][d_l][c][e] of the [128/C][4][C][32] box (plain layout, a warp's 32
-                    // rows are 32 consecutive 64-byte runs)
+                    // row r = (b_l, c), chunk ch = d_l (e 0..31): 64 bytes at [b_l][d_l - 2g][c]
+                    // of the warpgroup's [128/C][2][C][32] box (plain layout, a warp's 32 rows
+                    // are 32 consecutive 64-byte runs)
                     const int bl = r / a.opm_c, cl = r - bl * a.opm_c;
-                    uint8_t* dst = ostage + (((bl * 4 + ch) * a.opm_c) + cl) * 64;
+                    uint8_t* dst = ostage + g * C::BOX_BYTES + (((bl * 2 + hc) * a.opm_c) + cl) * 64;
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
                         uint4 w;
@@ -413,10 +427,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 } else {
                     const int nb = n0 + 32 * ch;
                     float v[32];
-                    // staging pieces of these 32 columns: box (ch / 2) of the tile's pair, row r,
-                    // pieces 4 (ch % 2) + q at (c ^ (r % 8))
-                    const int pair = KIND == kOpmUpdate ? 2 * buf : 0;
-                    uint8_t* row = ostage + (pair + (ch >> 1)) * C::BOX_BYTES + r * 128;
+                    // staging pieces of these 32 columns: the warpgroup's box, row r, pieces
+                    // 4 hc + q at (c ^ (r % 8))
+                    uint8_t* row = box16(buf) + r * 128;
                     if constexpr (KIND == kOpmUpdate) {
                         // (acc + bias[f]) / (eps + norm[m, d]) (+ residual), n = d F + f: the 32
                         // columns span at most two d (F = 16)
@@ -427,10 +440,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                             rd0 = i == i0 ? rden[i] : rd0;
                             rd1 = i == i1 ? rden[i] : rd1;
                         }
-                        const float* bias = &colv[0][nb & (a.F - 1)];
+                        const float* bias = &bias_sh[nb & (a.F - 1)];
 #pragma unroll
                         for (int q = 0; q < 4; ++q) {
-                            const int c = 4 * (ch & 1) + q;
+                            const int c = 4 * hc + q;
                             uint4 res = make_uint4(0, 0, 0, 0);
                             if (has_res) {
                                 res = *reinterpret_cast<const uint4*>(row + ((c ^ (r & 7)) << 4));
@@ -456,15 +469,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         // mask * (p + bp) * act(g + bg)
 #pragma unroll
                         for (int i = 0; i < 32; ++i) {
-                            const float p = __uint_as_float(r0[i]) + colv[0][32 * ch + i];
-                            const float g = __uint_as_float(r1[i]) + colv[1][32 * ch + i];
-                            const float sg = fused::sigmoid_fast(g);
-                            v[i] = mval * p * (a.act == 0 ? sg : g * sg);
+                            const float p = __uint_as_float(r0[i]) + colv[g][0][32 * hc + i];
+                            const float gt = __uint_as_float(r1[i]) + colv[g][1][32 * hc + i];
+                            const float sg = fused::sigmoid_fast(gt);
+                            v[i] = mval * p * (a.act == 0 ? sg : gt * sg);
                         }
                     }
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
-                        const int c = 4 * (ch & 1) + q;
+                        const int c = 4 * hc + q;
                         uint4 w;
                         w.x = E::pack(v[8 * q], v[8 * q + 1]);
                         w.y = E::pack(v[8 * q + 2], v[8 * q + 3]);
@@ -475,24 +488,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 }
             }
             if constexpr (KIND != kContract) {
-                // the accumulator buffer is free; the staged tile goes out by TMA
+                // this warpgroup's share of the accumulator buffer is free; its staged box goes
+                // out by TMA
                 tc_fence_before();
                 mbar_arrive(&acc_empty[buf]);
                 fence_async_smem();
-                named_sync(1, 128);
+                named_sync(1 + g, 128);
                 if (leader) {
-                    if constexpr (KIND == kOpmOuterG) {
-                        // the whole tile as one [128/C b][4 d][C c][32 e] box of G2
-                        tma_store_4d(&to, smem_u32(ostage), 0, 0, n0 / 32, m0 / a.opm_c);
+                    if (n0 + 64 * g >= a.N) {
+                        // nothing of this warpgroup's columns is inside the output
+                    } else if constexpr (KIND == kOpmOuterG) {
+                        // d 2g, 2g + 1 of the tile as one [128/C b][2 d][C c][32 e] box of G2
+                        tma_store_4d(&to, smem_u32(ostage + g * C::BOX_BYTES), 0, 0,
+                                     n0 / 32 + 2 * g, m0 / a.opm_c);
                     } else {
-                        const int pair = KIND == kOpmUpdate ? 2 * buf : 0;
-#pragma unroll
-                        for (int q = 0; q < C::BOXES; ++q) {
-                            if (n0 + q * C::BOX_COLS < a.N) {
-                                tma_store_3d(&to, smem_u32(ostage + (pair + q) * C::BOX_BYTES),
-                                             n0 + q * C::BOX_COLS, m0, bt);
-                            }
-                        }
+                        tma_store_3d(&to, smem_u32(box16(buf)), n0 + 64 * g, m0, bt);
                     }
                     bulk_commit();
                 }
@@ -505,7 +515,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             if constexpr (KIND == kOpmUpdate) {
                 for (int p = 0; p < 2; ++p) {
                     if (res_issued[p] > 0) {
-                        mbar_wait(&res_full[p], (res_issued[p] - 1) & 1, &g_status,
+                        mbar_wait(&res_full[g][p], (res_issued[p] - 1) & 1, &g_status,
                                   kStatusTmaWait, nullptr, kDrainLimitNs);
                     }
                 }
@@ -545,7 +555,7 @@ cudaError_t launch_gemm(cudaStream_t stream, int dtype, const void* A, const voi
         // G2 [b][d][c][e]: M = B C rows (b, c), N = D 32 columns (d, e)
         const uint64_t Cc = a.opm_c, D = N / 32, Bb = M / Cc;
         const uint64_t dg[4] = {32, Cc, D, Bb}, sg[3] = {32, 32 * Cc, 32 * Cc * D};
-        const uint32_t boxg[4] = {32, (uint32_t)Cc, 4, (uint32_t)(GBM / Cc)};
+        const uint32_t boxg[4] = {32, (uint32_t)Cc, 2, (uint32_t)(GBM / Cc)};
         map_ok = encode_tiled(&to, tdt, 2, 4, out, dg, sg, boxg, CU_TENSOR_MAP_SWIZZLE_NONE);
     } else if (map_ok) {
         map_ok = encode_tiled(&to, odt, C::OUT_ELEM, 3, out, dout, sout, boxo,

@@ -22,6 +22,9 @@ __attribute__((weak)) unsigned read_and_clear_status_fused() {
 __attribute__((weak)) unsigned read_and_clear_status_gemm() {
     return 0;
 }
+__attribute__((weak)) unsigned read_and_clear_status_opm() {
+    return 0;
+}
 
 int fail(int code, const std::string& msg) {
     t_last_error = msg;
@@ -44,5 +47,6 @@ extern "C" int cflk_version(void) {
 
 extern "C" unsigned cflk_device_status(void) {
     return cflk::read_and_clear_status_fwd() | cflk::read_and_clear_status_bwd() |
-           cflk::read_and_clear_status_fused() | cflk::read_and_clear_status_gemm();
+           cflk::read_and_clear_status_fused() | cflk::read_and_clear_status_gemm() |
+           cflk::read_and_clear_status_opm();
 }

@@ -229,11 +229,13 @@ CFLK_API int cflk_volta_opm_update(void* stream, int dtype, const void* lhs, con
 /* VoltaOpmOuter on 16 MSA rows: out [B,D,F] = sum over c, e of h(sum_a left[a,b,c] right[a,d,e])
  * wT[f, c*E + e], h the rounding of the float32 inner product to the 16-bit type (AF2's order).
  * left [16,B,C], right [16,D,E], wT [F,C*E], out [B,D,F], all 16-bit. The reference's limits: C a
- * multiple of 16, E 32, D a multiple of 4 with D/4 at most 65535, F 16, 32, 64 or 128. Two
- * persistent tcgen05 tile GEMMs per chunk of b: the outer products (K = 16, rounded, written
- * as G2 [b][d][c][e] into the workspace; a CUDA-core kernel when C does not divide 128) and
- * G2 [b*D, C*E] times wT. The workspace holds one chunk of G2 (whole multiples of 128/C rows
- * of b, about 64 MB, so a chunk stays in L2 between the two products):
+ * multiple of 16, E 32, D a multiple of 4 with D/4 at most 65535, F 16, 32, 64 or 128. At
+ * AF2's C = 32 one fused kernel: per 16 b x 16 d tile and chunk of 8 c x 8 e, a tcgen05 MMA of
+ * the outer products into tensor memory, rounded by a converter warpgroup into shared memory as
+ * the A operand of the MMAs against wT; no workspace (its size is 0). Other C: two persistent
+ * tile GEMMs per chunk of b, the outer products (K = 16, rounded, written as G2 [b][d][c][e]
+ * into the workspace; a CUDA-core kernel when C does not divide 128) and G2 [b*D, C*E] times
+ * wT; the workspace holds one chunk of G2 (whole multiples of 128/C rows of b, about 64 MB):
  * cflk_volta_opm_outer_workspace_size gives the recommended size; a smaller workspace (at least
  * one chunk of 128/C rows) runs more chunks. Buffers 16-byte aligned. Replaces VoltaOpmOuter,
  * cuda/volta_fused_ffi.h:300-335, kernel cuda/volta_ops.cu:710-787 (whose handler takes no

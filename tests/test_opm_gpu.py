@@ -148,13 +148,30 @@ def test_opm_outer_channels_bf16(C, F, cuda_device):
 
 
 def test_opm_outer_chunked_workspace(cuda_device):
-    """A workspace of one chunk (128 / C rows of b) runs the batch in many chunks, the same result."""
-    left, right, wT = outer_case(70, 68, 32, 128, 'f16', 3)
+    """C = 64 (the two-GEMM path): a workspace of one chunk (128 / C rows of b) runs the batch in
+    many chunks, the same result."""
+    left, right, wT = outer_case(70, 68, 64, 128, 'f16', 3)
     want = of.opm_outer(left, right, wT, 'f16')
-    ws = torch.empty(4 * 68 * 32 * 32 * 2, dtype=torch.uint8, device=cuda_device)
+    ws = torch.empty(2 * 68 * 64 * 32 * 2, dtype=torch.uint8, device=cuda_device)
     close('opm_outer chunked', run_outer(left, right, wT, 'f16', cuda_device, ws), want, 'f16')
     with pytest.raises(ValueError, match='workspace below one chunk'):
-        run_outer(left, right, wT, 'f16', cuda_device, ws[:4 * 68 * 32 * 32 * 2 - 16])
+        run_outer(left, right, wT, 'f16', cuda_device, ws[:2 * 68 * 64 * 32 * 2 - 16])
+
+
+@pytest.mark.parametrize('dt', ['bf16', 'f16'])
+@pytest.mark.parametrize('B,D,F', [(768, 768, 128), (300, 36, 16), (17, 100, 32), (64, 64, 64)])
+def test_opm_outer_fused_sizes(B, D, F, dt, cuda_device):
+    """The fused C = 32 kernel at AF2's pair size (768^2, F = c_z = 128, sampled rows checked) and
+    at sizes with partial 16 x 16 tiles and narrow F."""
+    left, right, wT = outer_case(B, D, 32, F, dt, B + D)
+    if B * D > 100000:
+        rows = np.random.default_rng(1).choice(B, 24, replace=False)
+        got = run_outer(left, right, wT, dt, cuda_device)[rows]
+        want = of.opm_outer(left[:, rows], right, wT, dt)
+    else:
+        got = run_outer(left, right, wT, dt, cuda_device)
+        want = of.opm_outer(left, right, wT, dt)
+    close('opm_outer fused B=%d D=%d F=%d' % (B, D, F), got, want, dt)
 
 
 def test_opm_outer_refusals(cuda_device):

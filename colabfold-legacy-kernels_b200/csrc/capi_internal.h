@@ -24,9 +24,11 @@ unsigned read_and_clear_status_fused();
 unsigned read_and_clear_status_gemm();
 unsigned read_and_clear_status_opm();
 
-// VoltaOpmOuter fused at C = E = 32 (the caller has validated the sizes)
+// VoltaOpmOuter fused at C = E = 32 (the caller has validated the sizes); the workspace holds
+// wT laid out chunk by chunk (F * 2 KB)
 int opm_outer_fused(void* stream, int dtype, const void* left, const void* right, const void* wT,
-                    void* out, int64_t B, int64_t D, int64_t F);
+                    void* out, int64_t B, int64_t D, int64_t F, void* workspace,
+                    size_t ws_bytes);
 
 // VoltaGdp through the tile GEMM (widths the resident-weight row-tile kernel does not take)
 int gdp_general(void* stream, int dtype, const void* x, const void* wp, const void* bp,

@@ -1032,8 +1032,12 @@ extern "C" int cflk_volta_opm_outer_workspace_size(int64_t B, int64_t C, int64_t
     if (__builtin_mul_overflow(D, C * E * 2, &per_b)) {
         return fail(kInvalidArgument, "opm_outer: workspace size overflows");
     }
-    if (per_b == 0 || B == 0 || C == 32) {
-        *bytes = 0;  // C = 32 runs the fused kernel, which needs no workspace
+    if (C == 32) {
+        *bytes = size_t(128) * 32 * 32 * 2;  // the fused kernel: wT laid out (F at most 128)
+        return kOk;
+    }
+    if (per_b == 0 || B == 0) {
+        *bytes = 0;
         return kOk;
     }
     const int64_t blk = opm_outer_block(C);
@@ -1075,14 +1079,12 @@ extern "C" int cflk_volta_opm_outer(void* stream, int dtype, const void* left, c
         D * 32 >= (int64_t(1) << 31)) {
         return fail(kInvalidArgument, "opm_outer: sizes must be below 2^31");
     }
-    if (!aligned16(left) || !aligned16(right) || !aligned16(wT) || !aligned16(out)) {
+    if (!aligned16(left) || !aligned16(right) || !aligned16(wT) || !aligned16(out) ||
+        !aligned16(workspace)) {
         return fail(kInvalidArgument, "opm_outer: buffers must be 16-byte aligned");
     }
     if (C == 32) {
-        return opm_outer_fused(stream, dtype, left, right, wT, out, B, D, F);
-    }
-    if (!aligned16(workspace)) {
-        return fail(kInvalidArgument, "opm_outer: buffers must be 16-byte aligned");
+        return opm_outer_fused(stream, dtype, left, right, wT, out, B, D, F, workspace, ws_bytes);
     }
     const int64_t per_b = D * C * 64;  // G2 bytes of one b
     // b rows a chunk: all of them, or whole multiples of 128 / C

@@ -10,16 +10,17 @@
 //     8 e, both MN-major in the unswizzled (interleaved) layout: TMA boxes [16 b][16 a][8 c] and
 //     [16 d][16 a][8 e] whose 128-byte core matrices are 8 rows a of one b (or d); the result
 //     G[b, c, d, e] lands in one of two 128-column TMEM buffers;
-//   * a converter warpgroup (thread = lane = (b, c)) reads its 16 d x 8 e, rounds them to the
-//     16-bit type and writes them as rows (b, d) of a K-major [256 rows][8 c x 8 e] tile (the
-//     second product's A operand, two of them in shared memory);
+//   * two converter warpgroups (thread = lane = (b, c), one warpgroup a half of the d) read
+//     8 d x 8 e each, round them to the 16-bit type and write them as rows (b, d) of a K-major
+//     [256 rows][8 c x 8 e] tile (the second product's A operand, two of them in shared memory);
 //   * second product: two M = 128 MMAs (b 0-7 and b 8-15) of that tile against the chunk's
-//     slice of wT (K-major, unswizzled: one TMA box [F/8][8 c][8 f][8 e] from a 4-D view of wT),
-//     accumulating out [256 rows][F] in TMEM over the 16 chunks;
+//     slice of wT, accumulating out [256 rows][F] in TMEM over the 16 chunks; the slices are
+//     first laid out chunk by chunk ([16 chunks][F][8 c x 8 e], in the workspace) so that each
+//     arrives as one K-major 128-byte-swizzled box;
 //   * an epilogue warpgroup rounds the accumulators and writes each 128-row half with TMA
 //     stores of [8 b][16 d][64 f] boxes (rows and columns past B, D, F clip).
 // Warp 0 streams the tile's left/right blocks (one tile ahead) and the wT slices (a ring of
-// three); warp 1 issues every MMA, the next chunk's first product ahead of this chunk's second.
+// three); warp 1 issues every MMA, the first product two chunks ahead of the second.
 // All waits are bounded; a wait that gives up ends the loads and the MMAs, and the drains at the
 // end leave no copy or MMA in flight.
 #include <cuda.h>
@@ -41,8 +42,10 @@ __device__ unsigned g_status;
 
 constexpr int kTB = 16, kTD = 16;          // b and d of a tile
 constexpr int kChunks = (32 / 8) * (32 / 8);  // 8 c x 8 e chunks of K = 1024
-constexpr int kThreads = 384;              // TMA, MMA, two idle, converters, epilogue
-constexpr int kConvWarp0 = 4, kEpiWarp0 = 8;
+// warp 0 TMA, warp 1 MMA, warps 2-9 two converter warpgroups (d 0-7 and d 8-15 of a chunk),
+// warps 10-13 the epilogue; a warp reaches TMEM lanes 32 (warp % 4) ..
+constexpr int kThreads = 448;
+constexpr int kConvWarp0 = 2, kEpiWarp0 = 10;
 constexpr unsigned long long kDrain = 200000000ull;
 
 // Every TMA box below has 16-byte rows and no swizzle (a swizzled box wants rows as wide as the
@@ -50,7 +53,7 @@ constexpr unsigned long long kDrain = 200000000ull;
 constexpr int kBox = 16 * 16 * 8 * 2;      // one [16 b or d][16 a][8 c or e] box: 4 KB
 constexpr int A1_BYTES = 4 * kBox;         // left: 4 c-blocks
 constexpr int AB_BYTES = 8 * kBox;         // left then right (4 e-blocks)
-constexpr int W_BYTES = 128 * 128;         // [16 f-groups][8 c][8 f][8 e]
+constexpr int W_BYTES = 128 * 128;         // [128 f][8 c x 8 e], 128-byte swizzle
 constexpr int kWStages = 3;
 constexpr int G_BYTES = 2 * 128 * 128;     // two 128-row halves of [rows][128 bytes]
 constexpr int OUT_BOX = 128 * 128;         // [8 b][16 d][64 f]
@@ -113,7 +116,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_init(&ab_full[i], 1);
                 mbar_init(&ab_empty[i], 1);
                 mbar_init(&s1_full[i], 1);
-                mbar_init(&g_full[i], 128);
+                mbar_init(&g_full[i], 256);  // both converter warpgroups
                 mbar_init(&g_empty[i], 1);
             }
             for (int i = 0; i < kWStages; ++i) {
@@ -181,8 +184,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 mbar_arrive_expect_tx(&w_full[s], W_BYTES);
-                tma_load_4d(smem + SM_W + s * W_BYTES, &tw, &w_full[s], 8 * (k & 3), 0,
-                            8 * (k >> 2), 0);
+                tma_load_3d(smem + SM_W + s * W_BYTES, &tw, &w_full[s], 0, 0, k);
             }
         }
         // the last copies land before the CTA can exit
@@ -196,74 +198,85 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1 && lane == 0) {
         // MMAs. First product: A = left rows (b, c) and B = right columns (d, e), MN-major and
         // interleaved: core matrices [8 a][8 c or e], the next 8 of M or N (the next b or d) 256
-        // bytes on, the second 8 rows a 128 bytes on. Second product: A = the converted chunk
-        // (K-major, 128-byte swizzle), B = the wT slice (K-major, interleaved: the next 8 of K
-        // (c) 128 bytes on, the next 8 f 1 KB on).
+        // bytes on, the second 8 rows a 128 bytes on. Second product: A = the converted chunk,
+        // B = the wT slice (both K-major, 128-byte swizzle). Global chunk q is chunk q % 16 of
+        // local tile q / 16; its first product runs two chunks ahead of its second.
         const bool bf = E::kBf16;
         const uint32_t id1 = idesc_f16(bf, 128, 128, true, true);
         const uint32_t id2 = idesc_f16(bf, 128, a.F, false, false);
         const uint32_t ab_base = smem_u32(smem + SM_AB), w_base = smem_u32(smem + SM_W),
                        g_base = smem_u32(smem + SM_G);
-        // chunk k: c-block k >> 2, e-block k & 3
-        const auto first = [&](int lt, int k, int q) {
-            const uint32_t ab = ab_base + (lt & 1) * AB_BYTES;
-            mma_ss(tmem + T_S1 + (q & 1) * 128,
+        const int total = ((ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x) *
+                          kChunks;
+        int ab_ready = -1;  // the last local tile whose blocks were waited for
+        const auto need_ab = [&](int lt) -> bool {
+            if (lt > ab_ready) {
+                if (!mbar_wait(&ab_full[lt & 1], (lt >> 1) & 1, &g_status, kStatusTmaWait,
+                               &abort_flag)) {
+                    return false;
+                }
+                tc_fence_after();
+                ab_ready = lt;
+            }
+            return true;
+        };
+        // chunk k: c-block k >> 2, e-block k & 3; its TMEM buffer was last read for chunk q - 2,
+        // whose conversion was waited for before that chunk's second product
+        const auto first = [&](int qq) {
+            const int k = qq % kChunks;
+            const uint32_t ab = ab_base + ((qq / kChunks) & 1) * AB_BYTES;
+            mma_ss(tmem + T_S1 + (qq & 1) * 128,
                    smem_desc(ab + (k >> 2) * kBox, 128, 256, kSwizzleNone),
                    smem_desc(ab + A1_BYTES + (k & 3) * kBox, 128, 256, kSwizzleNone), id1, 0u);
-            mma_commit(&s1_full[q & 1]);
+            mma_commit(&s1_full[qq & 1]);
         };
-        int lt = 0, q = 0, wq = 0;
-        bool ok = true;
-        for (int tile = blockIdx.x; ok && tile < ntiles; tile += gridDim.x, ++lt) {
-            if (!mbar_wait(&ab_full[lt & 1], (lt >> 1) & 1, &g_status, kStatusTmaWait,
-                           &abort_flag)) {
+        bool ok = total > 0 && need_ab(0);
+        if (ok) {
+            first(0);
+            first(1);
+        }
+        for (int q = 0; ok && q < total; ++q) {
+            const int lt = q / kChunks, k = q % kChunks, gb = q & 1, s = q % kWStages;
+            if (!mbar_wait(&g_full[gb], (q >> 1) & 1, &g_status, kStatusSyncWait, &abort_flag) ||
+                !mbar_wait(&w_full[s], (q / kWStages) & 1, &g_status, kStatusTmaWait,
+                           &abort_flag) ||
+                (k == 0 && lt >= 1 &&
+                 !mbar_wait(&acc_empty, (lt - 1) & 1, &g_status, kStatusSyncWait, &abort_flag))) {
                 break;
             }
             tc_fence_after();
-            first(lt, 0, q);
-            for (int k = 0; k < kChunks; ++k, ++q, ++wq) {
-                // the next chunk's first product runs while this chunk is converted (its TMEM
-                // buffer was last read for chunk q - 1, whose conversion was waited for)
-                if (k + 1 < kChunks) {
-                    first(lt, k + 1, q + 1);
+            const uint32_t ga = g_base + gb * G_BYTES, wa = w_base + s * W_BYTES;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+#pragma unroll
+                for (int ks = 0; ks < 4; ++ks) {
+                    mma_ss(tmem + T_ACC + h * 128,
+                           smem_desc(ga + h * (128 * 128) + 32 * ks, 16, 1024, kSwizzle128B),
+                           smem_desc(wa + 32 * ks, 16, 1024, kSwizzle128B), id2,
+                           (k > 0 || ks > 0) ? 1u : 0u);
                 }
-                const int gb = q & 1, s = wq % kWStages;
-                if (!mbar_wait(&g_full[gb], (q >> 1) & 1, &g_status, kStatusSyncWait,
-                               &abort_flag) ||
-                    !mbar_wait(&w_full[s], (wq / kWStages) & 1, &g_status, kStatusTmaWait,
-                               &abort_flag) ||
-                    (k == 0 && lt >= 1 &&
-                     !mbar_wait(&acc_empty, (lt - 1) & 1, &g_status, kStatusSyncWait,
-                                &abort_flag))) {
-                    ok = false;
+            }
+            mma_commit(&g_empty[gb]);
+            mma_commit(&w_empty[s]);
+            if (k == kChunks - 1) {
+                mma_commit(&ab_empty[lt & 1]);
+                mma_commit(&acc_full);
+            }
+            if (q + 2 < total) {
+                if (!need_ab((q + 2) / kChunks)) {
                     break;
                 }
-                tc_fence_after();
-                const uint32_t ga = g_base + gb * G_BYTES, wa = w_base + s * W_BYTES;
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-#pragma unroll
-                    for (int ks = 0; ks < 4; ++ks) {
-                        mma_ss(tmem + T_ACC + h * 128,
-                               smem_desc(ga + h * (128 * 128) + 32 * ks, 16, 1024, kSwizzle128B),
-                               smem_desc(wa + 256 * ks, 128, 1024, kSwizzleNone), id2,
-                               (k > 0 || ks > 0) ? 1u : 0u);
-                    }
-                }
-                mma_commit(&g_empty[gb]);
-                mma_commit(&w_empty[s]);
-                if (k == kChunks - 1) {
-                    mma_commit(&ab_empty[lt & 1]);
-                    mma_commit(&acc_full);
-                }
+                first(q + 2);
             }
         }
         mma_commit(&drain);
         mbar_wait(&drain, 0, &g_status, kStatusMmaWait, nullptr, kDrain);
     } else if (warp >= kConvWarp0 && warp < kEpiWarp0) {
-        // converters: thread = lane m = (b, c) = (m / 8, m % 8) of the first product; its 16 d x
-        // 8 e values go to rows (b, d) of the chunk tile, 16 bytes at piece c ^ (d % 8) of the
-        // row (128-byte swizzle), half b / 8
+        // converters: thread = lane m = (b, c) = (m / 8, m % 8) of the first product; warpgroup
+        // cg takes d 8 cg .. 8 cg + 7 (TMEM columns 64 cg ..), whose 8 e values go to rows (b, d)
+        // of the chunk tile, 16 bytes at piece c ^ (d % 8) of the row (128-byte swizzle), half
+        // b / 8
+        const int cg = (warp - kConvWarp0) >> 2;
         const int m = ((warp & 3) << 5) | lane;
         const int bl = m >> 3, cl = m & 7;
         const uint32_t lane_base = tmem_lane_base(warp);
@@ -274,7 +287,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int gb = q & 1;
             mbar_wait(&s1_full[gb], (q >> 1) & 1, &g_status, kStatusMmaWait, &abort_flag);
             tc_fence_after();
-            const uint32_t src = tmem + T_S1 + gb * 128 + lane_base;
+            const uint32_t src = tmem + T_S1 + gb * 128 + 64 * cg + lane_base;
             uint32_t v0[32], v1[32];
             tmem_ld32(src, v0);
             tmem_ld32(src + 32, v1);
@@ -297,13 +310,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     *reinterpret_cast<uint4*>(rows + d * 128 + ((cl ^ (d & 7)) << 4)) = w;
                 }
             };
-            put(v0, 0);
-            put(v1, 4);
-            tmem_ld32(src + 64, v0);
-            tmem_ld32(src + 96, v1);
-            tmem_wait_ld();
-            put(v0, 8);
-            put(v1, 12);
+            put(v0, 8 * cg);
+            put(v1, 8 * cg + 4);
             fence_async_smem();
             tc_fence_before();
             mbar_arrive(&g_full[gb]);
@@ -373,6 +381,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// wT [F][32 c][32 e] -> wr [16 chunks][F][8 c x 8 e], chunk k = (c-block k / 4, e-block k % 4):
+// one 16-byte run of 8 e a thread
+template <typename T>
+__global__ void opm_w_layout_kernel(const T* wT, T* wr, int F) {
+    const int n = 16 * F * 8;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const int cl = i & 7, f = (i >> 3) % F, k = (i >> 3) / F;
+        const int c = 8 * (k >> 2) + cl, e0 = 8 * (k & 3);
+        reinterpret_cast<uint4*>(wr)[i] =
+            *reinterpret_cast<const uint4*>(wT + (long long)f * 1024 + c * 32 + e0);
+    }
+}
+
 }  // namespace
 
 unsigned read_and_clear_status_opm() {
@@ -382,9 +403,15 @@ unsigned read_and_clear_status_opm() {
     return v;
 }
 
-// VoltaOpmOuter at C = E = 32 (validated by the caller), no workspace
+// VoltaOpmOuter at C = E = 32 (validated by the caller); the workspace takes wT laid out chunk by
+// chunk (F * 2 KB)
 int opm_outer_fused(void* stream, int dtype, const void* left, const void* right, const void* wT,
-                    void* out, int64_t B, int64_t D, int64_t F) {
+                    void* out, int64_t B, int64_t D, int64_t F, void* workspace,
+                    size_t ws_bytes) {
+    if (workspace == nullptr || ws_bytes < (size_t)F * 2048) {
+        return fail(kInvalidArgument,
+                    "opm_outer: workspace below one chunk (cflk_volta_opm_outer_workspace_size)");
+    }
     const CUtensorMapDataType tdt =
         dtype == kBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     CUtensorMap tl, tr, tw, to;
@@ -393,16 +420,16 @@ int opm_outer_fused(void* stream, int dtype, const void* left, const void* right
     const uint64_t dl[3] = {32, 16, (uint64_t)B}, sl[2] = {(uint64_t)B * 32, 32};
     const uint64_t dr[3] = {32, 16, (uint64_t)D}, sr[2] = {(uint64_t)D * 32, 32};
     const uint32_t box8[3] = {8, 16, 16};
-    // wT [F][32 c][32 e] as dims (e, f % 8, c, f / 8): boxes [16][8 c][8 f][8 e]
-    const uint64_t dw[4] = {32, 8, 32, (uint64_t)(F / 8)}, sw[3] = {32 * 32, 32, 8 * 32 * 32};
-    const uint32_t boxw[4] = {8, 8, 8, 16};
+    // the laid-out wT [16][F][64]: boxes [128 f][64] (rows past F read as zero)
+    const uint64_t dw[3] = {64, (uint64_t)F, 16}, sw[2] = {64, (uint64_t)F * 64};
+    const uint32_t boxw[3] = {64, 128, 1};
     // out [B][D][F]: boxes [8 b][16 d][64 f]
     const uint64_t dout[3] = {(uint64_t)F, (uint64_t)D, (uint64_t)B},
                    sout[2] = {(uint64_t)F, (uint64_t)D * F};
     const uint32_t boxo[3] = {64, 16, 8};
     if (!encode_tiled(&tl, tdt, 2, 3, left, dl, sl, box8, CU_TENSOR_MAP_SWIZZLE_NONE) ||
         !encode_tiled(&tr, tdt, 2, 3, right, dr, sr, box8, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !encode_tiled(&tw, tdt, 2, 4, wT, dw, sw, boxw, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !encode_tiled(&tw, tdt, 2, 3, workspace, dw, sw, boxw, CU_TENSOR_MAP_SWIZZLE_128B) ||
         !encode_tiled(&to, tdt, 2, 3, out, dout, sout, boxo, CU_TENSOR_MAP_SWIZZLE_128B)) {
         return fail(kInvalidArgument, "opm_outer: TMA descriptor rejected");
     }
@@ -427,7 +454,17 @@ int opm_outer_fused(void* stream, int dtype, const void* left, const void* right
     const int nsm = dev < kMaxDevices && sms[dev] > 0 ? sms[dev] : 148;
     const long long tiles = ((B + kTB - 1) / kTB) * ((D + kTD - 1) / kTD);
     const dim3 grid((unsigned)std::min<long long>(tiles, nsm));
-    kern<<<grid, kThreads, SMEM, static_cast<cudaStream_t>(stream)>>>(tl, tr, tw, to, args);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int nvec = (int)(16 * F * 8);
+    if (dtype == kBF16) {
+        opm_w_layout_kernel<__nv_bfloat16><<<(nvec + 255) / 256, 256, 0, st>>>(
+            static_cast<const __nv_bfloat16*>(wT), static_cast<__nv_bfloat16*>(workspace),
+            (int)F);
+    } else {
+        opm_w_layout_kernel<__half><<<(nvec + 255) / 256, 256, 0, st>>>(
+            static_cast<const __half*>(wT), static_cast<__half*>(workspace), (int)F);
+    }
+    kern<<<grid, kThreads, SMEM, st>>>(tl, tr, tw, to, args);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         return fail(kInternal, std::string("opm_outer launch: ") + cudaGetErrorString(e));

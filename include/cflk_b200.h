@@ -232,7 +232,8 @@ CFLK_API int cflk_volta_opm_update(void* stream, int dtype, const void* lhs, con
  * multiple of 16, E 32, D a multiple of 4 with D/4 at most 65535, F 16, 32, 64 or 128. At
  * AF2's C = 32 one fused kernel: per 16 b x 16 d tile and chunk of 8 c x 8 e, a tcgen05 MMA of
  * the outer products into tensor memory, rounded by a converter warpgroup into shared memory as
- * the A operand of the MMAs against wT; no workspace (its size is 0). Other C: two persistent
+ * the A operand of the MMAs against wT laid out chunk by chunk in the workspace (F * 2 KB;
+ * the size function gives 256 KB, enough for any F). Other C: two persistent
  * tile GEMMs per chunk of b, the outer products (K = 16, rounded, written as G2 [b][d][c][e]
  * into the workspace; a CUDA-core kernel when C does not divide 128) and G2 [b*D, C*E] times
  * wT; the workspace holds one chunk of G2 (whole multiples of 128/C rows of b, about 64 MB):

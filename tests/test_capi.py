@@ -116,8 +116,8 @@ def test_workspace_size_refuses_overflowing_sizes():
 
 def test_opm_outer_workspace_size():
     """One chunk of G2 [b][d][c][e] (16-bit), whole multiples of 128 / C rows of b, about 64 MB
-    (or the whole problem when smaller); none at C = 32 (the fused kernel); refusals before any
-    CUDA call."""
+    (or the whole problem when smaller); at C = 32 (the fused kernel) wT's 256 KB; refusals
+    before any CUDA call."""
     l = lib()
     n = ctypes.c_size_t(0)
     i64 = ctypes.c_int64
@@ -128,10 +128,10 @@ def test_opm_outer_workspace_size():
     assert l.cflk_volta_opm_outer_workspace_size(i64(3), i64(64), i64(8), i64(32),
                                                  ctypes.byref(n)) == 0
     assert n.value == 3 * 8 * 64 * 32 * 2
-    # C = 32: the fused kernel, no workspace
+    # C = 32: the fused kernel, whose workspace is wT laid out chunk by chunk (F <= 128)
     assert l.cflk_volta_opm_outer_workspace_size(i64(512), i64(32), i64(512), i64(32),
                                                  ctypes.byref(n)) == 0
-    assert n.value == 0
+    assert n.value == 128 * 32 * 32 * 2
     assert l.cflk_volta_opm_outer_workspace_size(i64(3), i64(32), i64(8), i64(16),
                                                  ctypes.byref(n)) == 1
 

@@ -65,16 +65,17 @@ struct GemmArgs {
 template <int KIND>
 struct GemmCfg {
     static constexpr int NB = KIND == kGdpDual ? 2 : 1;   // B matrices
-    // output tile 128 x BN: the contraction takes 256 columns, halving its A re-reads from L2
-    static constexpr int BN = KIND == kContract ? 256 : 128;
+    // output tile 128 x BN: the contraction and VoltaOpmUpdate take 256 columns, halving their A
+    // re-reads from L2 (and the shared-memory bytes an MMA reads per FLOP)
+    static constexpr int BN = KIND == kContract || KIND == kOpmUpdate ? 256 : 128;
     static constexpr int A_BYTES = GBM * GBK * 2;          // [128 rows][64 k] or two [64 k][64 m]
     static constexpr int B_BYTES = GBK * BN * 2;           // [BN rows][64 k] or BN/64 [64 k][64 n]
     static constexpr int STAGE_BYTES = A_BYTES + NB * B_BYTES;
     static constexpr int STAGES = NB == 1 && BN == 128 ? 4 : 3;
     static constexpr int OUT_ELEM = KIND == kContract ? 4 : 2;
-    // output staging in boxes of 128 rows x 128 bytes (64 16-bit or 32 float32 columns):
-    // VoltaOpmUpdate two tiles' boxes (the next tile's residual lands in the other pair while
-    // this tile's outputs are written), VoltaGdp one tile's, the contraction a ring of four
+    // output staging in boxes of 128 rows x 128 bytes (64 16-bit or 32 float32 columns): one
+    // tile's boxes (VoltaOpmUpdate's residual lands in them first), the contraction a ring of
+    // four
     static constexpr int BOX_BYTES = GBM * 128;
     static constexpr int BOX_COLS = 128 / OUT_ELEM;
     static constexpr int BOXES = BN / BOX_COLS;
@@ -295,26 +296,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             m0 = (rem % ntm) * GBM;
             n0 = (rem / ntm) * BN;
         };
-        // 16-bit kinds: warpgroup g's 64 columns are one box, VoltaOpmUpdate's in staging pair
-        // p (box 2p + g), the others' box g
-        const auto box16 = [&](int p) -> uint8_t* {
-            return ostage + ((KIND == kOpmUpdate ? 2 * p : 0) + g) * C::BOX_BYTES;
+        // 16-bit kinds: warpgroup g's BN / 2 columns are BN / 128 boxes (j), boxes g BN/128 + j
+        // of the staging; their first column
+        constexpr int WB = BN / 128;
+        const auto box16 = [&](int j) -> uint8_t* {
+            return ostage + (g * WB + j) * C::BOX_BYTES;
         };
-        // VoltaOpmUpdate: this warpgroup's residual box of a tile by TMA into pair p (columns or
-        // rows past the ends read as zero)
-        int res_issued[2] = {0, 0};  // residual loads per staging pair (the leader's count)
-        const auto load_res = [&](int tile, int p) {
-            int bt, m0, n0;
-            tile_origin(tile, bt, m0, n0);
-            ++res_issued[p];
-            mbar_arrive_expect_tx(&res_full[g][p], C::BOX_BYTES);
-            tma_load_3d(box16(p), &tb1, &res_full[g][p], n0 + 64 * g, m0, bt);
-        };
-        if constexpr (KIND == kOpmUpdate) {
-            if (has_res && leader && blockIdx.x < ntiles) {
-                load_res(blockIdx.x, 0);
+        // VoltaOpmUpdate: this warpgroup's residual boxes of the tile by TMA, issued as soon as
+        // the previous tile's stores have read the staging, so the copy overlaps the tile's MMAs
+        // (columns or rows past the ends read as zero)
+        int res_issued = 0;  // the leader's count
+        const auto load_res = [&](int n0, int m0, int bt) {
+            ++res_issued;
+            mbar_arrive_expect_tx(&res_full[g][0], WB * C::BOX_BYTES);
+#pragma unroll
+            for (int j = 0; j < WB; ++j) {
+                tma_load_3d(box16(j), &tb1, &res_full[g][0], n0 + (BN / 2) * g + 64 * j, m0, bt);
             }
-        }
+        };
         int lt = 0, box = 0;
         for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++lt) {
             const int buf = lt & 1;
@@ -327,8 +326,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 if (leader) {
                     bulk_wait_read<0>();
                     if constexpr (KIND == kOpmUpdate) {
-                        if (has_res && tile + (int)gridDim.x < ntiles) {
-                            load_res(tile + gridDim.x, buf ^ 1);
+                        if (has_res) {
+                            load_res(n0, m0, bt);
                         }
                     }
                 }
@@ -348,8 +347,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 mval = m < a.M ? E::to_f(static_cast<const T*>(a.mask)[m]) : 0.f;
             }
             if constexpr (KIND == kOpmUpdate) {
-                // 1 / (eps + norm[m, d]) for the tile's 128 / F values of d (at most 8)
-                const int d0 = n0 / a.F, nd = 128 / a.F;
+                // 1 / (eps + norm[m, d]) for the warpgroup's (BN / 2) / F values of d (at most 8)
+                const int d0 = (n0 + (BN / 2) * g) / a.F, nd = (BN / 2) / a.F;
                 const float* nrow = a.norm + (long long)m * a.D;
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
@@ -358,8 +357,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                   : 0.f;
                 }
                 if (has_res) {
-                    mbar_wait(&res_full[g][buf], (lt >> 1) & 1, &g_status, kStatusTmaWait,
-                              &abort_flag);
+                    mbar_wait(&res_full[g][0], lt & 1, &g_status, kStatusTmaWait, &abort_flag);
                 }
             }
             mbar_wait(&acc_full[buf], (lt >> 1) & 1, &g_status, kStatusMmaWait, &abort_flag);
@@ -427,13 +425,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 } else {
                     const int nb = n0 + 32 * ch;
                     float v[32];
-                    // staging pieces of these 32 columns: the warpgroup's box, row r, pieces
-                    // 4 hc + q at (c ^ (r % 8))
-                    uint8_t* row = box16(buf) + r * 128;
+                    // staging pieces of these 32 columns: the warpgroup's box hc / 2, row r,
+                    // pieces 4 (hc % 2) + q at (c ^ (r % 8))
+                    uint8_t* row = box16(hc >> 1) + r * 128;
                     if constexpr (KIND == kOpmUpdate) {
                         // (acc + bias[f]) / (eps + norm[m, d]) (+ residual), n = d F + f: the 32
                         // columns span at most two d (F = 16)
-                        const int i0 = (32 * ch) / a.F, i1 = (32 * ch + 16) / a.F;
+                        const int i0 = (32 * hc) / a.F, i1 = (32 * hc + 16) / a.F;
                         float rd0 = 0.f, rd1 = 0.f;
 #pragma unroll
                         for (int i = 0; i < 8; ++i) {  // selects, not a local-memory index
@@ -443,7 +441,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         const float* bias = &bias_sh[nb & (a.F - 1)];
 #pragma unroll
                         for (int q = 0; q < 4; ++q) {
-                            const int c = 4 * hc + q;
+                            const int c = 4 * (hc & 1) + q;
                             uint4 res = make_uint4(0, 0, 0, 0);
                             if (has_res) {
                                 res = *reinterpret_cast<const uint4*>(row + ((c ^ (r & 7)) << 4));
@@ -477,7 +475,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     }
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
-                        const int c = 4 * hc + q;
+                        const int c = 4 * (hc & 1) + q;
                         uint4 w;
                         w.x = E::pack(v[8 * q], v[8 * q + 1]);
                         w.y = E::pack(v[8 * q + 2], v[8 * q + 3]);
@@ -495,14 +493,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 fence_async_smem();
                 named_sync(1 + g, 128);
                 if (leader) {
-                    if (n0 + 64 * g >= a.N) {
-                        // nothing of this warpgroup's columns is inside the output
-                    } else if constexpr (KIND == kOpmOuterG) {
+                    if constexpr (KIND == kOpmOuterG) {
                         // d 2g, 2g + 1 of the tile as one [128/C b][2 d][C c][32 e] box of G2
-                        tma_store_4d(&to, smem_u32(ostage + g * C::BOX_BYTES), 0, 0,
-                                     n0 / 32 + 2 * g, m0 / a.opm_c);
+                        if (n0 + 64 * g < a.N) {
+                            tma_store_4d(&to, smem_u32(ostage + g * C::BOX_BYTES), 0, 0,
+                                         n0 / 32 + 2 * g, m0 / a.opm_c);
+                        }
                     } else {
-                        tma_store_3d(&to, smem_u32(box16(buf)), n0 + 64 * g, m0, bt);
+#pragma unroll
+                        for (int j = 0; j < WB; ++j) {
+                            const int col = n0 + (BN / 2) * g + 64 * j;
+                            if (col < a.N) {
+                                tma_store_3d(&to, smem_u32(box16(j)), col, m0, bt);
+                            }
+                        }
                     }
                     bulk_commit();
                 }
@@ -513,11 +517,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             // every residual load has landed before the CTA exits (after an abort a wait may
             // have given up on one still in flight)
             if constexpr (KIND == kOpmUpdate) {
-                for (int p = 0; p < 2; ++p) {
-                    if (res_issued[p] > 0) {
-                        mbar_wait(&res_full[g][p], (res_issued[p] - 1) & 1, &g_status,
-                                  kStatusTmaWait, nullptr, kDrainLimitNs);
-                    }
+                if (res_issued > 0) {
+                    mbar_wait(&res_full[g][0], (res_issued - 1) & 1, &g_status, kStatusTmaWait,
+                              nullptr, kDrainLimitNs);
                 }
             }
         }

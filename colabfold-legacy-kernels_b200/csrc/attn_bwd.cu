@@ -21,8 +21,10 @@
 //   * S^T = K Q^T and dP^T = V dout^T (M=128 keys, N=64 queries); worker t owns key t = TMEM
 //     lane t, forms P^T and dS^T and writes them back over its own S^T and dP^T columns as
 //     16-bit pairs, the A operands of dV += P^T dout and dK += dS^T q (A read from TMEM);
-//   * dS also goes MN-major into swizzled shared memory for dQ = dS k (M=64), whose fp32 tile
-//     is added into the workspace accumulator with 16-byte vector atomics;
+//   * dS also goes MN-major into swizzled shared memory for dQ = dS k (M=64); a CTA runs the
+//     key tiles of each (n, h) it owns in order, so the first key tile stores a query step's
+//     fp32 dQ tile into the workspace accumulator and the later ones add theirs with 16-byte
+//     vector atomics (no zero fill of the accumulator); a conversion pass rounds it to dQ;
 //   * the bias is transposed once per call into the workspace in its own 16-bit type
 //     [H][Sk][Sq'] (exact), so a key's bias values arrive by TMA as one contiguous 128-byte row;
 //   * dBias: each warpgroup stages its half-step's fp32 dS rows [32 queries][128 keys] in
@@ -31,7 +33,8 @@
 //     sequence, so concurrent items reduce into different rows. Where the dBias rows are not
 //     16-byte multiples (Sk % 4 != 0) the workers add dS with coalesced fp32 reductions
 //     instead (a warp covers 32 consecutive keys of a row).
-// Around it: the row statistic (delta), the bias transpose, the zero fills, the dQ conversion.
+// Around it: the row statistic (delta), the bias transpose, the dBias zero fill, the dQ
+// conversion.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -59,7 +62,7 @@ struct BwdParams {
     const uint8_t* kmask;
     const float* nlse;   // -lse, [N,H,Sq]
     const float* ndelta; // -delta
-    float* dq_acc;  // [N,H,Sq,D] fp32, zeroed
+    float* dq_acc;  // [N,H,Sq,D] fp32: stored by the first key tile, added to by the later ones
     void* dk;
     void* dv;
     float* dbias;   // [H,Sq,Sk] fp32, zeroed
@@ -154,18 +157,32 @@ __device__ __forceinline__ void red_add_f32(float* p, float v) {
 }
 
 // Where global step gi of a CTA lies: its work item (key tile, head, sequence) and query step.
-// A CTA takes items blockIdx.x, blockIdx.x + gridDim.x, ... (key tiles fastest, then heads,
-// then sequences) and runs every item's nqt query steps in turn. The query steps of an item
-// start at one that depends on its sequence, so the CTAs of different sequences running at once
-// reduce into different dBias rows.
+// Items are numbered key tiles fastest, then heads, then sequences; CTA b owns the (n, h) pairs
+// [b P / G, (b + 1) P / G) of the P = N H pairs (G CTAs), i.e. a contiguous run of items whose
+// key tiles of one (n, h) follow one another, and runs every item's nqs query steps in turn.
+// nqs is nqt (the steps that hold queries) rounded up to a multiple of the step sets, so that
+// step i of every item falls to the same set (whose threads then handle the same dQ elements
+// at every key tile); a step past nqt has no queries (all its rows lie past Sq: zero tiles, no
+// outputs). The query steps of an item start at one that depends on its
+// sequence, so the CTAs of different sequences running at once reduce into different dBias
+// rows.
 struct StepPos {
     int k0, h, n, q0;
     long long rowbase;  // (n * H + h) * Sq
 };
 
-// The position of local step i of the CTA's item j (divisions: once per item)
-__device__ __forceinline__ StepPos item_pos(const BwdParams& p, int nkt, int j) {
-    const int u = (int)blockIdx.x + j * (int)gridDim.x;
+// The first item of this CTA and how many it owns
+__device__ __forceinline__ void cta_items(const BwdParams& p, int nkt, int& item0, int& count) {
+    const long long pairs = (long long)p.N * p.H;
+    const long long b = blockIdx.x, g = gridDim.x;
+    const long long p0 = b * pairs / g, p1 = (b + 1) * pairs / g;
+    item0 = (int)(p0 * nkt);
+    count = (int)((p1 - p0) * nkt);
+}
+
+// The position of the CTA's item j (divisions: once per item)
+__device__ __forceinline__ StepPos item_pos(const BwdParams& p, int nkt, int item0, int j) {
+    const int u = item0 + j;
     const int rest = u / nkt;
     StepPos s;
     s.k0 = (u - rest * nkt) * kBK;
@@ -177,31 +194,39 @@ __device__ __forceinline__ StepPos item_pos(const BwdParams& p, int nkt, int j) 
 }
 
 __device__ __forceinline__ int rotated_q0(int n, int nqt, int i) {
+    if (i >= nqt) {
+        return nqt * kBQ;  // a padding step: every row past Sq
+    }
     const int r = n % nqt;
     return (i + r < nqt ? i + r : i + r - nqt) * kBQ;
 }
 
-// A walk over global steps gi = j * nqt + i in strides of `by` (by <= nqt is not required)
+// The CTA's schedule: key tiles, query steps holding queries, steps per item, first item
+struct Sched {
+    int nkt, nqt, nqs, item0;
+};
+
+// A walk over global steps gi = j * nqs + i in strides of `by` (by <= nqs is not required)
 struct StepCursor {
     int gi, j, i;
     StepPos pos;
-    __device__ __forceinline__ void start(const BwdParams& p, int nkt, int nqt, int g) {
+    __device__ __forceinline__ void start(const BwdParams& p, const Sched& sc, int g) {
         gi = g;
-        j = g / nqt;
-        i = g - j * nqt;
-        pos = item_pos(p, nkt, j);
-        pos.q0 = rotated_q0(pos.n, nqt, i);
+        j = g / sc.nqs;
+        i = g - j * sc.nqs;
+        pos = item_pos(p, sc.nkt, sc.item0, j);
+        pos.q0 = rotated_q0(pos.n, sc.nqt, i);
     }
-    __device__ __forceinline__ void advance(const BwdParams& p, int nkt, int nqt, int by) {
+    __device__ __forceinline__ void advance(const BwdParams& p, const Sched& sc, int by) {
         gi += by;
         i += by;
-        if (i >= nqt) {
-            const int dj = i / nqt;
+        if (i >= sc.nqs) {
+            const int dj = i / sc.nqs;
             j += dj;
-            i -= dj * nqt;
-            pos = item_pos(p, nkt, j);
+            i -= dj * sc.nqs;
+            pos = item_pos(p, sc.nkt, sc.item0, j);
         }
-        pos.q0 = rotated_q0(pos.n, nqt, i);
+        pos.q0 = rotated_q0(pos.n, sc.nqt, i);
     }
 };
 
@@ -228,10 +253,14 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
     const int DN = (D + 15) & ~15;
     const int nkt = (p.Sk + kBK - 1) / kBK;
     const int nqt = (p.Sq + kBQ - 1) / kBQ;
-    const int nitems = nkt * p.H * p.N;  // the host keeps nitems * nqt below 2^31
-    const int J = nitems > (int)blockIdx.x ? (nitems - 1 - (int)blockIdx.x) / (int)gridDim.x + 1
-                                           : 0;
-    const int total = J * nqt;  // this CTA's query steps
+    const int nqs = (nqt + NP - 1) / NP * NP;  // the host keeps items * nqs below 2^31
+    Sched sc;
+    int J;  // this CTA's items
+    cta_items(p, nkt, sc.item0, J);
+    sc.nkt = nkt;
+    sc.nqt = nqt;
+    sc.nqs = nqs;
+    const int total = J * nqs;  // this CTA's query steps
 
     if (warp == G::MMA_A) {
         if (lane == 0) {
@@ -270,7 +299,7 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
         // statistics and arrives on the stage's barrier (released with its own stores)
         {
             for (int j = 0; j < J; ++j) {
-                const StepPos it = item_pos(p, nkt, j);
+                const StepPos it = item_pos(p, nkt, sc.item0, j);
                 const int kb = j % KVB;
                 if (lane == 0) {
                     if (j >= KVB) {
@@ -286,8 +315,8 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
                                     it.h, it.k0, it.n);
                     }
                 }
-                for (int i = 0; i < nqt; ++i) {
-                    const int gi = j * nqt + i;
+                for (int i = 0; i < nqs; ++i) {
+                    const int gi = j * nqs + i;
                     StepPos sp = it;
                     sp.q0 = rotated_q0(it.n, nqt, i);
                     const int s = gi % NS;
@@ -364,7 +393,7 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
                 mma_commit(&q_empty[s]);
             };
             for (int j = 0, gi = 0; j < J; ++j) {
-                for (int i = 0; i < nqt; ++i, ++gi) {
+                for (int i = 0; i < nqs; ++i, ++gi) {
                     issue_s(gi, j, i);
                 }
             }
@@ -401,7 +430,7 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
                         mma_ss(tmem + G::T_DQ + w * G::DN, ad, bd, idesc_dq, ks > 0 ? 1u : 0u);
                     }
                     mma_commit(&dq_done[w]);
-                    if (i == nqt - 1) {
+                    if (i == nqs - 1) {
                         mma_commit(&kv_empty[kb]);
                     }
                 }
@@ -420,10 +449,10 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
                 }
                 mma_commit(&ts_done[w]);
                 mma_commit(&q_empty[s]);
-                if (i == nqt - 1) {
+                if (i == nqs - 1) {
                     mma_commit(&acc_full[db]);
                 }
-                if (++i == nqt) {
+                if (++i == nqs) {
                     i = 0;
                     ++j;
                 }
@@ -445,9 +474,12 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
         const uint32_t t_st = tmem + 128 * set + lane_base + 32 * hf, t_dp = t_st + 64;
 
         // dQ of a step: lanes 32w + r (r < 16) hold query row 16w + r (M=64 layout); the two
-        // warpgroups of the set take alternate 16-column chunks
+        // warpgroups of the set take alternate 16-column chunks. The same thread handles these
+        // dQ elements at this step of every key tile of the (n, h), in key-tile order: the first
+        // stores its tile, the later ones add to it (after that store: program order).
         const auto flush_dq = [&](const StepPos& sp) {
             const int q = sp.q0 + 16 * (warp & 3) + lane;
+            const bool first = sp.k0 == 0;
             for (int c = 16 * hf; c < DN; c += 32) {
                 uint32_t r[16];
                 tmem_ld16(t_dq + lane_base + c, r);
@@ -457,11 +489,15 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
 #pragma unroll
                     for (int g = 0; g < 4; ++g) {
                         if (c + 4 * g < D) {
-                            atomicAdd(reinterpret_cast<float4*>(dst + 4 * g),
-                                      make_float4(__uint_as_float(r[4 * g]) * p.scale,
-                                                  __uint_as_float(r[4 * g + 1]) * p.scale,
-                                                  __uint_as_float(r[4 * g + 2]) * p.scale,
-                                                  __uint_as_float(r[4 * g + 3]) * p.scale));
+                            const float4 v = make_float4(__uint_as_float(r[4 * g]) * p.scale,
+                                                         __uint_as_float(r[4 * g + 1]) * p.scale,
+                                                         __uint_as_float(r[4 * g + 2]) * p.scale,
+                                                         __uint_as_float(r[4 * g + 3]) * p.scale);
+                            if (first) {
+                                *reinterpret_cast<float4*>(dst + 4 * g) = v;
+                            } else {
+                                atomicAdd(reinterpret_cast<float4*>(dst + 4 * g), v);
+                            }
                         }
                     }
                 }
@@ -474,7 +510,7 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
             const int db = e % NB;
             mbar_wait(&acc_full[db], (e / NB) & 1, &g_status, kStatusMmaWait, &abort_flag);
             tc_fence_after();
-            const StepPos it = item_pos(p, nkt, e);
+            const StepPos it = item_pos(p, nkt, sc.item0, e);
             const int key = it.k0 + t;
             const long long krow = ((long long)it.n * p.H + it.h) * p.Sk + key;
             const int which = wg & 1;
@@ -611,9 +647,9 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
         // cur: this step; nxt: this set's next step; prev: the set's previous step (its dQ is
         // flushed at the start of this one)
         StepCursor cur, nxt;
-        cur.start(p, nkt, nqt, set);
+        cur.start(p, sc, set);
         nxt = cur;
-        nxt.advance(p, nkt, nqt, NP);
+        nxt.advance(p, sc, NP);
         StepPos prev = cur.pos;
         int k = 0, stored = 0;  // this set's steps so far; items whose dK/dV this group stored
         for (; cur.gi < total; ++k) {
@@ -671,7 +707,7 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
             }
             prev = sp;
             cur = nxt;
-            nxt.advance(p, nkt, nqt, NP);
+            nxt.advance(p, sc, NP);
         }
         if constexpr (DBIAS == kDbiasTma) {
             if (lane == 0) {
@@ -819,7 +855,6 @@ __global__ void bias_transpose_kernel(const T* __restrict__ bias, T* __restrict_
     }
 }
 
-// dq = dq_acc rounded to 16 bits, 8 elements a thread
 template <typename T>
 __global__ void dq_convert_kernel(const float* __restrict__ acc, T* __restrict__ dq,
                                   long long n8) {
@@ -849,7 +884,7 @@ bool aligned16(const void* p) {
     return (reinterpret_cast<uintptr_t>(p) & 15) == 0;
 }
 
-// Workspace: dQ accumulator | -delta | -lse | bias^T (16-bit, queries padded to a multiple of
+// Workspace: dQ partial sums | -delta | -lse | bias^T (16-bit, queries padded to a multiple of
 // 8) | (gated backward only) dO = dy * sigmoid(gate + gate_bias), 16-bit [N,H,Sq,D]; each part
 // 256-byte aligned. `ok` is false when a size product overflows 64 bits.
 struct Workspace {
@@ -900,8 +935,9 @@ cudaError_t launch_main(cudaStream_t stream, const CUtensorMap* maps, const BwdP
         cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
     }
     const int nsm = dev < kMaxDevices && sms[dev] > 0 ? sms[dev] : 148;
-    const long long items = (long long)((p.Sk + kBK - 1) / kBK) * p.H * p.N;  // < 2^31 / nqt
-    const dim3 grid((unsigned)std::min<long long>(items, nsm));
+    // every CTA owns at least one (n, h) pair and all of its key tiles
+    const long long pairs = (long long)p.N * p.H;
+    const dim3 grid((unsigned)std::min<long long>(pairs, nsm));
     kern<<<grid, BGeom<DP>::THREADS, smem, stream>>>(maps[0], maps[1], maps[2], maps[3], maps[4],
                                                      maps[5], p);
     return cudaGetLastError();
@@ -931,10 +967,6 @@ cudaError_t run_backward(cudaStream_t stream, const CUtensorMap* maps, const Bwd
     const long long rows = (long long)p.N * p.H * p.Sq;
     cudaError_t e;
     if ((e = cudaMemsetAsync(p.dbias, 0, sizeof(float) * (size_t)p.H * p.Sq * p.Sk, stream)) !=
-        cudaSuccess) {
-        return e;
-    }
-    if ((e = cudaMemsetAsync(p.dq_acc, 0, sizeof(float) * (size_t)rows * p.D, stream)) !=
         cudaSuccess) {
         return e;
     }
@@ -1029,7 +1061,7 @@ int backward(void* stream_, int dtype, const void* q, const void* k, const void*
             Sk >= (int64_t(1) << 31) ||
             __builtin_mul_overflow((Sk + kBK - 1) / kBK, H, &pairs) ||
             __builtin_mul_overflow(pairs, N, &pairs) ||
-            __builtin_mul_overflow(pairs, (Sq + kBQ - 1) / kBQ, &pairs) ||
+            __builtin_mul_overflow(pairs, ((Sq + kBQ - 1) / kBQ + 1) & ~int64_t(1), &pairs) ||
             pairs >= (int64_t(1) << 31)) {
             return fail(kInvalidArgument,
                         "volta_mma_bwd: more than 2^31 (key tile, query step) pairs");

@@ -27,25 +27,45 @@ using namespace fused;
 // ---------------------------------------------------------------------------------------------
 // The accumulators live in a ring of Op::kSlots blocks of Op::kSlotCols tensor-memory columns: the MMA
 // warp fills block j+1.. while the workers drain block j, so neither side waits for a whole
-// tile. With Op::kPingPong the two worker warpgroups take the tiles in turn (tile c to
-// warpgroup c % 2, which uses x stage c % 2), each doing a tile's whole prologue and epilogue, so
-// one tile's LayerNorm overlaps the other's epilogue; otherwise both split every tile.
+// tile. With Op::kPingPong the Op::kWorkerGroups worker warpgroups (two or three) take the
+// tiles in turn (tile c to warpgroup c % kWorkerGroups, in x stage c % kStages), each doing a
+// tile's whole prologue and epilogue, so one tile's LayerNorm overlaps another's epilogue;
+// otherwise two warpgroups split every tile.
 // Op supplies: T, Args (M, w_bytes, param_floats, eps), keep(), kOther, X_BYTES,
 // RED_FLOATS, STORE_BYTES, nblocks(), load_params, load_weights, load_x, issue_block, prologue,
-// epilogue_block, prefetch_block, padding, Regs, bind, finish, kPingPong, kSlots, kSlotCols.
+// epilogue_block, prefetch_block, padding, Regs, bind, finish, kPingPong, kWorkerGroups,
+// kSlots, kSlotCols.
 // STORE_BYTES of 1024-byte-aligned shared memory after the others are the op's output staging
 // (TMA stores through the map `to`), handed to Op::bind with the map.
 
+// Worker warpgroups and threads of an op's launch; the producer warp follows the workers. With
+// three worker warpgroups (416 threads) a thread has at most 128 registers: an SM sub-partition
+// holds four of the thirteen warps.
 template <class Op>
-__global__ void __launch_bounds__(kThreads, 1)
+struct Crew {
+    static constexpr int kGroups = Op::kWorkerGroups;
+    static constexpr int kWorkerThreads = 128 * kGroups;
+    static constexpr int kProducer = 4 * kGroups;
+    static constexpr int kThreads = kWorkerThreads + 32;
+    static_assert(kGroups == 2 || (kGroups == 3 && Op::kPingPong), "worker warpgroups");
+    // ping-pong: every stage serves one warpgroup only, so no waiter on a stage's barriers can
+    // run a phase ahead (a warpgroup meets its stages in its own order)
+    static_assert(!Op::kPingPong || Op::kStages % kGroups == 0, "stages per warpgroup");
+};
+
+template <class Op>
+__global__ void __launch_bounds__(Crew<Op>::kThreads, 1)
     row_tile_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap tw0,
                     const __grid_constant__ CUtensorMap tw1,
                     const __grid_constant__ CUtensorMap to,
                     const __grid_constant__ CUtensorMap to1, const typename Op::Args a) {
     constexpr int kSlots = Op::kSlots, kSlotCols = Op::kSlotCols;
-    // x stages: two (tile c in stage c % 2), or one where a stage is too large for two
+    // x stages: tile c in stage c % kStages; three where shared memory leaves room (the load of
+    // tile c + 3 starts as soon as tile c's MMAs are done, a whole tile before a worker needs
+    // it), two, or one where a stage is too large for two
     constexpr int kStages = Op::kStages;
-    static_assert(kStages == 2 || (kStages == 1 && !Op::kPingPong), "stages");
+    static_assert(kStages == 2 || kStages == 3 || (kStages == 1 && !Op::kPingPong), "stages");
+    constexpr int kStageBars = kStages > 2 ? kStages : 2;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -58,8 +78,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // accumulator slot barriers per warpgroup that consumes the slot's block (both ping-pong
     // warpgroups pass blocks through the same slots; one barrier each keeps every barrier's
     // phases in one consumer's order, so no waiter can be two phases ahead)
-    constexpr int kTeams = Op::kPingPong ? 2 : 1;
-    __shared__ uint64_t x_full[2], x_empty[2], a_ready[2], acc_full[kTeams][kSlots],
+    constexpr int kTeams = Op::kPingPong ? Crew<Op>::kGroups : 1;
+    constexpr int kProducerWarp = Crew<Op>::kProducer;
+    __shared__ uint64_t x_full[kStageBars], x_empty[kStageBars], a_ready[kStageBars],
+        acc_full[kTeams][kSlots],
         acc_empty[kTeams][kSlots], w_full;
     __shared__ uint32_t tmem_sh;
     __shared__ int abort_flag;
@@ -70,8 +92,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == kProducerWarp) {
         if (lane == 0) {
             // ping-pong ops: one worker warpgroup per tile (the two take the tiles in turn)
-            constexpr int kTeam = Op::kPingPong ? kWorkers / 2 : kWorkers;
-            for (int i = 0; i < 2; ++i) {
+            constexpr int kTeam = Op::kPingPong ? 128 : Crew<Op>::kWorkerThreads;
+            for (int i = 0; i < kStageBars; ++i) {
                 mbar_init(&x_full[i], 1);
                 mbar_init(&x_empty[i], 1);
                 mbar_init(&a_ready[i], kTeam);
@@ -89,7 +111,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         tmem_alloc(&tmem_sh, kSlots * kSlotCols);
         tmem_relinquish();
-    } else {
+    } else if (warp < kProducerWarp) {
         Op::load_params(a, sp, ws, threadIdx.x);
         fence_async_smem();  // weight rows the workers wrote, read by the MMA
     }
@@ -139,13 +161,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 mbar_wait(&a_ready[s], sph, &g_status, kStatusSyncWait, &abort_flag);
                 tc_fence_after();
-                const int team = kTeams == 2 ? (c & 1) : 0;
+                const int team = c % kTeams;
                 for (int j = 0; j < nb; ++j, ++q) {
                     const int slot = q % kSlots;
                     if (q >= kSlots) {
                         // the slot's previous block: consumed by its warpgroup (the n-th of that
                         // warpgroup's blocks in this slot completes the barrier's n-th phase)
-                        const int pt = kTeams == 2 ? (((q - kSlots) / nb) & 1) : 0;
+                        const int pt = ((q - kSlots) / nb) % kTeams;
                         const int bit = pt * kSlots + slot;
                         mbar_wait(&acc_empty[pt][slot], (empty_par >> bit) & 1, &g_status,
                                   kStatusSyncWait, &abort_flag);
@@ -171,7 +193,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             ++c;
         }
-    } else {
+    } else if (warp < kProducerWarp) {
         const int g = warp >> 2, t = ((warp & 3) << 5) | lane;
         const uint32_t lane_base = tmem_lane_base(warp);
         typename Op::Regs regs{};
@@ -197,7 +219,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             const int s = c % kStages, sph = (c / kStages) & 1;
             if constexpr (Op::kPingPong) {
-                if ((c & 1) != g) {  // the other warpgroup's tile
+                if (c % kTeams != g) {  // another warpgroup's tile
                     q += nb;
                     ++c;
                     continue;
@@ -208,7 +230,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             Op::prologue(a, stage, sp, red, t, g, m0, regs);
             fence_async_smem();
             mbar_arrive(&a_ready[s]);
-            const int team = kTeams == 2 ? g : 0;
+            const int team = kTeams > 1 ? g : 0;
             for (int j = 0; j < nb; ++j, ++q) {
                 const int slot = q % kSlots;
                 // global inputs of the block's epilogue start loading before the MMA wait
@@ -294,12 +316,16 @@ struct LnGdpOp {
     using T = T_;
     using E = Elem<T>;
     static constexpr int P = 2 * CI;
-    static constexpr int kStages = 2;
+    // three x stages where the weights leave room (CI = 64: 64 KB of weights)
+    static constexpr int kStages = CI <= 64 ? 3 : 2;
     static constexpr int X_BYTES = K * BM * 2;
     static constexpr float kOther = 0.f;
-    // the tile's row mask max(mask, 0): per warpgroup two buffers (its tile parity)
-    static constexpr int RED_FLOATS = 4 * BM;
     static constexpr bool kPingPong = true;
+    // with three stages, three warpgroups take the tiles in turn: twelve worker warps keep more
+    // of the LayerNorm's and the epilogue's latency covered than eight
+    static constexpr int kWorkerGroups = kStages;
+    // the tile's row mask max(mask, 0): per warpgroup two buffers (its tile parity)
+    static constexpr int RED_FLOATS = 2 * kWorkerGroups * BM;
     // the outputs are channel major, so the product is computed transposed (lanes = channels):
     // a block is 128 channels, the projection in the slot's columns [0, 128) and the gate in
     // [128, 256), one column per row of the tile
@@ -307,7 +333,7 @@ struct LnGdpOp {
     // output staging when M % 8 == 0 (TMA row strides): per worker warp one 2 KB box buffer
     // for CI = 128 (its weights fill shared memory), two for CI = 64
     using Stager = RowChunkStager<CI <= 64 ? 2 : 1>;
-    static constexpr int STORE_BYTES = (kWorkers / 32) * Stager::BYTES;
+    static constexpr int STORE_BYTES = 4 * kWorkerGroups * Stager::BYTES;
     struct Args {
         const T *x, *wpT, *bp, *wgT, *bg, *mask;
         const float *scale, *offset;
@@ -366,7 +392,13 @@ struct LnGdpOp {
         mv[t] = m0 + t < a.M ? fmaxf(regs.row_mask, 0.f) : 0.f;
         regs.maskv = mv;
         regs.parity ^= 1;
-        ln_row_regs<T, K>(stage, t, sp, sp + K, a.eps);
+        if constexpr (kWorkerGroups == 3) {
+            // three passes over the row in shared memory: the row held in registers would not
+            // fit the 128 registers a thread of three worker warpgroups has
+            ln_row_full<T, K>(stage, t, sp, sp + K, a.eps);
+        } else {
+            ln_row_regs<T, K>(stage, t, sp, sp + K, a.eps);
+        }
         named_sync(2 + g, 128);
     }
     static __device__ void prefetch_block(const Args&, int, int, int, int, Regs&) {}
@@ -459,7 +491,7 @@ struct LnGdpOp {
     }
     static __device__ void padding(const Args& a, int m0, int t, int g) {
         const int m = m0 + t;
-        if (m >= a.M) {
+        if (m >= a.M || g > 1) {  // warpgroup 0 zeroes left, 1 right
             return;
         }
         T* out = g == 0 ? a.left : a.right;
@@ -481,12 +513,15 @@ struct GdpOp {
     using E = Elem<T>;
     static constexpr int kSlots = 2, kSlotCols = 256;
     static constexpr bool kPingPong = true;
-    static constexpr int kStages = 2;
+    // three x stages (at most 64 KB of weights: K, N <= 128) and three warpgroups taking the
+    // tiles in turn
+    static constexpr int kStages = 3;
+    static constexpr int kWorkerGroups = 3;
     static constexpr int X_BYTES = K * BM * 2;
     static constexpr float kOther = 0.f;
     static constexpr int RED_FLOATS = 4;  // unused
     using Stager = RowChunkStager<2>;
-    static constexpr int STORE_BYTES = (kWorkers / 32) * Stager::BYTES;
+    static constexpr int STORE_BYTES = 4 * kWorkerGroups * Stager::BYTES;
     struct Args {
         const T *x, *wp, *bp, *wg, *bg, *mask;
         T* out;
@@ -583,22 +618,25 @@ struct GdpOp {
 // ---------------------------------------------------------------------------------------------
 // VoltaLnProj (LN = true): p [M, n] = LN(x) w, bias [heads, M] = (LN(x) wb)^T
 // VoltaOutProj (LN = false): out [M, n] = o w + b (+ residual)
-// One launch covers output columns [0, n) of a pass, n <= 512, p's row stride ldp.
+// One launch covers output columns [0, n) of a pass, n <= 512, p's row stride ldp. G worker
+// warpgroups take the tiles in turn, with as many x stages (two: three measured slower for the
+// output projection, whose residual registers then spill).
 // ---------------------------------------------------------------------------------------------
-template <typename T_, int K, bool LN>
+template <typename T_, int K, bool LN, int G = 2>
 struct ProjOp {
     using T = T_;
     using E = Elem<T>;
     static constexpr int kSlots = 4, kSlotCols = 128;
     static constexpr bool kPingPong = true;
-    static constexpr int kStages = 2;
+    static constexpr int kWorkerGroups = G;
+    static constexpr int kStages = G;
     static constexpr int X_BYTES = K * BM * 2;
     static constexpr float kOther = -1.f;
     static constexpr int RED_FLOATS = 4;  // unused: a row's LayerNorm is one thread's
     // output staging: per worker warp one 2 KB box buffer for ln_projection (its weights fill
     // shared memory), two for output_projection
     using Stager = RowChunkStager<LN ? 1 : 2>;
-    static constexpr int STORE_BYTES = (kWorkers / 32) * Stager::BYTES;
+    static constexpr int STORE_BYTES = 4 * G * Stager::BYTES;
     struct Args {
         const T *x, *wT, *b, *residual, *wbT, *keep;
         const float *scale, *offset;
@@ -784,9 +822,11 @@ struct ProjOp {
         }
         // with a residual the output aliases it, which it keeps
         if (a.n > 0 && a.residual == nullptr) {
-            const int half = a.n / 2;
+            // warpgroup g zeroes its share of the row, in 8-column pieces
+            const int share = (a.n + 8 * G - 1) / (8 * G) * 8;
+            const int c1 = min(a.n, (g + 1) * share);
             T* orow = a.out + (long long)m * a.ldp;
-            for (int c = g * half; c < (g + 1) * half; c += 8) {
+            for (int c = g * share; c < c1; c += 8) {
                 *reinterpret_cast<uint4*>(orow + c) = make_uint4(0, 0, 0, 0);
             }
         }
@@ -808,6 +848,7 @@ struct TrimulOp {
     using T = T_;
     using E = Elem<T>;
     static constexpr bool kPingPong = false;
+    static constexpr int kWorkerGroups = 2;
     static constexpr int kSlots = 4, kSlotCols = 128;
     // A stage starts with the tile's float32 x_cm columns ([C][128], by TMA with x when
     // M % 4 == 0), over whose first half the workers write Y; then x's atoms. At C = 128 such a
@@ -1727,7 +1768,7 @@ cudaError_t launch_op(cudaStream_t stream, const CUtensorMap& tx, const CUtensor
     }
     const int ntiles = (a.M + BM - 1) / BM;
     const int grid = std::min(ntiles, sm_count());
-    kern<<<grid, kThreads, smem, stream>>>(tx, tw0, tw1, to, to1, a);
+    kern<<<grid, Crew<Op>::kThreads, smem, stream>>>(tx, tw0, tw1, to, to1, a);
     return cudaGetLastError();
 }
 
@@ -1873,6 +1914,7 @@ cudaError_t proj_typed(cudaStream_t stream, int dtype, const void* x, const floa
     a.eps = eps;
     return launch_op<Op>(stream, tx, tw0, tw0, to, to, a);
 }
+
 
 
 template <typename T, int C, int CA, int O, bool ADD>

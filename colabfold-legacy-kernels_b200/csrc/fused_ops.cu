@@ -847,13 +847,16 @@ template <typename T_, int C, int CA, int O, bool ADD>
 struct TrimulOp {
     using T = T_;
     using E = Elem<T>;
-    static constexpr bool kPingPong = false;
     static constexpr int kWorkerGroups = 2;
     static constexpr int kSlots = 4, kSlotCols = 128;
     // A stage starts with the tile's float32 x_cm columns ([C][128], by TMA with x when
     // M % 4 == 0), over whose first half the workers write Y; then x's atoms. At C = 128 such a
     // stage (96 KB) leaves room for one only.
     static constexpr int kStages = C <= 64 ? 2 : 1;
+    // with two stages the warpgroups take the tiles in turn, a thread a whole row (both
+    // LayerNorms without a barrier between warpgroups, one tile's LayerNorms overlapping the
+    // other's epilogue); with one, both split every tile
+    static constexpr bool kPingPong = kStages == 2;
     static constexpr int X_BYTES = (C * 4 + CA * 2) * BM;
     static constexpr int XOFF = C * BM * 4;  // x's atoms after the x_cm / Y region
     static constexpr float kOther = -1.f;
@@ -872,7 +875,9 @@ struct TrimulOp {
         float eps;
     };
     struct Regs {
-        uint4 res[4];  // x of worker half g's 32 channels of the next block (add_input)
+        // x of the next block's channels (add_input): the block's 64 (ping-pong) or worker
+        // half g's 32
+        uint4 res[kPingPong ? 8 : 4];
         Stager st;
     };
     static __device__ void bind(Regs& r, uint8_t* stb, int warp) {
@@ -925,7 +930,68 @@ struct TrimulOp {
         mma_rows(acc + 64, xa + XOFF, wa + O * C * 2, O, CA, 64 * j, 64, E::kBf16, false);
     }
     static __device__ void prologue(const Args& a, uint8_t* stage, const float* sp, float* red,
-                                    int t, int g, int m0, Regs&) {
+                                    int t, int g, int m0, Regs& regs) {
+        if constexpr (kPingPong) {
+            prologue_row(a, stage, sp, t, g, m0);
+        } else {
+            prologue_split(a, stage, sp, red, t, g, m0);
+        }
+    }
+    // ping-pong: thread t of warpgroup g normalises column m = m0 + t of x_cm over all C
+    // channels (two-pass float32 from registers) into row t of Y, then row t of x in place
+    static __device__ void prologue_row(const Args& a, uint8_t* stage, const float* sp, int t,
+                                        int g, int m0) {
+        const int m = m0 + t;
+        const bool in = m < a.M;
+        float v[C];
+        if (a.xcm_tma) {
+            const float* xc = reinterpret_cast<const float*>(stage) + t;
+#pragma unroll
+            for (int i = 0; i < C; ++i) {
+                v[i] = xc[i * BM];
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < C; ++i) {
+                v[i] = in ? a.x_cm[(long long)i * a.M + m] : 0.f;
+            }
+        }
+        float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+        for (int i = 0; i < C; i += 2) {
+            s0 += v[i];
+            s1 += v[i + 1];
+        }
+        const float mean = (s0 + s1) * (1.f / C);
+        float q0 = 0.f, q1 = 0.f;
+#pragma unroll
+        for (int i = 0; i < C; i += 2) {
+            v[i] -= mean;
+            v[i + 1] -= mean;
+            q0 += v[i] * v[i];
+            q1 += v[i + 1] * v[i + 1];
+        }
+        const float rstd = rsqrtf((q0 + q1) * (1.f / C) + a.eps);
+        const float* ls = sp + 2 * CA;
+        const float* lo = sp + 2 * CA + C;
+        // Y overwrites the x_cm columns of other rows: all of the warpgroup's reads come first
+        named_sync(2 + g, 128);
+#pragma unroll
+        for (int ch = 0; ch < C / 8; ++ch) {
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int c = 8 * ch + 2 * e;
+                w[e] = E::pack(v[c] * rstd * ls[c] + lo[c], v[c + 1] * rstd * ls[c + 1] + lo[c + 1]);
+            }
+            *reinterpret_cast<uint4*>(stage + sw128(t, 8 * ch)) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        ln_row_full<T, CA>(stage + XOFF, t, sp, sp + CA, a.eps);
+    }
+    // split: worker half g takes channels [g C/2, (g+1) C/2) of both LayerNorms, the statistics
+    // exchanged through red
+    static __device__ void prologue_split(const Args& a, uint8_t* stage, const float* sp,
+                                          float* red, int t, int g, int m0) {
         // LN over the C channels of column m of the channel-major float32 x_cm
         constexpr int CH = C / 2;
         const int m = m0 + t;
@@ -986,36 +1052,49 @@ struct TrimulOp {
                                           Regs& regs) {
         const int m = m0 + t;
         if (j == 0 && !a.xcm_tma) {
-            const int mn = m + (int)gridDim.x * BM;
+            // this warpgroup's next tile (ping-pong: two tiles on, if none is skipped)
+            const int mn = m + (kPingPong ? 2 : 1) * (int)gridDim.x * BM;
             if (mn < a.M) {
-                const float* xc = a.x_cm + (long long)(g * (C / 2)) * a.M + mn;
+                constexpr int NC = kPingPong ? C : C / 2;
+                const float* xc = a.x_cm + (long long)(kPingPong ? 0 : g * NC) * a.M + mn;
 #pragma unroll 8
-                for (int i = 0; i < C / 2; ++i) {
+                for (int i = 0; i < NC; ++i) {
                     asm volatile("prefetch.global.L2 [%0];" ::"l"(xc + (long long)i * a.M));
                 }
             }
         }
         if constexpr (ADD) {
             if (m < a.M) {
-                const uint4* xr =
-                    reinterpret_cast<const uint4*>(a.x + (long long)m * CA + 64 * j + 32 * g);
+                constexpr int NR = kPingPong ? 8 : 4;
+                const uint4* xr = reinterpret_cast<const uint4*>(
+                    a.x + (long long)m * CA + 64 * j + (kPingPong ? 0 : 32 * g));
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
+                for (int i = 0; i < NR; ++i) {
                     regs.res[i] = xr[i];
                 }
             }
         }
     }
     // worker half g: channels 64j + 32g + [0, 32)
+    // (ping-pong: all 64 channels of block j, in two halves of 32)
     static __device__ void epilogue_block(const Args& a, uint32_t acc, const float* sp, int t,
                                           int g, int m0, int j, Regs& regs,
                                           const CUtensorMap* to, const CUtensorMap* to1) {
-        epilogue_staged(a, acc, sp, t, g, m0, j, regs, to);
+        if constexpr (kPingPong) {
+            epilogue_staged(a, acc, sp, t, 0, m0, j, regs, to);
+            epilogue_staged(a, acc, sp, t, 1, m0, j, regs, to);
+        } else {
+            epilogue_staged(a, acc, sp, t, g, m0, j, regs, to);
+        }
     }
+    // channels 64j + 32h + [0, 32) of row t
     static __device__ void epilogue_staged(const Args& a, uint32_t acc, const float* sp, int t,
-                                           int g, int m0, int j, Regs& regs,
+                                           int h, int m0, int j, Regs& regs,
                                            const CUtensorMap* to) {
-        const int lane = t & 31, row0 = m0 + (t & ~31), c0 = 32 * g;
+        const int lane = t & 31, row0 = m0 + (t & ~31), c0 = 32 * h;
+        // this half's residual registers (ping-pong: the block's 64 channels, split mode: the
+        // worker half's 32)
+        const int rb = kPingPong ? 4 * h : 0;
         const float* bo = sp + 2 * CA + 2 * C + 64 * j + c0;
         const float* bg = bo + O;
         // rows past M would compute garbage that the store clips: a warp wholly past M skips
@@ -1044,7 +1123,7 @@ struct TrimulOp {
                               (__uint_as_float(ro[4 * q + 3]) + b0.w) *
                                   sigmoid_fast(__uint_as_float(rg[4 * q + 3]) + b1.w)};
                 if constexpr (ADD) {
-                    const uint4 qq = regs.res[2 * hh + (q >> 1)];
+                    const uint4 qq = regs.res[rb + 2 * hh + (q >> 1)];
                     const float2 f0 = E::unpack((q & 1) ? qq.z : qq.x);
                     const float2 f1 = E::unpack((q & 1) ? qq.w : qq.y);
                     v[0] += f0.x;

@@ -62,7 +62,9 @@ struct BwdParams {
     const uint8_t* kmask;
     const float* nlse;   // -lse, [N,H,Sq]
     const float* ndelta; // -delta
-    float* dq_acc;  // [N,H,Sq,D] fp32: stored by the first key tile, added to by the later ones
+    float* dq_acc;  // [N,H,Sq,D] fp32: with contig stored by the first key tile, added to by
+                    // the later ones; otherwise zeroed before the kernel, added to by all
+    int contig;     // CTAs own contiguous runs of (n, h) pairs (the schedule below)
     void* dk;
     void* dv;
     float* dbias;   // [H,Sq,Sk] fp32, zeroed
@@ -157,54 +159,67 @@ __device__ __forceinline__ void red_add_f32(float* p, float v) {
 }
 
 // Where global step gi of a CTA lies: its work item (key tile, head, sequence) and query step.
-// Items are numbered key tiles fastest, then heads, then sequences; CTA b owns the (n, h) pairs
-// [b P / G, (b + 1) P / G) of the P = N H pairs (G CTAs), i.e. a contiguous run of items whose
-// key tiles of one (n, h) follow one another, and runs every item's nqs query steps in turn.
-// nqs is nqt (the steps that hold queries) rounded up to a multiple of the step sets, so that
-// step i of every item falls to the same set (whose threads then handle the same dQ elements
-// at every key tile); a step past nqt has no queries (all its rows lie past Sq: zero tiles, no
-// outputs). The query steps of an item start at one that depends on its
+// Items are numbered key tiles fastest, then heads, then sequences. With p.contig, CTA b owns
+// the (n, h) pairs [b P / G, (b + 1) P / G) of the P = N H pairs (G CTAs), i.e. a contiguous run
+// of items whose key tiles of one (n, h) follow one another; otherwise (where whole pairs would
+// balance the CTAs badly, P / G small) it takes items b, b + G, b + 2G, ... It runs every item's
+// nqs query steps in turn. With p.contig nqs is nqt (the steps that hold queries) rounded up to
+// a multiple of the step sets, so that step i of every item falls to the same set (whose
+// threads then handle the same dQ elements at every key tile); a step past nqt has no queries
+// (all its rows lie past Sq: zero tiles, no outputs). The query steps of an item start at one that depends on its
 // sequence, so the CTAs of different sequences running at once reduce into different dBias
 // rows.
 struct StepPos {
     int k0, h, n, q0;
+    int rot;            // n mod (query steps holding queries): the item's first step
     long long rowbase;  // (n * H + h) * Sq
 };
 
-// The first item of this CTA and how many it owns
-__device__ __forceinline__ void cta_items(const BwdParams& p, int nkt, int& item0, int& count) {
-    const long long pairs = (long long)p.N * p.H;
+// The CTA's schedule: key tiles, query steps holding queries, steps per item, its first item
+// and the stride between its items
+struct Sched {
+    int nkt, nqt, nqs, item0, istride;
+};
+
+// The first item of this CTA, the stride to its next, and how many it owns
+__device__ __forceinline__ void cta_items(const BwdParams& p, int nkt, Sched& sc, int& count) {
     const long long b = blockIdx.x, g = gridDim.x;
-    const long long p0 = b * pairs / g, p1 = (b + 1) * pairs / g;
-    item0 = (int)(p0 * nkt);
-    count = (int)((p1 - p0) * nkt);
+    if (p.contig) {
+        const long long pairs = (long long)p.N * p.H;
+        const long long p0 = b * pairs / g, p1 = (b + 1) * pairs / g;
+        sc.item0 = (int)(p0 * nkt);
+        sc.istride = 1;
+        count = (int)((p1 - p0) * nkt);
+    } else {
+        const long long items = (long long)nkt * p.H * p.N;
+        sc.item0 = (int)b;
+        sc.istride = (int)g;
+        count = items > b ? (int)((items - 1 - b) / g + 1) : 0;
+    }
 }
 
 // The position of the CTA's item j (divisions: once per item)
-__device__ __forceinline__ StepPos item_pos(const BwdParams& p, int nkt, int item0, int j) {
-    const int u = item0 + j;
+__device__ __forceinline__ StepPos item_pos(const BwdParams& p, const Sched& sc, int j) {
+    const int nkt = sc.nkt;
+    const int u = sc.item0 + j * sc.istride;
     const int rest = u / nkt;
     StepPos s;
     s.k0 = (u - rest * nkt) * kBK;
     s.h = rest % p.H;
     s.n = rest / p.H;
     s.q0 = 0;
+    s.rot = s.n % ((p.Sq + kBQ - 1) / kBQ);
     s.rowbase = ((long long)s.n * p.H + s.h) * p.Sq;
     return s;
 }
 
-__device__ __forceinline__ int rotated_q0(int n, int nqt, int i) {
+__device__ __forceinline__ int rotated_q0(const StepPos& s, int nqt, int i) {
     if (i >= nqt) {
         return nqt * kBQ;  // a padding step: every row past Sq
     }
-    const int r = n % nqt;
+    const int r = s.rot;
     return (i + r < nqt ? i + r : i + r - nqt) * kBQ;
 }
-
-// The CTA's schedule: key tiles, query steps holding queries, steps per item, first item
-struct Sched {
-    int nkt, nqt, nqs, item0;
-};
 
 // A walk over global steps gi = j * nqs + i in strides of `by` (by <= nqs is not required)
 struct StepCursor {
@@ -214,8 +229,8 @@ struct StepCursor {
         gi = g;
         j = g / sc.nqs;
         i = g - j * sc.nqs;
-        pos = item_pos(p, sc.nkt, sc.item0, j);
-        pos.q0 = rotated_q0(pos.n, sc.nqt, i);
+        pos = item_pos(p, sc, j);
+        pos.q0 = rotated_q0(pos, sc.nqt, i);
     }
     __device__ __forceinline__ void advance(const BwdParams& p, const Sched& sc, int by) {
         gi += by;
@@ -224,9 +239,9 @@ struct StepCursor {
             const int dj = i / sc.nqs;
             j += dj;
             i -= dj * sc.nqs;
-            pos = item_pos(p, sc.nkt, sc.item0, j);
+            pos = item_pos(p, sc, j);
         }
-        pos.q0 = rotated_q0(pos.n, sc.nqt, i);
+        pos.q0 = rotated_q0(pos, sc.nqt, i);
     }
 };
 
@@ -253,11 +268,12 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
     const int DN = (D + 15) & ~15;
     const int nkt = (p.Sk + kBK - 1) / kBK;
     const int nqt = (p.Sq + kBQ - 1) / kBQ;
-    const int nqs = (nqt + NP - 1) / NP * NP;  // the host keeps items * nqs below 2^31
+    // the host keeps items * nqs below 2^31
+    const int nqs = p.contig ? (nqt + NP - 1) / NP * NP : nqt;
     Sched sc;
     int J;  // this CTA's items
-    cta_items(p, nkt, sc.item0, J);
     sc.nkt = nkt;
+    cta_items(p, nkt, sc, J);
     sc.nqt = nqt;
     sc.nqs = nqs;
     const int total = J * nqs;  // this CTA's query steps
@@ -299,7 +315,7 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
         // statistics and arrives on the stage's barrier (released with its own stores)
         {
             for (int j = 0; j < J; ++j) {
-                const StepPos it = item_pos(p, nkt, sc.item0, j);
+                const StepPos it = item_pos(p, sc, j);
                 const int kb = j % KVB;
                 if (lane == 0) {
                     if (j >= KVB) {
@@ -318,7 +334,7 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
                 for (int i = 0; i < nqs; ++i) {
                     const int gi = j * nqs + i;
                     StepPos sp = it;
-                    sp.q0 = rotated_q0(it.n, nqt, i);
+                    sp.q0 = rotated_q0(it, nqt, i);
                     const int s = gi % NS;
                     // the statistics load ahead of the wait for the stage
                     float sv[4];
@@ -479,7 +495,7 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
         // stores its tile, the later ones add to it (after that store: program order).
         const auto flush_dq = [&](const StepPos& sp) {
             const int q = sp.q0 + 16 * (warp & 3) + lane;
-            const bool first = sp.k0 == 0;
+            const bool first = p.contig && sp.k0 == 0;
             for (int c = 16 * hf; c < DN; c += 32) {
                 uint32_t r[16];
                 tmem_ld16(t_dq + lane_base + c, r);
@@ -510,7 +526,7 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
             const int db = e % NB;
             mbar_wait(&acc_full[db], (e / NB) & 1, &g_status, kStatusMmaWait, &abort_flag);
             tc_fence_after();
-            const StepPos it = item_pos(p, nkt, sc.item0, e);
+            const StepPos it = item_pos(p, sc, e);
             const int key = it.k0 + t;
             const long long krow = ((long long)it.n * p.H + it.h) * p.Sk + key;
             const int which = wg & 1;
@@ -872,6 +888,15 @@ __global__ void dq_convert_kernel(const float* __restrict__ acc, T* __restrict__
     }
 }
 
+// SMs of device dev (cached)
+int sm_count_of(int dev) {
+    static int sms[kMaxDevices] = {};
+    if (dev >= 0 && dev < kMaxDevices && sms[dev] == 0) {
+        cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    }
+    return dev >= 0 && dev < kMaxDevices && sms[dev] > 0 ? sms[dev] : 148;
+}
+
 size_t align256(size_t x) {
     return (x + 255) & ~size_t(255);
 }
@@ -929,15 +954,11 @@ cudaError_t launch_main(cudaStream_t stream, const CUtensorMap* maps, const BwdP
         }
         attr_done[dev] = true;
     }
-    // persistent: one CTA per SM, each looping over work items
-    static int sms[kMaxDevices] = {};
-    if (dev < kMaxDevices && sms[dev] == 0) {
-        cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
-    }
-    const int nsm = dev < kMaxDevices && sms[dev] > 0 ? sms[dev] : 148;
-    // every CTA owns at least one (n, h) pair and all of its key tiles
+    // persistent: one CTA per SM, each looping over work items (with p.contig every CTA owns at
+    // least one (n, h) pair and all of its key tiles)
     const long long pairs = (long long)p.N * p.H;
-    const dim3 grid((unsigned)std::min<long long>(pairs, nsm));
+    const long long units = p.contig ? pairs : pairs * ((p.Sk + kBK - 1) / kBK);
+    const dim3 grid((unsigned)std::min<long long>(units, sm_count_of(dev)));
     kern<<<grid, BGeom<DP>::THREADS, smem, stream>>>(maps[0], maps[1], maps[2], maps[3], maps[4],
                                                      maps[5], p);
     return cudaGetLastError();
@@ -968,6 +989,12 @@ cudaError_t run_backward(cudaStream_t stream, const CUtensorMap* maps, const Bwd
     cudaError_t e;
     if ((e = cudaMemsetAsync(p.dbias, 0, sizeof(float) * (size_t)p.H * p.Sq * p.Sk, stream)) !=
         cudaSuccess) {
+        return e;
+    }
+    // the strided schedule adds every key tile's dQ into the accumulator
+    if (!p.contig &&
+        (e = cudaMemsetAsync(p.dq_acc, 0, sizeof(float) * (size_t)rows * p.D, stream)) !=
+            cudaSuccess) {
         return e;
     }
     if (g == nullptr) {
@@ -1160,6 +1187,16 @@ int backward(void* stream_, int dtype, const void* q, const void* k, const void*
     p.nlse = nlse;
     p.ndelta = ndelta;
     p.dq_acc = dq_acc;
+    {
+        // contiguous (n, h) runs when whole pairs balance the CTAs about as well as single
+        // items do (the busiest CTA within 2% of the strided schedule's), else strided
+        int dev = 0;
+        cudaGetDevice(&dev);
+        const long long g = sm_count_of(dev), pairs = N * H, nkt = (Sk + kBK - 1) / kBK;
+        const long long most_contig = (pairs + g - 1) / g * nkt;
+        const long long most_strided = (pairs * nkt + g - 1) / g;
+        p.contig = 100 * most_contig <= 102 * most_strided ? 1 : 0;
+    }
     p.dk = dk;
     p.dv = dv;
     p.dbias = dbias;

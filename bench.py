@@ -597,7 +597,7 @@ def run_ours(args):
                 'frac': bwd_tf / peak, 'traffic': BWD_DRAM_BYTES_PER_SEQ * n_local,
                 'traffic_unit': 'bytes per launch',
                 'traffic_source': 'ncu dram__bytes_read.sum + dram__bytes_write.sum of '
-                                  'attn_bwd_kernel at N_seq=64 (144.6 MB), scaled by the '
+                                  'attn_bwd_kernel at N_seq=256 (526.2 MB), scaled by the '
                                   'sequences processed'},
             'gated_step': {'ms': gated_ms,
                            'TFLOP/s': attn_flops(n_local) / (gated_ms * 1e-3) / 1e12,
@@ -896,9 +896,10 @@ def bench_next_rows(torch, b200, dev, rank, world, steps, warmup, flush, pk, onl
 
 
 # DRAM bytes (read + written) of one attn_bwd_kernel launch per sequence of the headline shape,
-# from one ncu capture at N_seq=64 (144.56 MB / 64); the full-size launch is too large to capture
-# under the profiling size rule and its traffic grows with the sequences processed
-BWD_DRAM_BYTES_PER_SEQ = 144.56e6 / 64
+# from one ncu capture at N_seq=256 (526.20 MB / 256; the contiguous (n, h) schedule the full
+# size runs); the full-size launch is larger than the profiling size rule allows and its traffic
+# grows with the sequences processed
+BWD_DRAM_BYTES_PER_SEQ = 526.20e6 / 256
 
 BIG_RES, BIG_H = 2048, 4
 

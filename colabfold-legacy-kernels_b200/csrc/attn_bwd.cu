@@ -888,6 +888,49 @@ __global__ void dq_convert_kernel(const float* __restrict__ acc, T* __restrict__
     }
 }
 
+// The same transpose with 16-byte accesses (Sk % 8 == 0, a 16-byte-aligned bias): a block moves
+// a 64 x 64 tile, each thread two 8-key pieces of bias rows in and two 8-query pieces of bt rows
+// out, through a shared tile padded so that the column reads spread over the banks
+template <typename T>
+__global__ void __launch_bounds__(256) bias_transpose_vec_kernel(const T* __restrict__ bias,
+                                                                 T* __restrict__ bt, int Sq,
+                                                                 int Sk, int Sqp) {
+    __shared__ __align__(16) uint16_t tile[64][64 + 2];
+    const int h = blockIdx.z, q0 = blockIdx.x * 64, k0 = blockIdx.y * 64, tid = threadIdx.x;
+    const uint16_t* src = reinterpret_cast<const uint16_t*>(bias) + (long long)h * Sq * Sk;
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const int piece = tid + 256 * r, qr = piece >> 3, kc = (piece & 7) * 8;
+        const int q = q0 + qr, k = k0 + kc;
+        uint4 w = make_uint4(0, 0, 0, 0);
+        if (q < Sq && k < Sk) {  // Sk % 8 == 0: the piece is whole
+            w = *reinterpret_cast<const uint4*>(src + (long long)q * Sk + k);
+        }
+        // rows of 132 bytes: every pair of keys starts on a 4-byte boundary
+        uint32_t* row = reinterpret_cast<uint32_t*>(&tile[qr][kc]);
+        row[0] = w.x;
+        row[1] = w.y;
+        row[2] = w.z;
+        row[3] = w.w;
+    }
+    __syncthreads();
+    uint16_t* dst = reinterpret_cast<uint16_t*>(bt) + (long long)h * Sk * Sqp;
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const int piece = tid + 256 * r, kr = piece >> 3, qc = (piece & 7) * 8;
+        const int k = k0 + kr, q = q0 + qc;
+        if (k < Sk && q < Sqp) {  // Sqp % 8 == 0: the piece is whole (zeros past Sq)
+            uint32_t ww[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                ww[e] = (uint32_t)tile[qc + 2 * e][kr] | ((uint32_t)tile[qc + 2 * e + 1][kr] << 16);
+            }
+            *reinterpret_cast<uint4*>(dst + (long long)k * Sqp + q) =
+                make_uint4(ww[0], ww[1], ww[2], ww[3]);
+        }
+    }
+}
+
 // SMs of device dev (cached)
 int sm_count_of(int dev) {
     static int sms[kMaxDevices] = {};
@@ -1014,10 +1057,17 @@ cudaError_t run_backward(cudaStream_t stream, const CUtensorMap* maps, const Bwd
             static_cast<T*>(g->dog), static_cast<T*>(g->dgate), g->dgate_bias, ndelta, nlse, p.H,
             p.Sq, p.D);
     }
-    const dim3 tgrid((Sqp + 31) / 32, (p.Sk + 31) / 32, p.H);
-    bias_transpose_kernel<T><<<tgrid, dim3(32, 8), 0, stream>>>(static_cast<const T*>(bias),
-                                                                 static_cast<T*>(bt), p.Sq, p.Sk,
-                                                                 Sqp);
+    if (p.Sk % 8 == 0 && aligned16(bias)) {
+        const dim3 tgrid((Sqp + 63) / 64, (p.Sk + 63) / 64, p.H);
+        bias_transpose_vec_kernel<T><<<tgrid, 256, 0, stream>>>(static_cast<const T*>(bias),
+                                                                static_cast<T*>(bt), p.Sq, p.Sk,
+                                                                Sqp);
+    } else {
+        const dim3 tgrid((Sqp + 31) / 32, (p.Sk + 31) / 32, p.H);
+        bias_transpose_kernel<T><<<tgrid, dim3(32, 8), 0, stream>>>(static_cast<const T*>(bias),
+                                                                     static_cast<T*>(bt), p.Sq,
+                                                                     p.Sk, Sqp);
+    }
     if ((e = cudaGetLastError()) != cudaSuccess) {
         return e;
     }

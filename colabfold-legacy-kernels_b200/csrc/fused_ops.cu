@@ -712,7 +712,8 @@ struct ProjOp {
     static __device__ void prologue(const Args& a, uint8_t* stage, const float* sp, float* red,
                                     int t, int g, int m0, Regs&) {
         if constexpr (LN) {
-            ln_row_full<T, K>(stage, t, sp, sp + K, a.eps);
+            // the row held in registers (fits the 168 registers of two worker warpgroups)
+            ln_row_regs<T, K>(stage, t, sp, sp + K, a.eps);
         }
     }
     // the residual of row t's first 64 columns of block j, loaded ahead of the MMA wait

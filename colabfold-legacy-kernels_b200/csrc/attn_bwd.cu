@@ -748,15 +748,23 @@ __global__ void __launch_bounds__(BGeom<DP>::THREADS, 1)
 }
 
 // The backward's row statistics, negated: ndelta[row] = -sum_c out[row][c] * dout[row][c] and
-// nlse[row] = -lse[row]; one thread per row, 16-byte loads
+// nlse[row] = -lse[row]; one thread per row, 16-byte loads. With dq_zero the row of the float32
+// dQ accumulator is zeroed in the same pass.
 template <typename T>
 __global__ void row_delta_kernel(const T* __restrict__ out, const T* __restrict__ dout,
                                  const float* __restrict__ lse, float* __restrict__ ndelta,
-                                 float* __restrict__ nlse, long long rows, int D) {
+                                 float* __restrict__ nlse, float* __restrict__ dq_zero,
+                                 long long rows, int D) {
     using E = Elem<T>;
     const long long r = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (r >= rows) {
         return;
+    }
+    if (dq_zero != nullptr) {
+        float4* z = reinterpret_cast<float4*>(dq_zero + r * D);
+        for (int c = 0; c < D / 4; ++c) {
+            z[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
     }
     const uint4* o = reinterpret_cast<const uint4*>(out + r * D);
     const uint4* g = reinterpret_cast<const uint4*>(dout + r * D);
@@ -785,8 +793,8 @@ __global__ void gate_prologue_kernel(const T* __restrict__ y, const T* __restric
                                      const T* __restrict__ gate, const T* __restrict__ gate_bias,
                                      const float* __restrict__ lse, T* __restrict__ dog,
                                      T* __restrict__ dgate, float* __restrict__ dgate_bias,
-                                     float* __restrict__ ndelta, float* __restrict__ nlse, int H,
-                                     int Sq, int D) {
+                                     float* __restrict__ ndelta, float* __restrict__ nlse,
+                                     float* __restrict__ dq_zero, int H, int Sq, int D) {
     using E = Elem<T>;
     extern __shared__ float gsh[];  // [64][D] dgate (float32), then [64][D/8] partial deltas
     const int cpr = D >> 3;
@@ -819,6 +827,11 @@ __global__ void gate_prologue_kernel(const T* __restrict__ y, const T* __restric
         }
         *reinterpret_cast<uint4*>(dog + off) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
         *reinterpret_cast<uint4*>(dgate + off) = make_uint4(qw[0], qw[1], qw[2], qw[3]);
+        if (dq_zero != nullptr) {  // this thread's 8 columns of the float32 dQ accumulator
+            float4* z = reinterpret_cast<float4*>(dq_zero + off);
+            z[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+            z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -890,11 +903,13 @@ __global__ void dq_convert_kernel(const float* __restrict__ acc, T* __restrict__
 
 // The same transpose with 16-byte accesses (Sk % 8 == 0, a 16-byte-aligned bias): a block moves
 // a 64 x 64 tile, each thread two 8-key pieces of bias rows in and two 8-query pieces of bt rows
-// out, through a shared tile padded so that the column reads spread over the banks
+// out, through a shared tile padded so that the column reads spread over the banks. With
+// dbias_zero (16-byte aligned) the block also zeroes the same tile of dBias [H, Sq, Sk].
 template <typename T>
 __global__ void __launch_bounds__(256) bias_transpose_vec_kernel(const T* __restrict__ bias,
                                                                  T* __restrict__ bt, int Sq,
-                                                                 int Sk, int Sqp) {
+                                                                 int Sk, int Sqp,
+                                                                 float* __restrict__ dbias_zero) {
     __shared__ __align__(16) uint16_t tile[64][64 + 2];
     const int h = blockIdx.z, q0 = blockIdx.x * 64, k0 = blockIdx.y * 64, tid = threadIdx.x;
     const uint16_t* src = reinterpret_cast<const uint16_t*>(bias) + (long long)h * Sq * Sk;
@@ -912,6 +927,18 @@ __global__ void __launch_bounds__(256) bias_transpose_vec_kernel(const T* __rest
         row[1] = w.y;
         row[2] = w.z;
         row[3] = w.w;
+    }
+    if (dbias_zero != nullptr) {
+        float* zb = dbias_zero + (long long)h * Sq * Sk;
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const int piece = tid + 256 * r, qr = piece >> 4, kc = (piece & 15) * 4;
+            const int q = q0 + qr, k = k0 + kc;
+            if (q < Sq && k < Sk) {  // Sk % 8 == 0: the 4 floats are whole
+                *reinterpret_cast<float4*>(zb + (long long)q * Sk + k) =
+                    make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
     }
     __syncthreads();
     uint16_t* dst = reinterpret_cast<uint16_t*>(bt) + (long long)h * Sk * Sqp;
@@ -1030,19 +1057,21 @@ cudaError_t run_backward(cudaStream_t stream, const CUtensorMap* maps, const Bwd
                          const GateIO* g) {
     const long long rows = (long long)p.N * p.H * p.Sq;
     cudaError_t e;
-    if ((e = cudaMemsetAsync(p.dbias, 0, sizeof(float) * (size_t)p.H * p.Sq * p.Sk, stream)) !=
-        cudaSuccess) {
-        return e;
-    }
-    // the strided schedule adds every key tile's dQ into the accumulator
-    if (!p.contig &&
-        (e = cudaMemsetAsync(p.dq_acc, 0, sizeof(float) * (size_t)rows * p.D, stream)) !=
+    // dBias is zeroed by the vectorised transpose where it can (16-byte aligned), else here
+    const bool vec_transpose = p.Sk % 8 == 0 && aligned16(bias);
+    const bool zero_in_transpose = vec_transpose && aligned16(p.dbias);
+    if (!zero_in_transpose &&
+        (e = cudaMemsetAsync(p.dbias, 0, sizeof(float) * (size_t)p.H * p.Sq * p.Sk, stream)) !=
             cudaSuccess) {
         return e;
     }
+    // the strided schedule adds every key tile's dQ into the accumulator, which the row
+    // statistic's pass zeroes
+    float* dq_zero = p.contig ? nullptr : p.dq_acc;
     if (g == nullptr) {
         row_delta_kernel<T><<<(unsigned)((rows + 255) / 256), 256, 0, stream>>>(
-            static_cast<const T*>(out), static_cast<const T*>(dout), lse, ndelta, nlse, rows, p.D);
+            static_cast<const T*>(out), static_cast<const T*>(dout), lse, ndelta, nlse, dq_zero,
+            rows, p.D);
     } else {
         if ((e = cudaMemsetAsync(g->dgate_bias, 0, sizeof(float) * (size_t)p.H * p.D, stream)) !=
             cudaSuccess) {
@@ -1054,14 +1083,14 @@ cudaError_t run_backward(cudaStream_t stream, const CUtensorMap* maps, const Bwd
                                   stream>>>(
             static_cast<const T*>(out), static_cast<const T*>(dout),
             static_cast<const T*>(g->gate), static_cast<const T*>(g->gate_bias), lse,
-            static_cast<T*>(g->dog), static_cast<T*>(g->dgate), g->dgate_bias, ndelta, nlse, p.H,
-            p.Sq, p.D);
+            static_cast<T*>(g->dog), static_cast<T*>(g->dgate), g->dgate_bias, ndelta, nlse,
+            dq_zero, p.H, p.Sq, p.D);
     }
-    if (p.Sk % 8 == 0 && aligned16(bias)) {
+    if (vec_transpose) {
         const dim3 tgrid((Sqp + 63) / 64, (p.Sk + 63) / 64, p.H);
-        bias_transpose_vec_kernel<T><<<tgrid, 256, 0, stream>>>(static_cast<const T*>(bias),
-                                                                static_cast<T*>(bt), p.Sq, p.Sk,
-                                                                Sqp);
+        bias_transpose_vec_kernel<T><<<tgrid, 256, 0, stream>>>(
+            static_cast<const T*>(bias), static_cast<T*>(bt), p.Sq, p.Sk, Sqp,
+            zero_in_transpose ? p.dbias : nullptr);
     } else {
         const dim3 tgrid((Sqp + 31) / 32, (p.Sk + 31) / 32, p.H);
         bias_transpose_kernel<T><<<tgrid, dim3(32, 8), 0, stream>>>(static_cast<const T*>(bias),

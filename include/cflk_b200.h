@@ -101,8 +101,10 @@ CFLK_API int cflk_volta_mma_bwd(void* stream, int dtype, const void* q, const vo
  * (cflk_volta_mma_bwd_workspace_size) is rejected with CFLK_INVALID_ARGUMENT. The first call on
  * a device looks up the array's device address (cudaGetSymbolAddress) for the current device,
  * so make that first call before any stream capture. All calls on a device share the array:
- * calls whose kernels overlap on the GPU race on it; calls ordered on one stream do not. The
- * accumulator is zero-filled by every call. Nothing is allocated. */
+ * calls whose kernels overlap on the GPU race on it; calls ordered on one stream do not. Every
+ * call writes the part of the array it uses before reading it (the float32 dQ accumulator is
+ * stored by the first key tile or zeroed first), so nothing carries over from the previous call.
+ * Nothing is allocated. */
 CFLK_API size_t cflk_volta_mma_bwd_noalloc_max_scratch(void);
 CFLK_API int cflk_volta_mma_bwd_noalloc(void* stream, int dtype, const void* q, const void* k,
                                         const void* v, const void* bias, const uint8_t* kmask,
